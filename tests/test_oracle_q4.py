@@ -1,0 +1,143 @@
+"""The Q4_0 oracle against llama.cpp's own answers, and its linear against the
+exact value of the quantised operands.
+
+These pin the CPU restatement (oracle/tn_oracle.c) before any GPU result is
+compared with it:
+
+1. writer bytes and reader bits equal llama.cpp gguf-py's frozen answers in
+   tests/golden/q4_gguf_golden.json (the reference's
+   scripts/q4quality/golden_gguf_py.json), with no tolerance, as the
+   reference's tests/numerics/test_q4ref.py:104-141 requires of candle;
+2. the same codec equals the installed gguf-py on seeded inputs;
+3. the linear is within the reference's counted float32 bound of its exact
+   value (scripts/q4quality/q4_gguf_ref.py:398-465, 511; K = K_in/32 + 3),
+   and the bound refuses a linear that skipped activation quantisation
+   (test_q4ref.py:203-255);
+4. lossless integer operands give the exact integer matmul
+   (tests/numerics/test_qgemm.py:102-137 of the reference).
+"""
+
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from tests import q4_exact
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "q4_gguf_golden.json")
+
+
+def _golden():
+    with open(GOLDEN) as fh:
+        return json.load(fh)
+
+
+def _f32(hexstr):
+    raw = bytes.fromhex(hexstr)
+    return np.array(struct.unpack(f"<{len(raw) // 4}f", raw), dtype=np.float32)
+
+
+def test_golden_file_still_exercises_its_edges():
+    doc = _golden()
+    cases = {(c["format"], c["name"]): c for c in doc["cases"]}
+    assert len(doc["provenance"]["gguf_quants_sha256"]) == 64
+    d = lambda c: struct.unpack("<e", bytes.fromhex(c["blob"])[0:2])[0]  # noqa: E731
+    assert d(cases[("q4_0", "pos_extreme")]) < 0 and d(cases[("q4_0", "neg_extreme")]) > 0
+    zero = cases[("q4_0", "zero")]
+    assert d(zero) == 0.0 and set(bytes.fromhex(zero["blob"])[2:]) == {0x88}
+    raw = struct.unpack("<H", bytes.fromhex(cases[("q4_0", "subnormal_d")]["blob"])[0:2])[0]
+    assert raw & 0x7C00 == 0 and raw & 0x3FF != 0
+    ties = _f32(cases[("q8_0", "ties")]["input_f32"])
+    assert np.max(np.abs(ties)) == 127.0 and 2.5 in ties and -126.5 in ties
+    assert len(doc["cases"]) == 9
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_writer_bytes_equal_llama_cpp(fmt):
+    quant = {"q4_0": oracle.q4_0_quantize, "q8_0": oracle.q8_0_quantize}[fmt]
+    n = 0
+    for c in _golden()["cases"]:
+        if c["format"] != fmt or "input_f32" not in c:
+            continue
+        got = quant(_f32(c["input_f32"]))
+        assert got == bytes.fromhex(c["blob"]), (fmt, c["name"])
+        n += 1
+    assert n == {"q4_0": 7, "q8_0": 2}[fmt]
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_reader_bits_equal_llama_cpp(fmt):
+    deq = {"q4_0": oracle.q4_0_dequantize, "q8_0": oracle.q8_0_dequantize}[fmt]
+    for c in _golden()["cases"]:
+        if c["format"] != fmt:
+            continue
+        n = int(np.prod(c["shape"]))
+        got = deq(bytes.fromhex(c["blob"]), n)
+        assert got.tobytes() == bytes.fromhex(c["dequant_f32"]), (fmt, c["name"])
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_codec_equals_installed_gguf_py(seed):
+    gguf = pytest.importorskip("gguf")
+    from gguf import quants
+
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((8, 256)) * (0.01 + seed)).astype(np.float32)
+    x[0, :32] = 0.0
+    x[1, 5] = -np.abs(x[1]).max() * 1.5  # a negative signed maximum
+    for fmt, qt, mine in (("q4_0", gguf.GGMLQuantizationType.Q4_0, oracle.q4_0_quantize),
+                          ("q8_0", gguf.GGMLQuantizationType.Q8_0, oracle.q8_0_quantize)):
+        want = quants.quantize(x, qt).tobytes()
+        assert mine(x) == want, fmt
+        deq = {"q4_0": oracle.q4_0_dequantize, "q8_0": oracle.q8_0_dequantize}[fmt]
+        assert deq(want, x.size).tobytes() == quants.dequantize(np.frombuffer(want, np.uint8).reshape(8, -1),
+                                                                 qt).astype(np.float32).tobytes()
+
+
+@pytest.mark.parametrize("rows,out_f,in_f,seed", [(1, 8, 64, 11), (3, 12, 512, 12), (2, 5, 1024, 13),
+                                                  (4, 37, 4096, 14)])
+def test_linear_within_counted_bound_of_exact_value(rows, out_f, in_f, seed):
+    w = (np.random.default_rng(seed + 1).standard_normal((out_f, in_f)) * 0.05).astype(np.float32)
+    x = q4_exact.tie_free_gauss(rows, in_f, seed)
+    blob = oracle.q4_0_quantize(w)
+    got = oracle.q4_0_linear(x, blob, out_f, threads=3)
+    xq = oracle.q8_0_quantize(x)
+    exact, abs_sum, ref_err = q4_exact.exact_linear_q4_0(xq, blob, rows, out_f, in_f)
+    bound = q4_exact.linear_bound(in_f, abs_sum, ref_err)
+    assert float(np.max(np.abs(got - exact) / bound)) <= 1.0
+    # The bound must refuse the nearest wrong linear: no activation quantisation.
+    wdq = oracle.q4_0_dequantize(blob, out_f * in_f).astype(np.float64).reshape(out_f, in_f)
+    assert float(np.max(np.abs(x.astype(np.float64) @ wdq.T - exact) / bound)) > 1.0
+
+
+def test_linear_is_the_row_dot_and_bias_is_one_add():
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((3, 256)).astype(np.float32)
+    w = rng.standard_normal((9, 256)).astype(np.float32)
+    bias = rng.standard_normal(9).astype(np.float32)
+    blob = oracle.q4_0_quantize(w)
+    y = oracle.q4_0_linear(x, blob, 9, threads=4)
+    yb = oracle.q4_0_linear(x, blob, 9, bias=bias, threads=2)
+    assert (yb == (y + bias).astype(np.float32)).all()
+    xq = oracle.q8_0_quantize(x)
+    nb = 256 // 32
+    for r in range(3):
+        for c in range(9):
+            one = oracle.lib().tno_q4_0_q8_0_dot(np.frombuffer(blob, np.uint8)[c * nb * 18:].ctypes.data,
+                                                 np.frombuffer(xq, np.uint8)[r * nb * 34:].ctypes.data, nb)
+            assert np.float32(one) == y[r, c]
+
+
+def test_lossless_integer_operands_give_the_exact_integer_matmul():
+    # scale 1 (f16 1.0), codes in [-8, 7]; activations integers with block absmax 127
+    rng = np.random.default_rng(7)
+    M, N, K = 3, 10, 256
+    codes = rng.integers(-8, 8, size=(N, K))
+    blob = q4_exact.q4_0_blob_from_codes(codes, np.ones((N, K // 32), dtype=np.float16))
+    x = rng.integers(-127, 128, size=(M, K)).astype(np.float32)
+    x[:, ::32] = 127.0  # every block's absmax is 127 -> d = 1, codes = x
+    y = oracle.q4_0_linear(x, blob, N)
+    assert (y.astype(np.float64) == x.astype(np.float64) @ codes.T.astype(np.float64)).all()
