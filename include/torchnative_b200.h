@@ -1,0 +1,197 @@
+/*
+ * torchnative_b200.h -- C ABI of the B200 (sm_100a) backend for torchnative's
+ * two hot operators: the GGML Q4_0 weight-only linear and
+ * scaled_dot_product_attention (flash attention with GQA and a KV cache).
+ *
+ * Plain pointers and sizes only; every device pointer is CUDA global memory on
+ * the current device; `stream` is a cudaStream_t passed as void* (NULL = the
+ * legacy default stream). Every entry point returns a tn_status and never
+ * throws; on failure tn_last_error() holds a message naming the operator, in
+ * the reference's wording where the reference has one.
+ *
+ * Each declaration names the reference interface it replaces (paths relative
+ * to the torchnative project root). The Rust binding a maintainer adds to
+ * torchnative/rust/torch_c is shown in INTEGRATION.md.
+ */
+#ifndef TORCHNATIVE_B200_H
+#define TORCHNATIVE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TN_ABI_VERSION 1
+
+#if defined(TN_BUILD) && defined(__GNUC__)
+#define TN_API __attribute__((visibility("default")))
+#else
+#define TN_API
+#endif
+
+/* Status codes. The Rust side maps them the way torch_c/src/err.rs does:
+ * TN_ERR_NOT_IMPLEMENTED -> NotImplementedError (err.rs::not_implemented),
+ * everything else -> RuntimeError naming the op. */
+typedef enum {
+    TN_OK = 0,
+    TN_ERR_NOT_IMPLEMENTED = 1, /* unsupported dtype / format / shape family, refused by name */
+    TN_ERR_SHAPE = 2,           /* shapes that do not describe one operation */
+    TN_ERR_INVALID = 3,         /* null or misaligned pointer, bad stride */
+    TN_ERR_CUDA = 4,            /* a CUDA runtime call or launch failed */
+    TN_ERR_OOM = 5,             /* device allocation failed */
+    TN_ERR_TIMEOUT = 6          /* a bounded device-side wait gave up */
+} tn_status;
+
+/* Element types, in torch's naming. */
+typedef enum { TN_F32 = 0, TN_F16 = 1, TN_BF16 = 2, TN_F64 = 3 } tn_dtype;
+
+/* How the Q4_0 linear treats its activations.
+ * TN_ACT_Q8_0: the reference's arithmetic -- each activation row is quantised
+ *   to GGML Q8_0 (k_quants.rs:676-706), block dots are exact integers and the
+ *   per-block scales are applied in float32 (k_quants.rs:312-330).
+ * TN_ACT_FLOAT: no activation quantisation; weights are dequantised exactly
+ *   to float32 and multiplied with the float activations (fp32 accumulate). */
+typedef enum { TN_ACT_Q8_0 = 0, TN_ACT_FLOAT = 1 } tn_act_mode;
+
+/* ---------------------------------------------------------------- runtime -- */
+
+TN_API int tn_abi_version(void);
+/* Message of the last failed call on this host thread ("" if none). */
+TN_API const char *tn_last_error(void);
+TN_API const char *tn_status_name(int status);
+
+/* Device facts the kernels size themselves by. Replaces the device resolve /
+ * arch check in torch_c/src/device.rs:370-392 (cuda_device) and :1505
+ * (cuda_arch_mismatch): TN_ERR_NOT_IMPLEMENTED when the device is not sm_100. */
+TN_API int tn_device_info(int device, int *sm_count, int *cc_major, int *cc_minor, int64_t *l2_bytes,
+                   int64_t *smem_optin_per_block);
+
+/* Synchronises the current device and reads its device-side error word: every
+ * spin-wait in these kernels is bounded, and a wait that gives up records a
+ * code there and returns instead of hanging. TN_ERR_TIMEOUT if set (cleared
+ * when reset != 0). No reference counterpart (candle's kernels never wait). */
+TN_API int tn_device_status(int reset);
+
+/* Caching device allocator (replaces candle's per-tensor cudarc alloc,
+ * vendor/candle-core/src/cuda_backend/device.rs:78-90). Blocks are reused
+ * for requests of the same rounded size on the same stream; tn_empty_cache
+ * returns unused blocks to the driver. */
+TN_API int tn_alloc(void **ptr, size_t bytes, void *stream);
+TN_API int tn_free(void *ptr, void *stream);
+TN_API int tn_empty_cache(void);
+TN_API int tn_memory_stats(size_t *allocated_bytes, size_t *reserved_bytes);
+
+/* Per-process call counters, the evidence of which path ran (the reference's
+ * _cuda_counters, torch_c/src/device.rs:1671-1700). */
+typedef struct {
+    uint64_t q4_linear_calls;
+    uint64_t q4_gemv_launches;     /* decode GEMV (TMA-staged) launches */
+    uint64_t q4_gemv_generic;      /* decode GEMV launches on the unstaged path (K % 256 != 0) */
+    uint64_t q4_gemm_launches;     /* prefill launches */
+    uint64_t q8_quant_launches;
+    uint64_t q4_codec_launches;
+    uint64_t sdpa_calls;
+    uint64_t sdpa_decode_launches; /* split-KV decode kernels */
+    uint64_t sdpa_prefill_launches;
+    uint64_t bytes_allocated;
+    uint64_t reserved[6];
+} tn_counters;
+TN_API int tn_get_counters(tn_counters *out);
+TN_API int tn_reset_counters(void);
+
+/* ------------------------------------------------------- Q4_0 op family -- */
+
+/* Q4_0 writer on the device: rows x cols float32 -> rows * cols/32 blocks of
+ * 18 bytes. Byte-identical to BlockQ4_0::from_float
+ * (vendor/candle-core/src/quantized/k_quants.rs:241-277), which
+ * torch._C._quantize(t, "q4_0") runs (torch_c/src/quant.rs:124-172). */
+TN_API int tn_q4_0_quantize(const float *x, void *blob, int64_t rows, int64_t cols, void *stream);
+
+/* Q4_0 reader: blob -> float32 [rows, cols], bit-identical to
+ * BlockQ4_0::to_float (k_quants.rs:219-239); replaces candle's
+ * dequantize_block_q4_0_f32 (vendor/candle-core/src/quantized/cuda.rs:105-160)
+ * behind torch._C._dequantize (quant.rs:180-189). */
+TN_API int tn_q4_0_dequantize(const void *blob, float *out, int64_t rows, int64_t cols, void *stream);
+
+/* Q8_0 writer for activations: x [rows, cols] (row stride x_row_stride
+ * elements, dtype x_dtype in {F32, BF16, F16}; bf16/f16 widened exactly) ->
+ * GGML Q8_0 blocks of 34 bytes, byte-identical to BlockQ8_0::from_float
+ * (k_quants.rs:676-706). Replaces candle's quantize_q8_1
+ * (vendor/candle-core/src/quantized/cuda.rs:48). */
+TN_API int tn_q8_0_quantize(const void *x, int x_dtype, int64_t x_row_stride, void *blob, int64_t rows,
+                     int64_t cols, void *stream);
+
+/* torch._C._quantized_linear(input, weight, bias) (torch_c/src/quant.rs:286-369):
+ * y[M, N] = x[M, K] @ W[N, K]^T (+ bias[N]).
+ *   x: device [M, K], dtype x_dtype in {F32, BF16, F16}, row stride
+ *      x_row_stride elements (>= K), unit inner stride.
+ *   w_blob: device, the GGML Q4_0 blob of W exactly as _quantized_blob /
+ *      _quantized_to hold it: N rows of K/32 blocks of 18 bytes.
+ *   bias: device float32 [N] or NULL (added in float32 after the product,
+ *      quant.rs:350-365).
+ *   y: device [M, N] row-major, dtype y_dtype in {F32, BF16, F16}.
+ *   act_mode: tn_act_mode.
+ * Replaces QMatMul::forward's CUDA arm (vendor/candle-core/src/quantized/
+ * mod.rs:1007-1043 -> quantized/cuda.rs:846-877: fast_mmvq for M <= 8,
+ * fast_mmq above). K must be a multiple of 32 (a Q4_0 row is whole blocks);
+ * otherwise TN_ERR_SHAPE in upstream's wording. M == 0 or N == 0 is a no-op.
+ * May allocate a workspace through the caching allocator on first use of a
+ * size (activation blocks); stream-ordered. */
+TN_API int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob,
+                   const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
+                   int act_mode, void *stream);
+
+/* The same linear split in two, for callers that fuse the activation
+ * quantisation into the kernel that produces the activations (an RMSNorm or a
+ * SiLU*mul epilogue) -- the reference does the two steps back to back too
+ * (k_quants.rs:2479-2510 then 2512-2553).
+ *
+ * Planar Q8_0 layout of M activation rows of K elements:
+ *   codes   int8  [M][codes_row_stride]  the Q8_0 codes, 32 per block in order
+ *   scales  f32   [M][K/32]              f32 of the block's f16 scale d
+ *   offsets f32   [M][K/32]              12582912 + 8 * sum(codes of the block)
+ * (12582912 = 1.5 * 2^23 is the magic number of the kernels' exact int->float
+ * step; the 8 * sum term removes the Q4_0 "-8" offset.) The blocks are the
+ * GGML Q8_0 blocks of tn_q8_0_quantize, byte for byte, rearranged. */
+TN_API int tn_q8_0_quantize_planar(const void *x, int x_dtype, int64_t x_row_stride, int8_t *codes,
+                                   int64_t codes_row_stride, float *scales, float *offsets,
+                                   int64_t rows, int64_t cols, void *stream);
+TN_API int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, const float *scales,
+                             const float *offsets, const void *w_blob, const float *bias, void *y,
+                             int y_dtype, int64_t M, int64_t N, int64_t K, void *stream);
+
+/* ------------------------------------------------------------ SDPA family -- */
+
+/* aten._scaled_dot_product_flash_attention_for_cpu.default(query, key, value,
+ *     dropout_p=0.0, is_causal=False, *, attn_mask=None, scale=None)
+ *     -> (out, logsumexp)
+ * reached through _C._aten_dispatch (torch_c/src/aten.rs:1524 -> 2687 ->
+ * routed 2771 -> CUDA arm 2861-2865 -> 7057 -> sdpa_flash_cpu 10092-10460).
+ *   q [B, Hq, L, D], k/v [B, Hkv, S, D]: device, dtype in {F32, BF16, F16},
+ *     element strides q_strides[4] etc. in [b, h, t, d] order with unit d
+ *     stride -- a KV-cache view narrowed out of a [B, Hkv, cap, D] buffer
+ *     (kv_cache.py:92-114) is read in place.
+ *   Grouped-query attention: query head h reads kv head h / (Hq / Hkv)
+ *     (repeat_kv_heads, aten.rs:17106-17130); Hq % Hkv != 0 is refused.
+ *   is_causal: upper-left aligned (row i attends keys 0..i), aten.rs:10038.
+ *   attn_mask: NULL or an additive mask in mask_dtype (query dtype or F32),
+ *     broadcast to [B, Hq, L, S] through mask_strides[4] (0 = broadcast).
+ *   scale: <= 0 or NaN means the default 1/sqrt(D).
+ *   out: device row-major [B, Hq, L, D] in the input dtype (the CUDA result
+ *     stays row-major, aten.rs:10436). lse: device row-major [B, Hq, L]
+ *     float32, or NULL when the caller does not read it.
+ * Refusals (aten.rs:10113-10172): dropout is not an argument here (the
+ * Rust/Python side refuses dropout_p > 0 with upstream's text); D not in
+ * {64, 128} or another unsupported combination -> TN_ERR_NOT_IMPLEMENTED. */
+TN_API int tn_sdpa_flash_attention(const void *q, const void *k, const void *v, const void *attn_mask,
+                            int mask_dtype, const int64_t *mask_strides, void *out, float *lse,
+                            int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t L, int64_t S,
+                            int64_t D, const int64_t *q_strides, const int64_t *k_strides,
+                            const int64_t *v_strides, int is_causal, double scale, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TORCHNATIVE_B200_H */

@@ -1,0 +1,118 @@
+"""ctypes binding of libtorchnative_b200.so (the C ABI in include/torchnative_b200.h).
+
+There is no fallback: if the library is missing or does not load, every
+operator raises. Build it with ``python -m torchnative_b200.build``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libtorchnative_b200.so")
+
+TN_OK = 0
+TN_ERR_NOT_IMPLEMENTED = 1
+TN_ERR_SHAPE = 2
+TN_ERR_INVALID = 3
+TN_ERR_CUDA = 4
+TN_ERR_OOM = 5
+TN_ERR_TIMEOUT = 6
+
+TN_F32, TN_F16, TN_BF16, TN_F64 = 0, 1, 2, 3
+TN_ACT_Q8_0, TN_ACT_FLOAT = 0, 1
+
+# Every entry point declared in include/torchnative_b200.h, with its ctypes signature.
+_P, _I, _I64, _SZ, _D = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_double
+_PI64 = ctypes.POINTER(ctypes.c_int64)
+
+
+class Counters(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in (
+        "q4_linear_calls", "q4_gemv_launches", "q4_gemv_generic", "q4_gemm_launches", "q8_quant_launches",
+        "q4_codec_launches", "sdpa_calls", "sdpa_decode_launches", "sdpa_prefill_launches", "bytes_allocated")] + [
+        ("reserved", ctypes.c_uint64 * 6)]
+
+
+SIGNATURES = {
+    "tn_abi_version": (_I, []),
+    "tn_last_error": (ctypes.c_char_p, []),
+    "tn_status_name": (ctypes.c_char_p, [_I]),
+    "tn_device_info": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), _PI64, _PI64]),
+    "tn_device_status": (_I, [_I]),
+    "tn_alloc": (_I, [ctypes.POINTER(_P), _SZ, _P]),
+    "tn_free": (_I, [_P, _P]),
+    "tn_empty_cache": (_I, []),
+    "tn_memory_stats": (_I, [ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
+    "tn_get_counters": (_I, [ctypes.POINTER(Counters)]),
+    "tn_reset_counters": (_I, []),
+    "tn_q4_0_quantize": (_I, [_P, _P, _I64, _I64, _P]),
+    "tn_q4_0_dequantize": (_I, [_P, _P, _I64, _I64, _P]),
+    "tn_q8_0_quantize": (_I, [_P, _I, _I64, _P, _I64, _I64, _P]),
+    "tn_q4_0_linear": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
+    "tn_q8_0_quantize_planar": (_I, [_P, _I, _I64, _P, _I64, _P, _P, _I64, _I64, _P]),
+    "tn_q4_0_linear_q8": (_I, [_P, _I64, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
+    "tn_sdpa_flash_attention": (_I, [_P, _P, _P, _P, _I, _PI64, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64,
+                                     _PI64, _PI64, _PI64, _I, _D, _P]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class NativeLibraryMissing(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it is not built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise NativeLibraryMissing(
+                        f"torchnative_b200: {LIB_PATH} is not built; run `python -m torchnative_b200.build`. "
+                        "There is no CPU fallback.")
+                L = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().tn_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int) -> None:
+    """Raise the exception the reference raises for this status
+    (torch_c/src/err.rs: not_implemented -> NotImplementedError, the rest
+    RuntimeError naming the op)."""
+    if status == TN_OK:
+        return
+    msg = last_error() or f"torchnative_b200 call failed with status {status}"
+    if status == TN_ERR_NOT_IMPLEMENTED:
+        raise NotImplementedError(msg)
+    if status == TN_ERR_TIMEOUT:
+        raise TimeoutError(msg)
+    raise RuntimeError(msg)
+
+
+def counters() -> dict:
+    c = Counters()
+    check(lib().tn_get_counters(ctypes.byref(c)))
+    return {n: int(getattr(c, n)) for n, _ in Counters._fields_ if n != "reserved"}
+
+
+def reset_counters() -> None:
+    check(lib().tn_reset_counters())
+
+
+def device_status(reset: bool = True) -> None:
+    check(lib().tn_device_status(1 if reset else 0))

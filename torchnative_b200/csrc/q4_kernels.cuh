@@ -1,0 +1,22 @@
+// q4_kernels.cuh -- internal launchers shared by the Q4_0 translation units.
+#pragma once
+
+#include "tn_common.cuh"
+
+namespace tn {
+
+// Planar Q8_0 activations (see q4_codec.cu): codes [rows][xq_row_stride] int8,
+// xd [rows][nb] f32 widened scale, xc [rows][nb] f32 = 12582912 + 8 * sum(codes).
+int launch_q8_planar(const void *x, int x_dtype, int64_t row_stride, int8_t *xq, float *xd, float *xc, int64_t rows,
+                     int64_t nb, int64_t xq_row_stride, cudaStream_t stream);
+
+// Largest activation-row count (<= 16) one GEMV launch holds in shared memory
+// for this K; 0 if even one row does not fit.
+int q4_gemv_max_rows(int64_t K);
+
+// Decode GEMV over planar Q8_0 activations: y[m, n] for m < M (M <= 16).
+int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
+                      const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
+                      cudaStream_t stream);
+
+}  // namespace tn

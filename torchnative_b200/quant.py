@@ -1,0 +1,248 @@
+"""The Q4_0 operator family on a B200, mirroring torchnative's `torch._C`
+quant entry points (torchnative/rust/torch_c/src/quant.rs) and its
+`QuantizedLinear` module (torchnative/python/torchnative/quant/__init__.py).
+
+Same names, argument meaning and errors as the reference; the compute goes
+through the C ABI of libtorchnative_b200.so. There is no CPU path here: a CPU
+tensor is refused by name (torchnative's own CPU kernels serve those).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as N
+
+Q4_0_BLOCK_ELEMS = 32
+Q4_0_BLOCK_BYTES = 18
+_FORMATS = {"q4_0": (Q4_0_BLOCK_ELEMS, Q4_0_BLOCK_BYTES)}
+
+_DTYPE_CODE = {torch.float32: N.TN_F32, torch.bfloat16: N.TN_BF16, torch.float16: N.TN_F16,
+               torch.float64: N.TN_F64}
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p | None:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+class QTensor:
+    """A block-quantised weight: the GGML blob plus its logical shape.
+
+    The reference keeps this as `Repr::Quantized(Arc<QTensor>)` inside a
+    TensorBase (torch_c/src/tensor.rs:110, 970, 1297). Here the blob is a uint8
+    torch tensor on the device, byte-identical to `_quantized_blob`.
+    """
+
+    __slots__ = ("blob", "shape", "format")
+
+    def __init__(self, blob: torch.Tensor, shape, fmt: str = "q4_0"):
+        if fmt not in _FORMATS:
+            raise NotImplementedError(f"torch._C._quantize: format {fmt!r} is not implemented on this backend "
+                                      f"(implemented: {sorted(_FORMATS)})")
+        if blob.dtype != torch.uint8 or blob.dim() != 1:
+            raise ValueError("QTensor blob must be a flat uint8 tensor")
+        self.blob = blob
+        self.shape = tuple(int(s) for s in shape)
+        self.format = fmt
+
+    @property
+    def device(self) -> torch.device:
+        return self.blob.device
+
+    def nbytes(self) -> int:
+        return self.blob.numel()
+
+    def __repr__(self):
+        return f"QTensor(shape={self.shape}, format={self.format}, device={self.device})"
+
+
+def _expect_blob_size(op: str, shape, fmt: str, nbytes: int) -> None:
+    elems, tbytes = _FORMATS[fmt]
+    count = 1
+    for s in shape:
+        count *= int(s)
+    want = count // elems * tbytes
+    if count % elems != 0 or nbytes != want:
+        raise ValueError(f"{op}: {fmt} stores {elems} elements in {tbytes} bytes, so a {list(shape)} tensor needs "
+                         f"{want} bytes; got {nbytes}")
+
+
+def _require_cuda(op: str, t: torch.Tensor) -> None:
+    if t.device.type != "cuda":
+        raise NotImplementedError(f"{op}: this is the CUDA arm (sm_100a); a {t.device.type} tensor belongs to "
+                                  "torchnative's CPU path")
+
+
+def _quantize(tensor: torch.Tensor, format: str = "q4_0") -> QTensor:
+    """torch._C._quantize (quant.rs:124-172) on the device."""
+    op = "torch._C._quantize"
+    if format not in _FORMATS:
+        raise NotImplementedError(f"{op}: format {format!r} is not implemented on this backend")
+    _require_cuda(op, tensor)
+    if tensor.dim() == 0:
+        raise NotImplementedError(f"{op}: a 0-d tensor cannot be quantised")
+    block = _FORMATS[format][0]
+    last = tensor.shape[-1]
+    if last % block != 0:
+        raise NotImplementedError(f"{op}: {format} stores {block} elements per block, so it must have their last dim "
+                                  f"divisible by block size -- got {last}, which is not a multiple of {block} "
+                                  f"(shape {list(tensor.shape)})")
+    src = tensor.detach().to(torch.float32).contiguous()
+    cols = last
+    rows = src.numel() // cols if cols else 0
+    blob = torch.empty(src.numel() // block * _FORMATS[format][1], dtype=torch.uint8, device=src.device)
+    N.check(N.lib().tn_q4_0_quantize(_ptr(src), _ptr(blob), rows, cols, _stream(src.device)))
+    return QTensor(blob, tuple(tensor.shape), format)
+
+
+def _dequantize(q: QTensor) -> torch.Tensor:
+    """torch._C._dequantize (quant.rs:180-189): back to dense float32, bit-exact."""
+    op = "torch._C._dequantize"
+    if not isinstance(q, QTensor):
+        raise TypeError(f"{op}: expected a quantised tensor")
+    _require_cuda(op, q.blob)
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    cols = q.shape[-1]
+    rows = out.numel() // cols if cols else 0
+    N.check(N.lib().tn_q4_0_dequantize(_ptr(q.blob), _ptr(out), rows, cols, _stream(q.device)))
+    return out
+
+
+def _quantized_format(q: QTensor) -> str:
+    return q.format
+
+
+def _quantized_nbytes(q: QTensor) -> int:
+    return q.nbytes()
+
+
+def _quantized_blob(q: QTensor) -> bytes:
+    """torch._C._quantized_blob (quant.rs:220-227): the raw GGML bytes."""
+    return q.blob.cpu().numpy().tobytes()
+
+
+def _quantized_from_blob(data: bytes, shape, format: str = "q4_0", device="cuda") -> QTensor:
+    """torch._C._quantized_from_blob (quant.rs:235-262), placed on `device`."""
+    op = "torch._C._quantized_from_blob"
+    if format not in _FORMATS:
+        raise NotImplementedError(f"{op}: format {format!r} is not implemented on this backend")
+    _expect_blob_size(op, shape, format, len(data))
+    host = torch.frombuffer(bytearray(data), dtype=torch.uint8)
+    return QTensor(host.to(device), shape, format)
+
+
+def _quantized_to(q: QTensor, device) -> QTensor:
+    """torch._C._quantized_to (quant.rs:384-405): the same blocks on another
+    device, byte for byte, never re-quantised; same device returns q itself."""
+    device = torch.device(device)
+    if q.device == device or (device.type == q.device.type and device.index is None):
+        return q
+    return QTensor(q.blob.to(device), q.shape, q.format)
+
+
+def _quantized_linear(input: torch.Tensor, weight: QTensor, bias: torch.Tensor | None = None,
+                      act_mode: int = N.TN_ACT_Q8_0) -> torch.Tensor:
+    """torch._C._quantized_linear(input, weight, bias) (quant.rs:286-369):
+    input @ dequant(weight).T + bias, with the reference's Q8_0 activation
+    quantisation (k_quants.rs:2479-2510) by default.
+
+    Accepts float32 activations as the reference does, and also bfloat16 and
+    float16 (widened exactly inside the kernel, so nothing is spent that the
+    caller cannot see); the result has the activation's dtype."""
+    op = "torch._C._quantized_linear"
+    if not isinstance(weight, QTensor):
+        raise NotImplementedError(f"{op}: the weight must be a quantised tensor (torch._C._quantize), got "
+                                  f"{type(weight).__name__}")
+    if input.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise NotImplementedError(f"{op}: the activation must be float32 (or bfloat16/float16 on CUDA), got {input.dtype}")
+    if input.device != weight.device:
+        raise RuntimeError(f"{op}: Expected all tensors to be on the same device, but found at least two devices, "
+                           f"{input.device} (the input) and {weight.device} (the quantised weight). Move the module "
+                           "with `.to(device)`; QuantizedLinear moves its blocks byte for byte (torch._C._quantized_to).")
+    _require_cuda(op, input)
+    if len(weight.shape) != 2:
+        raise RuntimeError(f"{op}: the quantised weight must be 2-D (out_features, in_features), got {weight.shape}")
+    out_features, in_features = weight.shape
+    if input.dim() == 0 or input.shape[-1] != in_features:
+        raise RuntimeError(f"{op}: mat1 and mat2 shapes cannot be multiplied ({list(input.shape)} and "
+                           f"{in_features}x{out_features})")
+    if bias is not None:
+        if bias.dtype != torch.float32:
+            raise NotImplementedError(f"{op}: the bias must be float32, got {bias.dtype}")
+        if tuple(bias.shape) != (out_features,):
+            raise RuntimeError(f"{op}: bias shape {list(bias.shape)} does not match out_features {out_features}")
+        if bias.device != input.device:
+            raise RuntimeError(f"{op}: Expected all tensors to be on the same device (bias on {bias.device})")
+        bias = bias.contiguous()
+    lead = input.shape[:-1]
+    x = input.reshape(-1, in_features)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    m = x.shape[0]
+    y = torch.empty((m, out_features), dtype=input.dtype, device=input.device)
+    if m and out_features:
+        code = _DTYPE_CODE[input.dtype]
+        N.check(N.lib().tn_q4_0_linear(_ptr(x), code, x.stride(0) if m > 1 else in_features, _ptr(weight.blob),
+                                       _ptr(bias), _ptr(y), code, m, out_features, in_features, int(act_mode),
+                                       _stream(input.device)))
+    return y.reshape(*lead, out_features)
+
+
+def _q8_0_quantize(x: torch.Tensor) -> torch.Tensor:
+    """The activation quantiser alone (BlockQ8_0::from_float, k_quants.rs:676-706):
+    rows of x -> GGML Q8_0 blocks, as a flat uint8 tensor."""
+    op = "torch._C._quantize"
+    _require_cuda(op, x)
+    if x.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise NotImplementedError(f"{op}: q8_0 activations must be float32, bfloat16 or float16, got {x.dtype}")
+    cols = x.shape[-1]
+    x2 = x.reshape(-1, cols)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    rows = x2.shape[0]
+    out = torch.empty(rows * (cols // 32) * 34, dtype=torch.uint8, device=x.device)
+    N.check(N.lib().tn_q8_0_quantize(_ptr(x2), _DTYPE_CODE[x.dtype], x2.stride(0) if rows > 1 else cols, _ptr(out),
+                                     rows, cols, _stream(x.device)))
+    return out
+
+
+class QuantizedLinear(torch.nn.Module):
+    """`nn.Linear` with a Q4_0 weight on the device (quant/__init__.py:100-252
+    of the reference): `qweight` is a plain attribute, not a Parameter; the bias
+    stays dense float32; `.to(device)` moves the blocks byte for byte."""
+
+    def __init__(self, in_features, out_features, qweight: QTensor | None, bias, fmt: str = "q4_0"):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.format = fmt
+        self.qweight = qweight
+        self.bias = bias
+
+    @classmethod
+    def from_linear(cls, mod: torch.nn.Linear, fmt: str = "q4_0"):
+        out_features, in_features = mod.weight.shape
+        return cls(in_features, out_features, _quantize(mod.weight, fmt), mod.bias, fmt)
+
+    def _apply(self, fn, recurse=True):
+        result = super()._apply(fn, recurse)
+        if self.qweight is not None:
+            target = fn(torch.empty(0)).device
+            if self.qweight.device != target:
+                self.qweight = _quantized_to(self.qweight, target)
+        return result
+
+    def forward(self, x):
+        if self.qweight is None:
+            raise RuntimeError("QuantizedLinear was asked to run before its weight arrived.")
+        return _quantized_linear(x, self.qweight, self.bias)
+
+    def extra_repr(self):
+        return (f"in_features={self.in_features}, out_features={self.out_features}, "
+                f"bias={self.bias is not None}, format={self.format}")
