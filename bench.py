@@ -23,7 +23,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -51,6 +50,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default=None, choices=["gemv"],
+                    help="kernel-level case instead of the decode step: 'gemv' times the decode GEMV alone on the "
+                         "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
+    ap.add_argument("--rows", type=int, default=1, help="activation rows M for --case gemv")
     return ap.parse_args()
 
 
@@ -58,59 +61,54 @@ def parse():
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (every 200 ms)."""
+    """SM clock and throttle reasons sampled during the timed region: NVML
+    polled every 5 ms from a thread (nvidia-smi's own loop is too coarse for a
+    timed region of tens of milliseconds), nvidia-smi as a fallback."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((float(mhz), int(rs)))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.005)
+
+            self._t = threading.Thread(target=poll, daemon=True)
             self._t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        except Exception:
+            self._t = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self._t is not None:
             self._t.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
 
 
 # --------------------------------------------------------------------------- workload
@@ -168,7 +166,7 @@ class Q4DecodeStack:
                                                stream))
         self.N.check(L.tn_q4_0_linear_q8(P(self.codes.data_ptr()), k, P(self.scales.data_ptr()),
                                          P(self.offsets.data_ptr()), P(w.data_ptr()), None, P(y.data_ptr()),
-                                         self.N.TN_BF16, self.M, n, k, stream))
+                                         self.N.TN_BF16, self.M, n, k, self.N.TN_WEIGHTS_STATIC, stream))
 
     def step(self, stream):
         """One decode token's Q4_0 work: 4 linears x 32 layers + lm_head."""
@@ -190,7 +188,7 @@ class Q4DecodeStack:
         self.N.check(L.tn_q4_0_linear_q8(P(self.codes.data_ptr()), HIDDEN, P(self.scales.data_ptr()),
                                          P(self.offsets.data_ptr()), P(self.layers[layer]["gate_up"].data_ptr()),
                                          None, P(self.gu.data_ptr()), self.N.TN_BF16, self.M, 2 * INTER, HIDDEN,
-                                         stream))
+                                         self.N.TN_WEIGHTS_STATIC, stream))
 
     def dominant_algorithmic_bytes(self):
         n, k = 2 * INTER, HIDDEN
@@ -454,6 +452,9 @@ def run_reference(args, rank, world):
 
 def main():
     args = parse()
+    if args.case == "gemv":
+        run_case_gemv(args)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -469,6 +470,69 @@ def main():
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+
+def run_case_gemv(args):
+    """Kernel-level timing of the decode GEMV (planar Q8_0 activations already
+    on the device) on BASELINE's (N, K) shapes, rotating over enough weight
+    copies that the weights never sit in L2. Prints one JSON line per shape."""
+    import ctypes
+
+    import torch
+
+    from torchnative_b200 import _native as N, build
+
+    build.build()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    M = args.rows
+    peak, peak_kind = measured_peaks()
+    P = ctypes.c_void_p
+    L = N.lib()
+    for n, k in ((14336, 4096), (4096, 14336), (6144, 4096), (28672, 4096)):
+        wbytes = q4_bytes(n, k)
+        copies = max(2, -(-300_000_000 // wbytes))
+        ws = [random_q4_blob(n, k, gen, dev) for _ in range(copies)]
+        x = torch.randn((M, k), device=dev, generator=gen).to(torch.bfloat16)
+        codes = torch.empty((M, k), device=dev, dtype=torch.int8)
+        scales = torch.empty((M, k // 32), device=dev)
+        offs = torch.empty((M, k // 32), device=dev)
+        y = torch.empty((M, n), device=dev, dtype=torch.bfloat16)
+        s = lambda: P(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+        N.check(L.tn_q8_0_quantize_planar(P(x.data_ptr()), N.TN_BF16, k, P(codes.data_ptr()), k,
+                                          P(scales.data_ptr()), P(offs.data_ptr()), M, k, s()))
+
+        def launch(w):
+            N.check(L.tn_q4_0_linear_q8(P(codes.data_ptr()), k, P(scales.data_ptr()), P(offs.data_ptr()),
+                                        P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, M, n, k,
+                                        N.TN_WEIGHTS_STATIC, s()))
+
+        launch(ws[0])
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for w in ws:
+                launch(w)
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (args.steps * copies)
+        algo = wbytes + M * (k + k // 32 * 8) + M * n * 2
+        print(json.dumps({"case": "gemv", "M": M, "N": n, "K": k, "us_per_launch": us,
+                          "GBps": algo / us / 1e3, "frac": algo / us / 1e3 / peak, "peak": peak,
+                          "peak_kind": peak_kind, "copies": copies}), flush=True)
+        del ws
+        torch.cuda.empty_cache()
+    N.device_status(reset=True)
 
 
 if __name__ == "__main__":

@@ -158,9 +158,14 @@ TN_API int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, cons
 TN_API int tn_q8_0_quantize_planar(const void *x, int x_dtype, int64_t x_row_stride, int8_t *codes,
                                    int64_t codes_row_stride, float *scales, float *offsets,
                                    int64_t rows, int64_t cols, void *stream);
+/* flags: TN_WEIGHTS_STATIC -- the caller vouches that no work queued before
+ * this call on the stream writes w_blob (true of a model's weights), so the
+ * kernel may start streaming the weights before the previous kernel in the
+ * stream has finished (programmatic dependent launch). 0 = always wait. */
+#define TN_WEIGHTS_STATIC 1
 TN_API int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, const float *scales,
                              const float *offsets, const void *w_blob, const float *bias, void *y,
-                             int y_dtype, int64_t M, int64_t N, int64_t K, void *stream);
+                             int y_dtype, int64_t M, int64_t N, int64_t K, int flags, void *stream);
 
 /* ------------------------------------------------------------ SDPA family -- */
 

@@ -23,6 +23,7 @@ TN_ERR_TIMEOUT = 6
 
 TN_F32, TN_F16, TN_BF16, TN_F64 = 0, 1, 2, 3
 TN_ACT_Q8_0, TN_ACT_FLOAT = 0, 1
+TN_WEIGHTS_STATIC = 1
 
 # Every entry point declared in include/torchnative_b200.h, with its ctypes signature.
 _P, _I, _I64, _SZ, _D = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_double
@@ -53,7 +54,7 @@ SIGNATURES = {
     "tn_q8_0_quantize": (_I, [_P, _I, _I64, _P, _I64, _I64, _P]),
     "tn_q4_0_linear": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
     "tn_q8_0_quantize_planar": (_I, [_P, _I, _I64, _P, _I64, _P, _P, _I64, _I64, _P]),
-    "tn_q4_0_linear_q8": (_I, [_P, _I64, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
+    "tn_q4_0_linear_q8": (_I, [_P, _I64, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
     "tn_sdpa_flash_attention": (_I, [_P, _P, _P, _P, _I, _PI64, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64,
                                      _PI64, _PI64, _PI64, _I, _D, _P]),
 }

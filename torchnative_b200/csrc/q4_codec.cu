@@ -50,17 +50,21 @@ __global__ void q4_0_quantize_kernel(const float *__restrict__ x, uint8_t *__res
     }
     float d = __fdiv_rn(mx, -8.0f);
     float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
-    uint8_t *out = blob + i * 18;
-    unsigned short db = __half_as_ushort(__float2half_rn(d));
-    out[0] = static_cast<uint8_t>(db & 0xff);
-    out[1] = static_cast<uint8_t>(db >> 8);
+    // Stored as nine little-endian 16-bit halves: blocks are 18 bytes, so
+    // every block starts on a 2-byte boundary.
+    unsigned short *out = reinterpret_cast<unsigned short *>(blob + i * 18);
+    out[0] = __half_as_ushort(__float2half_rn(d));
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        uint32_t q0 = sat_u8_trunc(__fadd_rn(__fmul_rn(v[j], id), 8.5f));
-        uint32_t q1 = sat_u8_trunc(__fadd_rn(__fmul_rn(v[16 + j], id), 8.5f));
-        q0 = q0 < 15u ? q0 : 15u;
-        q1 = q1 < 15u ? q1 : 15u;
-        out[2 + j] = static_cast<uint8_t>(q0 | (q1 << 4));
+    for (int j = 0; j < 16; j += 2) {
+        uint32_t a0 = sat_u8_trunc(__fadd_rn(__fmul_rn(v[j], id), 8.5f));
+        uint32_t a1 = sat_u8_trunc(__fadd_rn(__fmul_rn(v[16 + j], id), 8.5f));
+        uint32_t b0 = sat_u8_trunc(__fadd_rn(__fmul_rn(v[j + 1], id), 8.5f));
+        uint32_t b1 = sat_u8_trunc(__fadd_rn(__fmul_rn(v[16 + j + 1], id), 8.5f));
+        a0 = a0 < 15u ? a0 : 15u;
+        a1 = a1 < 15u ? a1 : 15u;
+        b0 = b0 < 15u ? b0 : 15u;
+        b1 = b1 < 15u ? b1 : 15u;
+        out[1 + j / 2] = static_cast<unsigned short>((a0 | (a1 << 4)) | ((b0 | (b1 << 4)) << 8));
     }
 }
 
@@ -111,11 +115,13 @@ __global__ void q8_0_quantize_blob_kernel(const void *__restrict__ x, int64_t ro
     int8_t codes[32];
     int sum;
     uint32_t db = q8_0_block<T>(x, r * row_stride + b * 32, codes, &sum);
-    uint8_t *out = blob + i * 34;
-    out[0] = static_cast<uint8_t>(db & 0xff);
-    out[1] = static_cast<uint8_t>(db >> 8);
+    // Seventeen little-endian 16-bit halves (34-byte blocks start on 2-byte boundaries).
+    unsigned short *out = reinterpret_cast<unsigned short *>(blob + i * 34);
+    out[0] = static_cast<unsigned short>(db);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) out[2 + j] = static_cast<uint8_t>(codes[j]);
+    for (int j = 0; j < 32; j += 2)
+        out[1 + j / 2] = static_cast<unsigned short>((uint32_t)(uint8_t)codes[j] |
+                                                     ((uint32_t)(uint8_t)codes[j + 1] << 8));
 }
 
 // Planar Q8_0: the same blocks, split into codes [rows][K] int8, the widened
@@ -125,6 +131,10 @@ template <typename T>
 __global__ void q8_0_quantize_planar_kernel(const void *__restrict__ x, int64_t row_stride, int8_t *__restrict__ xq,
                                             float *__restrict__ xd, float *__restrict__ xc, int64_t rows, int64_t nb,
                                             int64_t xq_row_stride) {
+    // Launched as a programmatic dependent: let the consumer GEMV start its
+    // weight prefetch now, and wait for whatever produced x.
+    pdl_launch_dependents();
+    pdl_wait();
     int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= rows * nb) return;
     int64_t r = i / nb, b = i % nb;
@@ -152,21 +162,32 @@ int launch_q8_planar(const void *x, int x_dtype, int64_t row_stride, int8_t *xq,
     int64_t n = rows * nb;
     if (n == 0) return TN_OK;
     int threads = 128;
-    unsigned grid = (unsigned)((n + threads - 1) / threads);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((n + threads - 1) / threads));
+    cfg.blockDim = dim3(threads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
     switch (x_dtype) {
     case TN_F32:
-        q8_0_quantize_planar_kernel<float><<<grid, threads, 0, stream>>>(x, row_stride, xq, xd, xc, rows, nb,
-                                                                          xq_row_stride);
+        e = cudaLaunchKernelEx(&cfg, q8_0_quantize_planar_kernel<float>, x, row_stride, xq, xd, xc, rows, nb,
+                               xq_row_stride);
         break;
     case TN_BF16:
-        q8_0_quantize_planar_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(x, row_stride, xq, xd, xc, rows, nb,
-                                                                                  xq_row_stride);
+        e = cudaLaunchKernelEx(&cfg, q8_0_quantize_planar_kernel<__nv_bfloat16>, x, row_stride, xq, xd, xc, rows, nb,
+                               xq_row_stride);
         break;
     default:
-        q8_0_quantize_planar_kernel<__half><<<grid, threads, 0, stream>>>(x, row_stride, xq, xd, xc, rows, nb,
-                                                                           xq_row_stride);
+        e = cudaLaunchKernelEx(&cfg, q8_0_quantize_planar_kernel<__half>, x, row_stride, xq, xd, xc, rows, nb,
+                               xq_row_stride);
         break;
     }
+    int st = check_cuda(e, "torch._C._quantized_linear (activation Q8_0)", "cudaLaunchKernelEx");
+    if (st) return st;
     __atomic_fetch_add(&counters().q8_quant_launches, 1ull, __ATOMIC_RELAXED);
     return check_launch("torch._C._quantized_linear (activation Q8_0)");
 }

@@ -2,14 +2,16 @@
 // Q8_0-activation arithmetic, streamed from HBM with bulk-async (TMA) copies.
 //
 // Work split. CTA c of G owns output columns (weight rows) [c*N/G, (c+1)*N/G).
-// One producer warp streams those weight rows -- each row is K/32 GGML blocks of
-// 18 bytes, i.e. rowbytes = 18*K/32 contiguous bytes -- into a ring of shared
+// One producer lane streams those weight rows -- each row is K/32 GGML blocks
+// of 18 bytes, rowbytes = 18*K/32 contiguous bytes -- into a ring of shared
 // memory slots with cp.async.bulk (one copy per row, completion counted on the
-// slot's mbarrier). Eight consumer warps take rows round-robin; a warp splits
-// its row's blocks across its 32 lanes in pairs (36 bytes = 9 words; 9 is odd,
-// so the 32 lanes of a warp hit 32 different banks), takes exact integer block
-// dots with dp4a against the Q8_0 activation codes held in shared memory, and
-// applies the per-block scales in float32. A warp-shuffle tree sums the lanes.
+// slot's mbarrier). Eight consumer warps take rows two at a time (rows 2q and
+// 2q+1 for q = warp, warp+8, ...): two independent accumulation chains per
+// lane, and every activation load serves both rows. A warp splits a row's
+// blocks across its 32 lanes in pairs (36 bytes = 9 words; 9 is odd, so the 32
+// lanes hit 32 different banks), takes exact integer block dots with dp4a
+// against the Q8_0 activation codes held in shared memory, and applies the
+// per-block scales in float32. A reduce-scatter shuffle butterfly sums lanes.
 //
 // Arithmetic (reference: k_quants.rs:312-330 vec_dot_unopt). Per block b:
 //   I_b = sum_j (q4_j - 8) * q8_j                 exact int32
@@ -18,8 +20,8 @@
 // (bits 0x4B400000 + I read as float = 12582912 + I, exact for |I| < 2^22), and
 // the "-8" offset is folded into the subtracted constant xc = 12582912 + 8*sum(q8).
 // Each lane accumulates its blocks with fmaf (one rounding per block), then a
-// 5-level shuffle tree: depth ceil(nb/32) + 5 <= nb + 3, the depth the
-// reference's own bound counts (scripts/q4quality/q4_gguf_ref.py:370-405).
+// 5-level shuffle tree: depth ceil(nb/64)*2 + 5 <= nb + 3 for nb >= 2, the
+// depth the reference's own bound counts (scripts/q4quality/q4_gguf_ref.py:370-405).
 #include "q4_kernels.cuh"
 
 namespace tn {
@@ -28,7 +30,10 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxSlots = 32;
-constexpr uint32_t kMagic = 0x4B400000u;  // 12582912.0f
+constexpr uint32_t kMagic = 0x4B400000u;           // 12582912.0f
+// Shared memory per CTA when two CTAs share an SM (228 KB per SM, 1 KB of it
+// reserved per CTA).
+constexpr size_t kTwoCtaBudget = 112 * 1024;
 
 struct GemvParams {
     const uint8_t *w;
@@ -45,37 +50,67 @@ struct GemvParams {
     int nb;       // blocks per weight row
     int nbp;      // nb rounded up to even (x staging granularity)
     int rowbytes; // 18 * nb
+    int wpc;      // consumer warps per chunk (a chunk is 2 * wpc rows)
+    int slot_bytes;
     int nslots;
+    int flags;
     int *err;
 };
 
-// Shared-memory layout (dynamic):
-//   [0, 16*kMaxSlots)                   full[kMaxSlots], empty[kMaxSlots] mbarriers
-//   xs   M * nbp * 32 bytes             activation codes, pair-swizzled (see stage_x)
-//   xds  M * nbp floats                 widened activation scales
-//   xcs  M * nbp floats                 offset constants
-//   slots nslots * rowbytes             weight rows (16-byte aligned)
+// Shared-memory layout (dynamic), as 32-bit shared-window addresses:
+//   bars  full[kMaxSlots], empty[kMaxSlots] mbarriers
+//   xs    M * nbp * 32 bytes      activation codes, pair-swizzled (xchunk)
+//   xds   M * nbp floats          widened activation scales
+//   xcs   M * nbp floats          offset constants
+//   slots nslots * slot_bytes     chunks of 2*wpc weight rows (16-byte aligned)
 struct Smem {
     uint64_t *full, *empty;
-    uint8_t *xs;
-    float *xds, *xcs;
-    uint8_t *slots;
+    uint32_t xs, xds, xcs, slots;
 };
 
 __device__ __forceinline__ Smem carve(uint8_t *base, const GemvParams &p) {
     Smem s;
     s.full = reinterpret_cast<uint64_t *>(base);
     s.empty = s.full + kMaxSlots;
-    size_t off = 16 * kMaxSlots;
-    s.xs = base + off;
-    off += (size_t)p.M * p.nbp * 32;
-    s.xds = reinterpret_cast<float *>(base + off);
-    off += (size_t)p.M * p.nbp * 4;
-    s.xcs = reinterpret_cast<float *>(base + off);
-    off += (size_t)p.M * p.nbp * 4;
-    off = (off + 127) & ~size_t(127);
-    s.slots = base + off;
+    const uint32_t b = smem_u32(base);
+    uint32_t off = 16 * kMaxSlots;
+    s.xs = b + off;
+    off += (uint32_t)p.M * p.nbp * 32;
+    s.xds = b + off;
+    off += (uint32_t)p.M * p.nbp * 4;
+    s.xcs = b + off;
+    off += (uint32_t)p.M * p.nbp * 4;
+    off = (off + 127) & ~127u;
+    s.slots = b + off;
     return s;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ int4 lds128(uint32_t a) {
+    int4 v;
+    asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float2 lds64f(uint32_t a) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, int4 v) {
+    asm volatile("st.shared.v4.s32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void stsf(uint32_t a, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
 
 // Byte offset of 16-byte chunk c (0..3) of block pair `pair` inside one
@@ -83,35 +118,83 @@ __device__ __forceinline__ Smem carve(uint8_t *base, const GemvParams &p) {
 // block 2*pair, chunks 2/3 those of block 2*pair+1. The XOR spreads the eight
 // lanes of a quarter-warp (which read pairs l..l+7) over all eight 16-byte bank
 // groups, so every 128-bit load below is conflict-free.
-__device__ __forceinline__ int xchunk(int pair, int c) { return pair * 64 + 16 * (c ^ ((pair >> 1) & 3)); }
+__device__ __forceinline__ uint32_t xchunk(int pair, int c) {
+    return (uint32_t)(pair * 64 + 16 * (c ^ ((pair >> 1) & 3)));
+}
 
-template <int MT>
-__device__ __forceinline__ void block_dot(uint32_t q0, uint32_t q1, uint32_t q2, uint32_t q3, uint32_t dbits, int b,
-                                          const Smem &s, const GemvParams &p, float (&acc)[MT]) {
-    const uint32_t lo0 = q0 & 0x0F0F0F0Fu, lo1 = q1 & 0x0F0F0F0Fu, lo2 = q2 & 0x0F0F0F0Fu, lo3 = q3 & 0x0F0F0F0Fu;
-    const uint32_t hi0 = (q0 >> 4) & 0x0F0F0F0Fu, hi1 = (q1 >> 4) & 0x0F0F0F0Fu, hi2 = (q2 >> 4) & 0x0F0F0F0Fu,
-                   hi3 = (q3 >> 4) & 0x0F0F0F0Fu;
-    const float dw = half_bits_to_f32(dbits);
-    const int pair = b >> 1, cb = (b & 1) * 2;
-    const int off_lo = xchunk(pair, cb), off_hi = xchunk(pair, cb + 1);
-    const int xrow = p.nbp * 32;
+// One Q4_0 block, unpacked: low and high nibbles of its 16 code bytes (values
+// 0..15, element j and element j+16 of the block), and its f16 scale.
+struct Blk {
+    uint32_t lo[4], hi[4];
+    float d;
+};
+
+__device__ __forceinline__ Blk unpack(uint32_t q0, uint32_t q1, uint32_t q2, uint32_t q3, uint32_t dbits) {
+    Blk b;
+    const uint32_t q[4] = {q0, q1, q2, q3};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        b.lo[i] = q[i] & 0x0F0F0F0Fu;
+        b.hi[i] = (q[i] >> 4) & 0x0F0F0F0Fu;
+    }
+    b.d = half_bits_to_f32(dbits);
+    return b;
+}
+
+// 12582912 + sum_j nibble_j * x_j, exactly, as float bits.
+__device__ __forceinline__ float magic_dot(const Blk &w, int4 xl, int4 xh) {
+    int I = (int)kMagic;
+    I = __dp4a((int)w.lo[0], xl.x, I);
+    I = __dp4a((int)w.lo[1], xl.y, I);
+    I = __dp4a((int)w.lo[2], xl.z, I);
+    I = __dp4a((int)w.lo[3], xl.w, I);
+    I = __dp4a((int)w.hi[0], xh.x, I);
+    I = __dp4a((int)w.hi[1], xh.y, I);
+    I = __dp4a((int)w.hi[2], xh.z, I);
+    I = __dp4a((int)w.hi[3], xh.w, I);
+    return __int_as_float(I);
+}
+
+// Accumulate blocks b0 = 2*pair and b1 = 2*pair + 1 of up to two rows (A, B)
+// against every activation row m < M.
+template <int MT, bool TWO>
+__device__ __forceinline__ void pair_dot(const Blk &a0, const Blk &a1, const Blk &b0, const Blk &b1, int pair,
+                                         const Smem &s, const GemvParams &p, float (&acc)[2][MT]) {
+    const uint32_t xrow = (uint32_t)p.nbp * 32;
+    const uint32_t c0 = xchunk(pair, 0), c1 = xchunk(pair, 1), c2 = xchunk(pair, 2), c3 = xchunk(pair, 3);
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
         if (m < p.M) {
-            const int4 xl = *reinterpret_cast<const int4 *>(s.xs + m * xrow + off_lo);
-            const int4 xh = *reinterpret_cast<const int4 *>(s.xs + m * xrow + off_hi);
-            int I = (int)kMagic;
-            I = __dp4a((int)lo0, xl.x, I);
-            I = __dp4a((int)lo1, xl.y, I);
-            I = __dp4a((int)lo2, xl.z, I);
-            I = __dp4a((int)lo3, xl.w, I);
-            I = __dp4a((int)hi0, xh.x, I);
-            I = __dp4a((int)hi1, xh.y, I);
-            I = __dp4a((int)hi2, xh.z, I);
-            I = __dp4a((int)hi3, xh.w, I);
-            const float f = __int_as_float(I) - s.xcs[m * p.nbp + b];
-            const float sc = dw * s.xds[m * p.nbp + b];
-            acc[m] = fmaf(f, sc, acc[m]);
+            const uint32_t xb = s.xs + m * xrow;
+            const int4 x0 = lds128(xb + c0), x1 = lds128(xb + c1), x2 = lds128(xb + c2), x3 = lds128(xb + c3);
+            const uint32_t so = (uint32_t)(m * p.nbp + 2 * pair) * 4;
+            const float2 xd = lds64f(s.xds + so), xc = lds64f(s.xcs + so);
+            acc[0][m] = fmaf(magic_dot(a0, x0, x1) - xc.x, a0.d * xd.x, acc[0][m]);
+            acc[0][m] = fmaf(magic_dot(a1, x2, x3) - xc.y, a1.d * xd.y, acc[0][m]);
+            if (TWO) {
+                acc[1][m] = fmaf(magic_dot(b0, x0, x1) - xc.x, b0.d * xd.x, acc[1][m]);
+                acc[1][m] = fmaf(magic_dot(b1, x2, x3) - xc.y, b1.d * xd.y, acc[1][m]);
+            }
+        }
+    }
+}
+
+// Single-block variant for the unstaged path (block b of rows A and B).
+template <int MT, bool TWO>
+__device__ __forceinline__ void single_dot(const Blk &a, const Blk &bb, int b, const Smem &s, const GemvParams &p,
+                                           float (&acc)[2][MT]) {
+    const uint32_t xrow = (uint32_t)p.nbp * 32;
+    const int pair = b >> 1, cb = (b & 1) * 2;
+    const uint32_t cl = xchunk(pair, cb), ch = xchunk(pair, cb + 1);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        if (m < p.M) {
+            const uint32_t xb = s.xs + m * xrow;
+            const int4 xl = lds128(xb + cl), xh = lds128(xb + ch);
+            const uint32_t so = (uint32_t)(m * p.nbp + b) * 4;
+            const float xd = ldsf(s.xds + so), xc = ldsf(s.xcs + so);
+            acc[0][m] = fmaf(magic_dot(a, xl, xh) - xc, a.d * xd, acc[0][m]);
+            if (TWO) acc[1][m] = fmaf(magic_dot(bb, xl, xh) - xc, bb.d * xd, acc[1][m]);
         }
     }
 }
@@ -125,91 +208,150 @@ __device__ __forceinline__ void stage_x(const Smem &s, const GemvParams &p, int 
         int4 v = make_int4(0, 0, 0, 0);
         if (b < p.nb) v = __ldg(reinterpret_cast<const int4 *>(p.xq + m * p.xq_row_stride + b * 32 + half * 16));
         const int pair = b >> 1, c = (b & 1) * 2 + half;
-        *reinterpret_cast<int4 *>(s.xs + m * p.nbp * 32 + xchunk(pair, c)) = v;
+        sts128(s.xs + (uint32_t)m * p.nbp * 32 + xchunk(pair, c), v);
     }
     for (int idx = tid; idx < p.M * p.nbp; idx += nthr) {
         const int m = idx / p.nbp, b = idx % p.nbp;
-        s.xds[idx] = b < p.nb ? __ldg(p.xd + (int64_t)m * p.nb + b) : 0.0f;
-        s.xcs[idx] = b < p.nb ? __ldg(p.xc + (int64_t)m * p.nb + b) : 12582912.0f;
+        stsf(s.xds + idx * 4, b < p.nb ? __ldg(p.xd + (int64_t)m * p.nb + b) : 0.0f);
+        stsf(s.xcs + idx * 4, b < p.nb ? __ldg(p.xc + (int64_t)m * p.nb + b) : 12582912.0f);
     }
 }
 
+// Reduce-scatter across the warp: V = 2*MT values per lane (row r, column m at
+// index r*MT + m). After log2(V) butterfly levels each lane holds a partial of
+// one value, index lane >> (5 - log2 V); the remaining levels finish the sum.
 template <int MT>
-__device__ __forceinline__ void finish_row(float (&acc)[MT], const GemvParams &p, int64_t n, int lane) {
+__device__ __forceinline__ void finish_rows(float (&acc)[2][MT], const GemvParams &p, int64_t n0, bool has_b,
+                                            int lane) {
+    constexpr int V = 2 * MT;
+    constexpr int LOGV = (V == 2) ? 1 : (V == 4) ? 2 : (V == 8) ? 3 : (V == 16) ? 4 : 5;
+    float v[V];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        float v = acc[m];
+    for (int i = 0; i < V; ++i) v[i] = acc[i / MT][i % MT];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        acc[m] = v;
+    for (int k = 0; k < LOGV; ++k) {
+        const int off = 16 >> k;
+        const bool upper = (lane & off) != 0;
+        const int half = V >> (k + 1);
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
     }
-    float mine = 0.0f;
+    float t = v[0];
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-        if (lane == m) mine = acc[m];
-    if (lane < p.M) {
-        if (p.bias) mine = mine + __ldg(p.bias + n);
-        store_out(p.y, p.y_dtype, lane * p.y_row_stride + n, mine);
+    for (int off = 16 >> LOGV; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+    const int idx = lane >> (5 - LOGV);
+    const int r = idx / MT, m = idx % MT;
+    if ((lane & ((1 << (5 - LOGV)) - 1)) == 0 && m < p.M && (r == 0 || has_b)) {
+        const int64_t n = n0 + r;
+        if (p.bias) t = t + __ldg(p.bias + n);
+        store_out(p.y, p.y_dtype, m * p.y_row_stride + n, t);
     }
 }
 
 // 16-bit little-endian loads of one 18-byte block from global memory (the
 // unstaged path: K % 256 != 0, so rows are not 16-byte multiples).
-__device__ __forceinline__ void load_block_global(const uint8_t *blk, uint32_t &d, uint32_t &q0, uint32_t &q1,
-                                                  uint32_t &q2, uint32_t &q3) {
+__device__ __forceinline__ Blk load_block_global(const uint8_t *blk) {
     const unsigned short *h = reinterpret_cast<const unsigned short *>(blk);
     uint32_t u[9];
 #pragma unroll
     for (int i = 0; i < 9; ++i) u[i] = __ldg(h + i);
-    d = u[0];
-    q0 = u[1] | (u[2] << 16);
-    q1 = u[3] | (u[4] << 16);
-    q2 = u[5] | (u[6] << 16);
-    q3 = u[7] | (u[8] << 16);
+    return unpack(u[1] | (u[2] << 16), u[3] | (u[4] << 16), u[5] | (u[6] << 16), u[7] | (u[8] << 16), u[0]);
+}
+
+template <int MT, bool TWO>
+__device__ __forceinline__ void staged_rows(const Smem &s, const GemvParams &p, uint32_t rowA, uint32_t rowB,
+                                            int lane, float (&acc)[2][MT]) {
+    const int npairs = p.nb >> 1;
+    for (int pp = lane; pp < npairs; pp += 32) {
+        const uint32_t a = rowA + pp * 36, b = rowB + pp * 36;
+        uint32_t wa[9], wb[9];
+#pragma unroll
+        for (int i = 0; i < 9; ++i) wa[i] = lds32(a + 4 * i);
+        if (TWO) {
+#pragma unroll
+            for (int i = 0; i < 9; ++i) wb[i] = lds32(b + 4 * i);
+        }
+        const Blk a0 = unpack(__funnelshift_r(wa[0], wa[1], 16), __funnelshift_r(wa[1], wa[2], 16),
+                              __funnelshift_r(wa[2], wa[3], 16), __funnelshift_r(wa[3], wa[4], 16), wa[0] & 0xffffu);
+        const Blk a1 = unpack(wa[5], wa[6], wa[7], wa[8], wa[4] >> 16);
+        Blk b0 = a0, b1 = a1;
+        if (TWO) {
+            b0 = unpack(__funnelshift_r(wb[0], wb[1], 16), __funnelshift_r(wb[1], wb[2], 16),
+                        __funnelshift_r(wb[2], wb[3], 16), __funnelshift_r(wb[3], wb[4], 16), wb[0] & 0xffffu);
+            b1 = unpack(wb[5], wb[6], wb[7], wb[8], wb[4] >> 16);
+        }
+        pair_dot<MT, TWO>(a0, a1, b0, b1, pp, s, p, acc);
+    }
+}
+
+template <int MT, bool TWO>
+__device__ __forceinline__ void global_rows(const Smem &s, const GemvParams &p, const uint8_t *rowA,
+                                            const uint8_t *rowB, int lane, float (&acc)[2][MT]) {
+    for (int b = lane; b < p.nb; b += 32) {
+        const Blk a = load_block_global(rowA + b * 18);
+        const Blk bb = TWO ? load_block_global(rowB + b * 18) : a;
+        single_dot<MT, TWO>(a, bb, b, s, p, acc);
+    }
 }
 
 template <int MT, bool STAGED>
-__global__ void __launch_bounds__(kThreads, 1) q4_gemv_q8_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, p);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t G = gridDim.x, c = blockIdx.x;
     const int64_t r0 = c * p.N / G, r1 = (c + 1) * p.N / G;
     const int nrows = (int)(r1 - r0);
+    // Chunks of R = 2 * wpc consecutive rows; chunk j lives in slot j % nslots
+    // and is consumed by warp group j % groups (wpc warps, two rows each).
+    const int wpc = p.wpc, R = 2 * p.wpc, groups = kConsumerWarps / p.wpc;
+    const int nchunks = (nrows + R - 1) / R;
 
     if (STAGED && threadIdx.x == 0) {
         for (int i = 0; i < p.nslots; ++i) {
             mbar_init(&s.full[i], 1);
-            mbar_init(&s.empty[i], 1);
+            mbar_init(&s.empty[i], (uint32_t)wpc);
         }
         fence_mbar_init();
     }
     __syncthreads();
+    // Let the next kernel in the stream be scheduled now: it waits for this
+    // grid's completion (griddepcontrol.wait) before it reads anything this
+    // grid writes, and until then only prefetches its own static weights.
+    if (threadIdx.x == 0) pdl_launch_dependents();
 
     if (warp == kConsumerWarps) {
-        // ---------------- producer: one lane streams this CTA's weight rows
+        // ---------------- producer: one lane streams this CTA's weight rows,
+        // one bulk copy per chunk (the CTA's rows are contiguous in the blob).
         if (STAGED && lane == 0) {
-            // The weights may have been written by the previous kernel in the
-            // stream (a quantise on the device), so wait for it like the
-            // consumers do.
-            pdl_wait();
+            // Unless the caller vouches that nothing queued before this call
+            // writes the weights (TN_WEIGHTS_STATIC), wait for the previous
+            // kernel like the consumers do; otherwise start streaming weights
+            // while it finishes.
+            if (!(p.flags & TN_WEIGHTS_STATIC)) pdl_wait();
             const uint64_t pol = policy_evict_first();
             int issued = 0;
-            for (int i = 0; i < nrows; ++i) {
-                const int slot = i % p.nslots, use = i / p.nslots;
+            for (int j = 0; j < nchunks; ++j) {
+                const int slot = j % p.nslots, use = j / p.nslots;
                 if (use > 0 && !mbar_wait(&s.empty[slot], (use - 1) & 1)) {
                     record_device_error(p.err, DEV_ERR_WAIT_EMPTY);
                     break;
                 }
-                mbar_arrive_expect_tx(&s.full[slot], (uint32_t)p.rowbytes);
-                bulk_g2s_hint(s.slots + (size_t)slot * p.rowbytes, p.w + (r0 + i) * (int64_t)p.rowbytes,
-                              (uint32_t)p.rowbytes, &s.full[slot], pol);
-                issued = i + 1;
+                const int rows = min(R, nrows - j * R);
+                const uint32_t bytes = (uint32_t)rows * (uint32_t)p.rowbytes;
+                mbar_arrive_expect_tx(&s.full[slot], bytes);
+                bulk_g2s_hint_u32(s.slots + (uint32_t)slot * p.slot_bytes, p.w + (r0 + (int64_t)j * R) * p.rowbytes,
+                                  bytes, &s.full[slot], pol);
+                issued = j + 1;
             }
             // Drain: every copy issued must have landed before the CTA exits.
             // (On the normal path the consumers already waited for all of them.)
-            for (int i = issued > p.nslots ? issued - p.nslots : 0; i < issued; ++i) {
-                if (!mbar_wait(&s.full[i % p.nslots], (i / p.nslots) & 1)) {
+            for (int j = issued > p.nslots ? issued - p.nslots : 0; j < issued; ++j) {
+                if (!mbar_wait(&s.full[j % p.nslots], (j / p.nslots) & 1)) {
                     record_device_error(p.err, DEV_ERR_DRAIN);
                     break;
                 }
@@ -223,38 +365,36 @@ __global__ void __launch_bounds__(kThreads, 1) q4_gemv_q8_kernel(const GemvParam
     stage_x(s, p, threadIdx.x, kConsumerWarps * 32);
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
-    const int npairs = p.nb >> 1;
-    for (int i = warp; i < nrows; i += kConsumerWarps) {
-        const int64_t n = r0 + i;
-        float acc[MT];
+    const int group = warp / wpc, gw = warp % wpc;
+    for (int j = group; j < nchunks; j += groups) {
+        const int i = j * R + 2 * gw;  // my first row within the CTA's range
+        const bool has_a = i < nrows, has_b = i + 1 < nrows;
+        float acc[2][MT];
 #pragma unroll
-        for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) acc[r][m] = 0.0f;
         if (STAGED) {
-            const int slot = i % p.nslots;
-            if (!mbar_wait(&s.full[slot], (i / p.nslots) & 1)) {
+            const int slot = j % p.nslots;
+            if (!mbar_wait(&s.full[slot], (j / p.nslots) & 1)) {
                 record_device_error(p.err, DEV_ERR_WAIT_FULL);
                 return;
             }
-            const uint32_t *row = reinterpret_cast<const uint32_t *>(s.slots + (size_t)slot * p.rowbytes);
-            for (int pp = lane; pp < npairs; pp += 32) {
-                const uint32_t *w9 = row + pp * 9;
-                const uint32_t w0 = w9[0], w1 = w9[1], w2 = w9[2], w3 = w9[3], w4 = w9[4];
-                const uint32_t w5 = w9[5], w6 = w9[6], w7 = w9[7], w8 = w9[8];
-                block_dot<MT>(__funnelshift_r(w0, w1, 16), __funnelshift_r(w1, w2, 16), __funnelshift_r(w2, w3, 16),
-                              __funnelshift_r(w3, w4, 16), w0 & 0xffffu, 2 * pp, s, p, acc);
-                block_dot<MT>(w5, w6, w7, w8, w4 >> 16, 2 * pp + 1, s, p, acc);
-            }
+            const uint32_t ra = s.slots + (uint32_t)slot * p.slot_bytes + (uint32_t)(2 * gw) * p.rowbytes;
+            if (has_b)
+                staged_rows<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
+            else if (has_a)
+                staged_rows<MT, false>(s, p, ra, ra, lane, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.empty[slot]);
-        } else {
-            const uint8_t *row = p.w + n * (int64_t)p.rowbytes;
-            for (int b = lane; b < p.nb; b += 32) {
-                uint32_t d, q0, q1, q2, q3;
-                load_block_global(row + b * 18, d, q0, q1, q2, q3);
-                block_dot<MT>(q0, q1, q2, q3, d, b, s, p, acc);
-            }
+        } else if (has_a) {
+            const uint8_t *ra = p.w + (r0 + i) * (int64_t)p.rowbytes;
+            if (has_b)
+                global_rows<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
+            else
+                global_rows<MT, false>(s, p, ra, ra, lane, acc);
         }
-        finish_row<MT>(acc, p, n, lane);
+        if (has_a) finish_rows<MT>(acc, p, r0 + i, has_b, lane);
     }
 }
 
@@ -287,10 +427,44 @@ int launch_variant(const GemvParams &p, int grid, size_t smem, cudaStream_t stre
     return TN_OK;
 }
 
-size_t smem_bytes(int M, int nbp, int nslots, int rowbytes) {
+size_t smem_bytes(int M, int nbp, int nslots, int slot_bytes) {
     size_t off = 16 * kMaxSlots + (size_t)M * nbp * 40;
     off = (off + 127) & ~size_t(127);
-    return off + (size_t)nslots * rowbytes;
+    return off + (size_t)nslots * slot_bytes;
+}
+
+struct Plan {
+    bool ok;
+    int wpc, slot_bytes, nslots;
+};
+
+// Chunk size and ring depth. A chunk is 2 * wpc rows copied by one bulk copy:
+// the largest wpc whose chunk stays within ~24 KB (many small copies in flight
+// were measured to cap the fetch rate), and enough slots for ~128 KB in flight
+// per SM. nslots is a multiple of the number of warp groups, so chunk j and
+// chunk j - nslots belong to the same group and no warp ever waits on a slot's
+// barrier more than one phase ahead (parity waits cannot tell phases two apart).
+Plan plan_slots(int M, int nbp, int rowbytes, bool staged, size_t budget, size_t in_flight) {
+    Plan pl{false, 1, 0, 0};
+    const size_t base = smem_bytes(M, nbp, 0, 0);
+    if (!staged) {
+        pl.ok = base <= budget;
+        pl.wpc = kConsumerWarps / 2;
+        return pl;
+    }
+    int wpc = kConsumerWarps;
+    while (wpc > 1 && 2 * wpc * rowbytes > 24 * 1024) wpc >>= 1;
+    const int groups = kConsumerWarps / wpc;
+    const int slot_bytes = 2 * wpc * rowbytes;
+    if (base + (size_t)groups * slot_bytes > budget) return pl;
+    int nslots = (int)((budget - base) / slot_bytes);
+    const int want = (int)((in_flight + slot_bytes - 1) / slot_bytes);
+    nslots = nslots < want ? nslots : want;
+    nslots = nslots < kMaxSlots ? nslots : kMaxSlots;
+    nslots = (nslots / groups) * groups;
+    if (nslots < groups) return pl;
+    pl = Plan{true, wpc, slot_bytes, nslots};
+    return pl;
 }
 
 }  // namespace
@@ -301,13 +475,13 @@ int q4_gemv_max_rows(int64_t K) {
     const int nb = (int)(K / 32), nbp = (nb + 1) & ~1, rowbytes = 18 * nb;
     const bool staged = (K % 256 == 0);
     for (int mt = 16; mt >= 1; mt >>= 1)
-        if (smem_bytes(mt, nbp, staged ? kConsumerWarps : 0, rowbytes) <= (size_t)f.smem_optin) return mt;
+        if (plan_slots(mt, nbp, rowbytes, staged, (size_t)f.smem_optin, 128 * 1024).ok) return mt;
     return 0;
 }
 
 int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
                       const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
-                      cudaStream_t stream) {
+                      int flags, cudaStream_t stream) {
     const char *op = "torch._C._quantized_linear";
     DeviceFacts f{};
     int st = device_facts(&f);
@@ -329,31 +503,25 @@ int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const
     p.rowbytes = 18 * p.nb;
     p.err = device_error_word();
     const bool staged = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(w) & 15) == 0);
-    const size_t budget = (size_t)f.smem_optin;
-    int nslots = 0;
-    if (staged) {
-        const size_t base = smem_bytes(M, p.nbp, 0, p.rowbytes);
-        if (base + (size_t)kConsumerWarps * p.rowbytes > budget)
-            return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: activation tile too large for "
-                                                                       "shared memory");
-        nslots = (int)((budget - base) / p.rowbytes);
-        // ~96 KB in flight per SM covers HBM latency; more only costs occupancy.
-        const int want = (int)((96 * 1024 + p.rowbytes - 1) / p.rowbytes);
-        nslots = nslots < want ? nslots : want;
-        nslots = nslots < kMaxSlots ? nslots : kMaxSlots;
-        // A multiple of the consumer-warp count: row i and row i - nslots then
-        // belong to the same warp, so no warp ever waits on a slot's barrier
-        // more than one phase ahead (parity waits cannot tell phases two apart).
-        nslots = (nslots / kConsumerWarps) * kConsumerWarps;
-        nslots = nslots > kConsumerWarps ? nslots : kConsumerWarps;
-    } else if (smem_bytes(M, p.nbp, 0, 0) > budget) {
+    // Two CTAs per SM for M <= 2 (each with ~64 KB in flight): the next
+    // kernel's CTAs can then start streaming while this one's last CTAs drain.
+    Plan plan{false, 1, 0, 0};
+    int ctas_per_sm = 1;
+    if (M <= 2) {
+        plan = plan_slots(M, p.nbp, p.rowbytes, staged, kTwoCtaBudget, 64 * 1024);
+        if (plan.ok) ctas_per_sm = 2;
+    }
+    if (!plan.ok) plan = plan_slots(M, p.nbp, p.rowbytes, staged, (size_t)f.smem_optin, 128 * 1024);
+    if (!plan.ok)
         return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: activation tile too large for "
                                                                    "shared memory");
-    }
-    p.nslots = nslots;
-    const size_t smem = smem_bytes(M, p.nbp, nslots, p.rowbytes);
-    int64_t grid = f.sm_count;
-    const int64_t by_rows = (N + kConsumerWarps - 1) / kConsumerWarps;
+    p.wpc = plan.wpc;
+    p.slot_bytes = plan.slot_bytes;
+    p.nslots = plan.nslots;
+    const size_t smem = smem_bytes(M, p.nbp, plan.nslots, plan.slot_bytes);
+    p.flags = flags;
+    int64_t grid = (int64_t)f.sm_count * ctas_per_sm;
+    const int64_t by_rows = (N + 2 * plan.wpc - 1) / (2 * plan.wpc);
     if (by_rows < grid) grid = by_rows > 0 ? by_rows : 1;
 #define TN_GEMV_CASE(MT)                                                                   \
     if (M <= MT)                                                                           \

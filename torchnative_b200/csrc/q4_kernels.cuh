@@ -17,6 +17,6 @@ int q4_gemv_max_rows(int64_t K);
 // Decode GEMV over planar Q8_0 activations: y[m, n] for m < M (M <= 16).
 int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
                       const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
-                      cudaStream_t stream);
+                      int flags, cudaStream_t stream);
 
 }  // namespace tn

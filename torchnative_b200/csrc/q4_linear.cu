@@ -56,7 +56,7 @@ extern "C" int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, 
         const int mc = (int)((M - m0) < chunk ? (M - m0) : chunk);
         st = tn::launch_q4_gemv_q8(static_cast<const uint8_t *>(w_blob), xq + m0 * K, xd + m0 * nb, xc + m0 * nb, K,
                                    bias, static_cast<uint8_t *>(y) + (size_t)m0 * N * ysz, y_dtype, N, mc, N, K,
-                                   stream);
+                                   0, stream);
         if (st) return st;
     }
     return TN_OK;
@@ -84,7 +84,7 @@ extern "C" int tn_q8_0_quantize_planar(const void *x, int x_dtype, int64_t x_row
 
 extern "C" int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, const float *scales,
                                  const float *offsets, const void *w_blob, const float *bias, void *y, int y_dtype,
-                                 int64_t M, int64_t N, int64_t K, void *stream_) {
+                                 int64_t M, int64_t N, int64_t K, int flags, void *stream_) {
     const std::string op = "torch._C._quantized_linear";
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
@@ -109,7 +109,8 @@ extern "C" int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, 
         const int mc = (int)((M - m0) < chunk ? (M - m0) : chunk);
         int st = tn::launch_q4_gemv_q8(static_cast<const uint8_t *>(w_blob), codes + m0 * codes_row_stride,
                                        scales + m0 * nb, offsets + m0 * nb, codes_row_stride, bias,
-                                       static_cast<uint8_t *>(y) + (size_t)m0 * N * ysz, y_dtype, N, mc, N, K, stream);
+                                       static_cast<uint8_t *>(y) + (size_t)m0 * N * ysz, y_dtype, N, mc, N, K, flags,
+                                       stream);
         if (st) return st;
     }
     return TN_OK;

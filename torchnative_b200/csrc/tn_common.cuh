@@ -114,6 +114,16 @@ __device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32
         : "memory");
 }
 
+// Same, destination given as a 32-bit shared-window address.
+__device__ __forceinline__ void bulk_g2s_hint_u32(uint32_t dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                                  uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            dst),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
