@@ -1,15 +1,98 @@
 // sdpa.cu -- tn_sdpa_flash_attention: the C-ABI door of
-// aten._scaled_dot_product_flash_attention_for_cpu (torch_c/src/aten.rs:10092-10460).
-#include "tn_common.cuh"
+// aten._scaled_dot_product_flash_attention_for_cpu (torch_c/src/aten.rs:10092-10460)
+// on a B200. Argument checks follow the reference's order and wording
+// (aten.rs:10113-10172, 10226-10261, 17112-17122).
+#include <cmath>
+
+#include "sdpa_common.cuh"
+
+namespace {
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
 
 extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void *v, const void *attn_mask,
                                        int mask_dtype, const int64_t *mask_strides, void *out, float *lse, int dtype,
                                        int64_t B, int64_t Hq, int64_t Hkv, int64_t L, int64_t S, int64_t D,
                                        const int64_t *q_strides, const int64_t *k_strides, const int64_t *v_strides,
-                                       int is_causal, double scale, void *stream) {
-    (void)q, (void)k, (void)v, (void)attn_mask, (void)mask_dtype, (void)mask_strides, (void)out, (void)lse;
-    (void)dtype, (void)B, (void)Hq, (void)Hkv, (void)L, (void)S, (void)D, (void)q_strides, (void)k_strides;
-    (void)v_strides, (void)is_causal, (void)scale, (void)stream;
-    return tn::set_error(TN_ERR_NOT_IMPLEMENTED,
-                         "aten._scaled_dot_product_flash_attention_for_cpu.default: not implemented on CUDA yet");
+                                       int is_causal, double scale, void *stream_) {
+    const std::string op = "aten._scaled_dot_product_flash_attention_for_cpu.default";
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    __atomic_fetch_add(&tn::counters().sdpa_calls, 1ull, __ATOMIC_RELAXED);
+    if (dtype == TN_F64)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": torch.float64 attention is not implemented on CUDA");
+    if (dtype != TN_F32 && dtype != TN_BF16 && dtype != TN_F16)
+        return tn::set_error(TN_ERR_SHAPE, "scaled_dot_product_attention_flash_attention: Expected data type in FP32, "
+                                           "FP64, BF16, FP16, but got " +
+                                               std::string(tn_dtype_name(dtype)) + " instead.");
+    if (B < 0 || Hq < 0 || Hkv < 0 || L < 0 || S < 0 || D < 0)
+        return tn::set_error(TN_ERR_SHAPE, op + ": negative size");
+    if (D == 0 || S == 0)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED,
+                             op + ": a zero key length or head dimension is not implemented in torch._C shim");
+    if (B == 0 || Hq == 0 || L == 0) return TN_OK;
+    if (Hkv == 0 || Hq % Hkv != 0)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED,
+                             op + ": grouped-query attention with " + std::to_string(Hq) + " query heads and " +
+                                 std::to_string(Hkv) +
+                                 " key/value heads is not implemented in torch._C shim -- the head counts do not divide");
+    if (D != 64 && D != 128)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED,
+                             op + ": head dimension " + std::to_string(D) + " is not implemented on CUDA (64, 128)");
+    if (attn_mask && mask_dtype != TN_F32 && mask_dtype != dtype)
+        return tn::set_error(TN_ERR_SHAPE, "scaled_dot_product_attention_flash_attention: Attention mask is the same "
+                                           "data type as query");
+    if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides || (attn_mask && !mask_strides))
+        return tn::set_error(TN_ERR_INVALID, op + ": null pointer");
+    if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1)
+        return tn::set_error(TN_ERR_INVALID, op + ": the head dimension must have unit stride");
+    const size_t es = tn_dtype_size(dtype);
+    for (int i = 0; i < 3; ++i)
+        if ((k_strides[i] * (int64_t)es) % 16 != 0 || (v_strides[i] * (int64_t)es) % 16 != 0)
+            return tn::set_error(TN_ERR_INVALID, op + ": key/value strides must be multiples of 16 bytes");
+    if (!aligned16(k) || !aligned16(v))
+        return tn::set_error(TN_ERR_INVALID, op + ": key/value must be 16-byte aligned");
+    if (B > 65535 || Hkv > 65535 || S > (int64_t)1 << 30 || L > (int64_t)1 << 30)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": size beyond the kernel's grid limits");
+
+    tn::DeviceFacts f{};
+    int st = tn::device_facts(&f);
+    if (st) return st;
+    tn::SdpaParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.mask = attn_mask;
+    p.out = out;
+    p.lse = lse;
+    for (int i = 0; i < 4; ++i) {
+        p.qs[i] = q_strides[i];
+        p.ks[i] = k_strides[i];
+        p.vs[i] = v_strides[i];
+        p.ms[i] = attn_mask ? mask_strides[i] : 0;
+    }
+    p.B = (int)B;
+    p.Hq = (int)Hq;
+    p.Hkv = (int)Hkv;
+    p.L = (int)L;
+    p.S = (int)S;
+    p.D = (int)D;
+    p.rep = (int)(Hq / Hkv);
+    p.mask_dtype = mask_dtype;
+    p.causal = is_causal ? 1 : 0;
+    // Default 1/sqrt(D) in f64, then f32 (candle's affine casts its f64 multiplier).
+    const double sc = (std::isnan(scale) || scale <= 0.0) ? 1.0 / std::sqrt((double)D) : scale;
+    p.scale = (float)sc;
+    p.err = tn::device_error_word();
+
+    st = tn::plan_sdpa_decode(p, f.sm_count);
+    if (st) return st;
+    void *ws = nullptr;
+    st = tn::workspace(&ws, tn::sdpa_decode_workspace(p), stream, /*slot=*/1);
+    if (st) return st;
+    const int64_t rows = (int64_t)p.B * p.Hq * p.L;
+    p.part_o = static_cast<float *>(ws);
+    p.part_ml = p.part_o + rows * p.splits * p.D;
+    return tn::launch_sdpa_decode(p, dtype, stream);
 }

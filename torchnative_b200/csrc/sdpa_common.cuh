@@ -1,0 +1,34 @@
+// sdpa_common.cuh -- shared definitions of the attention kernels.
+#pragma once
+
+#include "tn_common.cuh"
+
+namespace tn {
+
+// One attention call, as the kernels see it. Element strides in [b, h, t, d]
+// order; the d stride is 1 for q, k, v.
+struct SdpaParams {
+    const void *q, *k, *v, *mask;
+    void *out;
+    float *lse;
+    int64_t qs[4], ks[4], vs[4], ms[4];
+    int B, Hq, Hkv, L, S, D;
+    int rep;        // Hq / Hkv
+    int mask_dtype; // TN_F32 or the input dtype
+    int causal;
+    float scale;
+    // split-KV decode
+    int rows;       // query rows per CTA (rep * L or a slice of it)
+    int row_groups; // ceil(rep * L / rows)
+    int splits;     // key splits per (b, kv head, row group)
+    int keys_per_split;
+    float *part_o;  // [B*Hq*L][splits][D] f32 unnormalised partial outputs
+    float *part_ml; // [B*Hq*L][splits][2]  running max and sum
+    int *err;
+};
+
+int launch_sdpa_decode(const SdpaParams &p, int dtype, cudaStream_t stream);
+size_t sdpa_decode_workspace(const SdpaParams &p);
+int plan_sdpa_decode(SdpaParams &p, int sm_count);
+
+}  // namespace tn
