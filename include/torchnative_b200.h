@@ -167,6 +167,25 @@ TN_API int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, cons
                              const float *offsets, const void *w_blob, const float *bias, void *y,
                              int y_dtype, int64_t M, int64_t N, int64_t K, int flags, void *stream);
 
+/* tn_q4_0_linear without any device allocation. No counterpart in the
+ * reference: it exists for hosts that cannot let a library call cudaMalloc
+ * while they run -- an engine that owns a preplanned arena of HBM, work being
+ * recorded into a CUDA graph under global capture mode, a loop that cannot
+ * absorb cudaMalloc's implicit synchronisation. Same arguments, arithmetic and
+ * result as tn_q4_0_linear in TN_ACT_Q8_0 mode; the Q8_0 activation blocks go
+ * to a fixed __device__ array inside this library (320 KB, held on every GPU
+ * that loads the library until the process exits) instead of the allocator.
+ * Limits: M <= TN_NOALLOC_MAX_ROWS and K <= TN_NOALLOC_MAX_IN; larger calls
+ * return TN_ERR_SHAPE and allocate nothing. The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress, that device current);
+ * make it before any stream capture. All calls share the one array, so calls
+ * that can overlap on the GPU (unordered streams) race. */
+#define TN_NOALLOC_MAX_ROWS 16
+#define TN_NOALLOC_MAX_IN 16384
+TN_API int tn_q4_0_linear_noalloc(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob,
+                                  const float *bias, void *y, int y_dtype, int64_t M, int64_t N,
+                                  int64_t K, void *stream);
+
 /* ------------------------------------------------------------ SDPA family -- */
 
 /* aten._scaled_dot_product_flash_attention_for_cpu.default(query, key, value,

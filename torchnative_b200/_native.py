@@ -55,6 +55,7 @@ SIGNATURES = {
     "tn_q4_0_linear": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
     "tn_q8_0_quantize_planar": (_I, [_P, _I, _I64, _P, _I64, _P, _P, _I64, _I64, _P]),
     "tn_q4_0_linear_q8": (_I, [_P, _I64, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
+    "tn_q4_0_linear_noalloc": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
     "tn_sdpa_flash_attention": (_I, [_P, _P, _P, _P, _I, _PI64, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64,
                                      _PI64, _PI64, _PI64, _I, _D, _P]),
 }
