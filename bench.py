@@ -1,20 +1,23 @@
 """bench.py -- the driver's benchmark contract.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
 
-Workload (Llama-3-8B-shaped, batch 1): one step is
-the Q4_0 part of one greedy decode token -- for each of the 32 layers the
-fused q/k/v projection (6144 x 4096), o_proj (4096 x 4096), the fused
-gate/up projection (28672 x 4096) and down_proj (4096 x 14336), each preceded
-by the Q8_0 activation quantiser the reference runs, then lm_head
-(128256 x 4096): 4.22 GB of Q4_0 weights, all random (codes uniform in
-[-8, 7], scales f16(|N(0,1)| * 0.01)), bf16 activations. The weights (4.2 GB)
-are far larger than L2 (126 MB), so nothing is re-read from L2 between steps.
-The step is captured once in a CUDA graph and replayed.
+Workload (Llama-3-8B-shaped, batch 1 by default): one
+step is one greedy decode token, the whole of it -- for each of 32 layers:
+RMSNorm (+ the Q8_0 activation quantiser the reference runs before every Q4_0
+linear), the fused q/k/v Q4_0 linear (6144 x 4096), RoPE + KV-cache append,
+SDPA against the cache (32 query / 8 KV heads, D = 128), o_proj (4096 x 4096),
+residual + RMSNorm, the fused gate/up Q4_0 linear (28672 x 4096), SiLU*up,
+down_proj (4096 x 14336), residual; then final norm, lm_head (128256 x 4096),
+argmax and the next token's embedding. The KV cache holds a 2048-token prompt
+(synthetic values) and grows by one slot per step. Weights are random Q4_0
+blobs (codes uniform in [-8, 7], scales f16(|N(0,1)| * 0.01)), bf16
+activations. 4.2 GB of weights per token, far beyond L2 (126 MB). The step is
+one CUDA graph, replayed.
 
 Prints one JSON line (rank 0). `value` is device-resident tokens/s; `e2e`
-adds, every step, the pinned host->device copy of the token's hidden state
-and the device->host copy of the logits.
+adds, every step, the pinned host->device copy of the input token ids, their
+embedding, and the device->host copy of the next token ids.
 """
 
 from __future__ import annotations
@@ -54,6 +57,7 @@ def parse():
                     help="kernel-level case instead of the decode step: 'gemv' times the decode GEMV alone on the "
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
     ap.add_argument("--rows", type=int, default=1, help="activation rows M for --case gemv")
+    ap.add_argument("--batch", type=int, default=1, help="sequences decoded together (BASELINE: 1 and 16)")
     return ap.parse_args()
 
 
@@ -115,107 +119,40 @@ class ClockSampler:
 
 
 def random_q4_blob(n: int, k: int, gen, dev):
-    """Q4_0 blob built directly in the block layout on the device: two nibbles
-    of uniform random bytes (codes uniform in [-8, 7]) and f16 scales
-    |N(0,1)| * 0.01."""
-    import torch
+    from torchnative_b200.llama_decode import random_q4_blob as r
 
-    nb = k // 32
-    qs = torch.randint(0, 256, (n, nb, 16), dtype=torch.uint8, device=dev, generator=gen)
-    d = (torch.randn((n, nb, 1), device=dev, generator=gen).abs() * 0.01).to(torch.float16).view(torch.uint8)
-    return torch.cat([d, qs], dim=2).reshape(-1).contiguous()
+    return r(n, k, gen, dev)
 
 
-class Q4DecodeStack:
-    """The Q4_0 linears of a Llama-3-8B-shaped decode step at batch M, through
-    the C ABI (planar Q8_0 quantiser + decode GEMV per linear)."""
-
-    def __init__(self, dev, M=1, seed=0):
-        import torch
-
-        from torchnative_b200 import _native as N
-
-        self.N = N
-        self.dev, self.M = dev, M
-        gen = torch.Generator(device=dev)
-        gen.manual_seed(seed)
-        self.layers = [{name: random_q4_blob(n, k, gen, dev) for name, n, k in LAYER_LINEARS} for _ in range(LAYERS)]
-        self.lm_head = random_q4_blob(VOCAB, HIDDEN, gen, dev)
-        bf = torch.bfloat16
-        self.h = torch.randn((M, HIDDEN), device=dev, generator=gen).to(bf)
-        self.attn = torch.randn((M, HIDDEN), device=dev, generator=gen).to(bf)
-        self.act = torch.randn((M, INTER), device=dev, generator=gen).to(bf)
-        self.qkv = torch.empty((M, QKV_N), device=dev, dtype=bf)
-        self.o = torch.empty((M, HIDDEN), device=dev, dtype=bf)
-        self.gu = torch.empty((M, 2 * INTER), device=dev, dtype=bf)
-        self.down = torch.empty((M, HIDDEN), device=dev, dtype=bf)
-        self.logits = torch.empty((M, VOCAB), device=dev, dtype=bf)
-        kmax = INTER
-        self.codes = torch.empty((M, kmax), device=dev, dtype=torch.int8)
-        self.scales = torch.empty((M, kmax // 32), device=dev, dtype=torch.float32)
-        self.offsets = torch.empty((M, kmax // 32), device=dev, dtype=torch.float32)
-        self.weight_bytes = sum(q4_bytes(n, k) for _, n, k in LAYER_LINEARS) * LAYERS + q4_bytes(VOCAB, HIDDEN)
-
-    def _linear(self, x, w, y, n, k, stream):
-        import ctypes
-
-        L = self.N.lib()
-        P = ctypes.c_void_p
-        self.N.check(L.tn_q8_0_quantize_planar(P(x.data_ptr()), self.N.TN_BF16, k, P(self.codes.data_ptr()), k,
-                                               P(self.scales.data_ptr()), P(self.offsets.data_ptr()), self.M, k,
-                                               stream))
-        self.N.check(L.tn_q4_0_linear_q8(P(self.codes.data_ptr()), k, P(self.scales.data_ptr()),
-                                         P(self.offsets.data_ptr()), P(w.data_ptr()), None, P(y.data_ptr()),
-                                         self.N.TN_BF16, self.M, n, k, self.N.TN_WEIGHTS_STATIC, stream))
-
-    def step(self, stream):
-        """One decode token's Q4_0 work: 4 linears x 32 layers + lm_head."""
-        for lw in self.layers:
-            self._linear(self.h, lw["qkv"], self.qkv, QKV_N, HIDDEN, stream)
-            self._linear(self.attn, lw["o"], self.o, HIDDEN, HIDDEN, stream)
-            self._linear(self.h, lw["gate_up"], self.gu, 2 * INTER, HIDDEN, stream)
-            self._linear(self.act, lw["down"], self.down, HIDDEN, INTER, stream)
-        self._linear(self.h, self.lm_head, self.logits, VOCAB, HIDDEN, stream)
-
-    kernels_per_step = 2 * (4 * LAYERS + 1)
-
-    def dominant_launch(self, stream, layer):
-        """The gate/up GEMV alone (the largest Q4_0 kernel of a layer)."""
-        import ctypes
-
-        L = self.N.lib()
-        P = ctypes.c_void_p
-        self.N.check(L.tn_q4_0_linear_q8(P(self.codes.data_ptr()), HIDDEN, P(self.scales.data_ptr()),
-                                         P(self.offsets.data_ptr()), P(self.layers[layer]["gate_up"].data_ptr()),
-                                         None, P(self.gu.data_ptr()), self.N.TN_BF16, self.M, 2 * INTER, HIDDEN,
-                                         self.N.TN_WEIGHTS_STATIC, stream))
-
-    def dominant_algorithmic_bytes(self):
-        n, k = 2 * INTER, HIDDEN
-        # weights + planar Q8_0 activations (codes + scale + offset per block) + bf16 output
-        return q4_bytes(n, k) + self.M * (k + k // 32 * 8) + self.M * n * 2
+PROMPT = 2048
 
 
 # --------------------------------------------------------------------------- CPU side
 
 
-def cpu_step_seconds(layer_blobs: dict, lm_head_blob, threads: int, reps: int = 1) -> float:
-    """The reference's CPU arithmetic (oracle/tn_oracle.c: Q8_0 activations,
-    vec_dot_unopt, 4-column quads over `threads` workers) over one token:
-    the four linears of a layer 32 times (the same layer's weights each time)
-    and lm_head. Returns seconds per token (min over reps)."""
+def cpu_step_seconds(layer_blobs: dict, lm_head_blob, threads: int, reps: int = 1, context: int = PROMPT) -> float:
+    """The reference's CPU arithmetic (oracle/tn_oracle.c) for the two hot
+    operators of one token: per layer the four Q4_0 linears (Q8_0 activations,
+    vec_dot_unopt, 4-column quads over `threads` workers; the same layer's
+    weights each time) and SDPA over a `context`-token cache (sdpa_flash_cpu's
+    default arithmetic, f32), then lm_head. Returns seconds per token (min over
+    reps). The glue between them (norms, RoPE, SiLU) is not timed."""
     import numpy as np
 
     from oracle import oracle
 
     rng = np.random.default_rng(1)
     xs = {k: rng.standard_normal((1, k)).astype(np.float32) for k in (HIDDEN, INTER)}
+    q = rng.standard_normal((1, HEADS, 1, HEAD_DIM)).astype(np.float32)
+    kc = rng.standard_normal((1, KV_HEADS, context, HEAD_DIM)).astype(np.float32)
+    vc = rng.standard_normal((1, KV_HEADS, context, HEAD_DIM)).astype(np.float32)
     best = float("inf")
     for _ in range(reps):
         t0 = time.perf_counter()
         for _layer in range(LAYERS):
             for name, n, k in LAYER_LINEARS:
                 oracle.q4_0_linear(xs[k], layer_blobs[name], n, threads=threads)
+            oracle.sdpa(q, kc, vc, threads=threads)
         oracle.q4_0_linear(xs[HIDDEN], lm_head_blob, VOCAB, threads=threads)
         best = min(best, time.perf_counter() - t0)
     return best
@@ -293,31 +230,38 @@ def run_ours(args, rank, world, local):
     import torch
 
     from torchnative_b200 import _native, build
+    from torchnative_b200.llama_decode import LLAMA3_8B, Q4LlamaDecoder
 
     build.build()
     dev = torch.device("cuda", local)
-    stack = Q4DecodeStack(dev, M=1, seed=1234 + rank)
-    cur = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+    B = args.batch
+    cap = PROMPT + args.warmup + args.steps + 8
+    dec = Q4LlamaDecoder(LLAMA3_8B, batch=B, capacity=cap, device=dev, seed=1234 + rank)
+    P = ctypes.c_void_p
+    cur = lambda: P(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+    first = torch.randint(0, LLAMA3_8B.vocab, (B,), device=dev, dtype=torch.int32)
 
-    # eager warm-up: sets kernel attributes, checks the path runs
-    stack.step(cur())
-    torch.cuda.synchronize()
+    dec.fill_prompt_cache(PROMPT)
+    dec.start(first)
+    g = dec.capture()  # runs one eager step, then captures
     _native.device_status(reset=True)
+    dec.fill_prompt_cache(PROMPT)
+    dec.start(first)
 
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        stack.step(cur())
+    # the dominant kernel alone: 32 back-to-back gate/up GEMVs over the 32 layers' weights
     gd = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gd):
-        for layer in range(LAYERS):
-            stack.dominant_launch(cur(), layer)
+        for lw in dec.layers:
+            _native.check(_native.lib().tn_q4_0_linear_q8(
+                P(dec.codes.data_ptr()), HIDDEN, P(dec.scales.data_ptr()), P(dec.offsets.data_ptr()),
+                P(lw["gate_up"].data_ptr()), None, P(dec.gu.data_ptr()), _native.TN_BF16, B, 2 * INTER, HIDDEN,
+                _native.TN_WEIGHTS_STATIC, cur()))
 
     for _ in range(args.warmup):
         g.replay()
     torch.cuda.synchronize()
     barrier(world)
-
-    _native.reset_counters()
+    pos0 = int(dec.pos.item())
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
@@ -327,29 +271,36 @@ def run_ours(args, rank, world, local):
         end.record()
         torch.cuda.synchronize()
     ms = start.elapsed_time(end) / args.steps
+    assert int(dec.pos.item()) == pos0 + args.steps, "the step did not advance the cache"
     barrier(world)
     ms = max_over_ranks(ms, world)
+    mean_ctx = pos0 + (args.steps + 1) / 2.0
 
-    # end to end: pinned H2D of the hidden state + step + D2H of the logits, every step
-    h_host = torch.randn((1, HIDDEN)).to(torch.bfloat16).pin_memory()
-    logits_host = torch.empty((1, VOCAB), dtype=torch.bfloat16).pin_memory()
-    for _ in range(2):
-        stack.h.copy_(h_host, non_blocking=True)
+    # end to end: pinned H2D of the token ids, their embedding, the step, D2H of the next ids
+    tok_host = torch.randint(0, LLAMA3_8B.vocab, (B,), dtype=torch.int32).pin_memory()
+    out_host = torch.empty((B,), dtype=torch.int32).pin_memory()
+    dec.fill_prompt_cache(PROMPT)
+
+    def e2e_step():
+        dec.tokens.copy_(tok_host, non_blocking=True)
+        _native.check(_native.lib().tn_llama_embed(P(dec.tokens.data_ptr()), B, P(dec.embed.data_ptr()), HIDDEN,
+                                                   P(dec.h.data_ptr()), cur()))
         g.replay()
-        logits_host.copy_(stack.logits, non_blocking=True)
+        out_host.copy_(dec.tokens, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
     torch.cuda.synchronize()
     barrier(world)
+    dec.fill_prompt_cache(PROMPT)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        stack.h.copy_(h_host, non_blocking=True)
-        g.replay()
-        logits_host.copy_(stack.logits, non_blocking=True)
+        e2e_step()
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
 
-    # dominant kernel: 32 back-to-back gate/up GEMVs over the 32 layers' weights
     for _ in range(3):
         gd.replay()
     torch.cuda.synchronize()
@@ -364,13 +315,13 @@ def run_ours(args, rank, world, local):
     _native.device_status(reset=True)
 
     peak, peak_kind = measured_peaks()
-    algo = stack.dominant_algorithmic_bytes()
+    n, k = 2 * INTER, HIDDEN
+    algo = q4_bytes(n, k) + B * (k + k // 32 * 8) + B * n * 2
     achieved = algo / (dom_us * 1e-6) / 1e9
-    launches = stack.kernels_per_step * args.steps
-
+    step_bytes = dec.weight_bytes + dec.kv_bytes(int(mean_ctx))
     result = {
         "metric": METRIC,
-        "value": world * 1000.0 / ms,
+        "value": world * B * 1000.0 / ms,
         "unit": "tok/s",
         "n_gpus": world,
         "steps": args.steps,
@@ -379,34 +330,35 @@ def run_ours(args, rank, world, local):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "q4_0 x q8_0 -> f32 accumulate (bf16 activations)",
-        "data": "synthetic: random Q4_0 weights (codes U[-8,7], scales f16(|N(0,1)|*0.01)), N(0,1) activations",
-        "config": {"workload": "Llama-3-8B-shaped Q4_0 decode, batch 1: the Q4_0 linears of one token "
-                               "(32 x [qkv 6144x4096, o 4096x4096, gate_up 28672x4096, down 4096x14336] + "
-                               "lm_head 128256x4096), each after the Q8_0 activation quantiser; CUDA graph",
-                   "global_batch": world, "parallelism": f"replicas{world}",
+        "dtype": "bf16 activations; Q4_0 x Q8_0 linears (int dot, f32 scale/accumulate); f32 attention math",
+        "data": "synthetic: random Q4_0 weights (codes U[-8,7], scales f16(|N(0,1)|*0.01)), bf16 norms/embeddings, "
+                "N(0,1) prompt KV cache",
+        "config": {"workload": f"Llama-3-8B-shaped Q4_0 greedy decode step, batch {B}, {PROMPT}-token prompt cache "
+                               "growing one slot per step; one CUDA graph per token",
+                   "model": "Llama-3-8B-shaped (32 layers, 4096 hidden, 32/8 heads, D 128, MLP 14336, vocab 128256)",
+                   "global_batch": world * B, "seq_len": PROMPT, "parallelism": f"replicas{world}",
                    "l2": "inputs larger than L2 (4.22 GB of weights per step)",
-                   "weight_bytes_per_token": stack.weight_bytes,
-                   "hbm_roofline_tok_s_per_gpu": peak * 1e9 / stack.weight_bytes},
-        "roofline": {"bound": "hbm", "kernel": "q4_gemv_q8_kernel (gate_up 28672x4096, M=1)", "achieved": achieved,
+                   "mean_context": mean_ctx, "bytes_per_step": step_bytes,
+                   "hbm_roofline_tok_s_per_gpu": B * peak * 1e9 / step_bytes},
+        "roofline": {"bound": "hbm", "kernel": "q4_gemv_q8_kernel (gate/up 28672x4096)", "achieved": achieved,
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": committed_traffic(), "algorithmic_bytes": algo, "avg_launch_us": dom_us},
-        "step_hbm_frac": (stack.weight_bytes / (ms * 1e-3) / 1e9) / peak,
-        "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 2,
-                "d2h_bytes_per_step": VOCAB * 2},
-        "gpu_launches": launches,
+        "step_hbm_frac": (step_bytes / (ms * 1e-3) / 1e9) / peak,
+        "e2e": {"value": world * B * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": dec.kernels_per_step * args.steps,
         "clocks": clocks.summary(),
-        "counters": _native.counters(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        blobs = {name: stack.layers[0][name].cpu().numpy() for name, _, _ in LAYER_LINEARS}
-        lm = stack.lm_head.cpu().numpy()
+        blobs = {"qkv": dec.layers[0]["qkv"].cpu().numpy(), "o": dec.layers[0]["o"].cpu().numpy(),
+                 "gate_up": dec.layers[0]["gate_up"].cpu().numpy(), "down": dec.layers[0]["down"].cpu().numpy()}
+        lm = dec.lm_head.cpu().numpy()
         th = host_threads()
-        sec = cpu_step_seconds(blobs, lm, th, reps=3)
+        sec = cpu_step_seconds(blobs, lm, th, reps=2)
         result["cpu_baseline"] = {"value": 1.0 / sec, "unit": "tok/s", "cores": th, "kind": "port",
-                                  "sample": "one token: layer 0's four Q4_0 linears run 32 times + lm_head, "
-                                            "oracle/tn_oracle.c restatement of the reference CPU arithmetic, "
-                                            "min of 3"}
+                                  "sample": f"one token at batch 1: layer 0's four Q4_0 linears and SDPA over a "
+                                            f"{PROMPT}-token f32 cache, 32 times, + lm_head; oracle/tn_oracle.c "
+                                            "restatement of the reference CPU arithmetic; min of 2"}
     return result
 
 
@@ -430,7 +382,7 @@ def run_reference(args, rank, world):
     blobs = {name: blob(n, k) for name, n, k in LAYER_LINEARS}
     lm = blob(VOCAB, HIDDEN)
     th = host_threads()
-    for _ in range(args.warmup):
+    for _ in range(min(args.warmup, 1)):
         cpu_step_seconds(blobs, lm, th)
     t0 = time.perf_counter()
     for _ in range(args.steps):
@@ -441,11 +393,12 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q4_0 x q8_0 -> f32 accumulate", "data": "synthetic",
-        "config": {"workload": "Llama-3-8B-shaped Q4_0 decode, batch 1: the Q4_0 linears of one token "
-                               "(layer weights reused per layer on the CPU)", "global_batch": 1,
-                   "parallelism": "host CPU"},
+        "config": {"workload": f"Llama-3-8B-shaped Q4_0 greedy decode step, batch 1, {PROMPT}-token cache: the "
+                               "two hot operators on the host CPU (layer weights reused per layer)",
+                   "global_batch": 1, "seq_len": PROMPT, "parallelism": "host CPU"},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": th, "kind": "port",
-                         "sample": "one token per step: one layer's four Q4_0 linears run 32 times + lm_head"},
+                         "sample": "one token per step: one layer's four Q4_0 linears and SDPA over a "
+                                   f"{PROMPT}-token cache, 32 times, + lm_head"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

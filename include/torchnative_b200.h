@@ -215,6 +215,51 @@ TN_API int tn_sdpa_flash_attention(const void *q, const void *k, const void *v, 
                             int64_t D, const int64_t *q_strides, const int64_t *k_strides,
                             const int64_t *v_strides, int is_causal, double scale, void *stream);
 
+/* Decode-time SDPA against a KV cache whose length lives on the device:
+ * query [B, Hq, 1, D]; k_cache/v_cache [B, Hkv, capacity, D] (any b/h
+ * strides, unit d stride); the first *len_dev + len_add keys are attended
+ * (clamped to capacity). The work is planned for `capacity`, so one CUDA graph
+ * of a decode step stays valid while the cache grows. Non-causal (a single
+ * query row attends every cached key, as transformers calls it at decode).
+ * Same arithmetic as tn_sdpa_flash_attention. */
+TN_API int tn_sdpa_decode_cache(const void *q, const void *k_cache, const void *v_cache, void *out,
+                                float *lse, int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                                int64_t capacity, const int64_t *q_strides, const int64_t *k_strides,
+                                const int64_t *v_strides, const int *len_dev, int64_t len_add,
+                                double scale, void *stream);
+
+/* ------------------------------------------------ decode-step glue (bf16) --
+ * The work between the hot operators in one greedy token of transformers'
+ * LlamaForCausalLM (modeling_llama.py: LlamaRMSNorm, apply_rotary_pos_emb,
+ * LlamaMLP, the residual adds, argmax in generate), each producing what the
+ * next Q4_0 linear reads: planar Q8_0 activations (see tn_q8_0_quantize_planar).
+ * All tensors are bf16 unless stated; rows are contiguous. */
+
+/* h_out = bf16(h + delta) (delta may be NULL; h_out may be NULL or == h);
+ * y = weight * bf16(h32 * rsqrt(mean(h32^2) + eps)); y -> planar Q8_0. H % 32 == 0, H <= 8192. */
+TN_API int tn_llama_add_rmsnorm_q8(const void *h, const void *delta, void *h_out, const void *weight,
+                                   float eps, int64_t rows, int64_t H, int8_t *codes, float *scales,
+                                   float *offsets, void *stream);
+/* act = bf16(bf16(silu(gate)) * up) from rows [gate (I) | up (I)]; act -> planar Q8_0. */
+TN_API int tn_llama_silu_mul_q8(const void *gate_up, int64_t rows, int64_t I, int8_t *codes,
+                                float *scales, float *offsets, void *stream);
+/* Rotary embedding (rotate_half convention, cos/sin rounded to bf16 as
+ * transformers does) of the q and k heads of rows [q (Hq*D) | k (Hkv*D) | v (Hkv*D)]
+ * at position pos = pos_dev ? *pos_dev : pos_host; q -> q_out [B, Hq, D];
+ * rotated k and v -> slot pos of k_cache/v_cache (element strides cache_b_stride,
+ * cache_h_stride, slot stride D). inv_freq: f32 [D/2] on the device. */
+TN_API int tn_llama_rope_append(const void *qkv, const float *inv_freq, const int *pos_dev,
+                                int64_t pos_host, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                                void *q_out, void *k_cache, void *v_cache, int64_t cache_b_stride,
+                                int64_t cache_h_stride, void *stream);
+/* tokens[r] = argmax(logits[r]) (first index of the maximum); h[r] = embed[tokens[r]];
+ * if pos_dev, *pos_dev += 1. */
+TN_API int tn_llama_argmax_embed(const void *logits, int64_t rows, int64_t V, int *tokens,
+                                 const void *embed, int64_t H, void *h, int *pos_dev, void *stream);
+/* h[r] = embed[tokens[r]]. */
+TN_API int tn_llama_embed(const int *tokens, int64_t rows, const void *embed, int64_t H, void *h,
+                          void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,235 @@
+"""The decode-step glue on the GPU against transformers' Llama modules (the
+caller of the two hot operators), and one full decode step of a small
+Q4_0 Llama against a host reference assembled from the same definitions."""
+
+import ctypes
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests import q4_exact
+
+pytestmark = pytest.mark.gpu
+P = ctypes.c_void_p
+
+
+@pytest.fixture(scope="module")
+def N(cuda_device):
+    from torchnative_b200 import _native, build
+
+    build.build()
+    _native.lib()
+    return _native
+
+
+def _stream():
+    return P(torch.cuda.current_stream().cuda_stream)
+
+
+def _planar_to_blob(codes, scales, rows, cols):
+    """Planar Q8_0 (codes, f32 scales) back to GGML Q8_0 bytes, for comparing
+    with the oracle's quantiser."""
+    nb = cols // 32
+    out = np.empty((rows, nb, 34), dtype=np.uint8)
+    out[:, :, 0:2] = scales.reshape(rows, nb, 1).astype(np.float16).view(np.uint8)
+    out[:, :, 2:] = codes.reshape(rows, nb, 32).view(np.uint8)
+    return out.tobytes()
+
+
+def _ref_rmsnorm(h, w, eps):
+    x = h.float()
+    var = x.pow(2).mean(-1, keepdim=True)
+    return w * (x * torch.rsqrt(var + eps)).to(torch.bfloat16)
+
+
+def test_add_rmsnorm_q8_matches_llama_rmsnorm(N, cuda_device):
+    B, H, eps = 3, 4096, 1e-5
+    g = torch.Generator(device=cuda_device).manual_seed(1)
+    h = torch.randn((B, H), device=cuda_device, generator=g).to(torch.bfloat16)
+    d = torch.randn((B, H), device=cuda_device, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, device=cuda_device, generator=g)).to(torch.bfloat16)
+    h_out = torch.empty_like(h)
+    codes = torch.empty((B, H), dtype=torch.int8, device=cuda_device)
+    sc = torch.empty((B, H // 32), device=cuda_device)
+    of = torch.empty((B, H // 32), device=cuda_device)
+    N.check(N.lib().tn_llama_add_rmsnorm_q8(P(h.data_ptr()), P(d.data_ptr()), P(h_out.data_ptr()), P(w.data_ptr()),
+                                            eps, B, H, P(codes.data_ptr()), P(sc.data_ptr()), P(of.data_ptr()),
+                                            _stream()))
+    want_h = (h + d)
+    assert torch.equal(h_out, want_h)
+    y = _ref_rmsnorm(want_h, w, eps)
+    want = np.frombuffer(oracle.q8_0_quantize(y.float().cpu().numpy()), np.uint8).reshape(B, H // 32, 34)
+    got = np.frombuffer(_planar_to_blob(codes.cpu().numpy(), sc.cpu().numpy(), B, H), np.uint8).reshape(B, H // 32, 34)
+    # the norm's f32 reduction order differs from torch's: a block may see one bf16 ulp of difference
+    same = (got == want).all(axis=2).mean()
+    assert same >= 0.97, same
+    deq_g = oracle.q8_0_dequantize(got.tobytes(), B * H)
+    deq_w = oracle.q8_0_dequantize(want.tobytes(), B * H)
+    assert np.max(np.abs(deq_g - deq_w)) <= 0.02 * np.max(np.abs(deq_w))
+    # the offsets are 12582912 + 8 * sum(codes)
+    assert torch.equal(of.cpu(), 12582912.0 + 8.0 * codes.cpu().view(B, H // 32, 32).sum(-1).float())
+
+
+def test_silu_mul_q8_matches_llama_mlp(N, cuda_device):
+    B, I = 2, 14336
+    g = torch.Generator(device=cuda_device).manual_seed(2)
+    gu = torch.randn((B, 2 * I), device=cuda_device, generator=g).to(torch.bfloat16)
+    codes = torch.empty((B, I), dtype=torch.int8, device=cuda_device)
+    sc = torch.empty((B, I // 32), device=cuda_device)
+    of = torch.empty((B, I // 32), device=cuda_device)
+    N.check(N.lib().tn_llama_silu_mul_q8(P(gu.data_ptr()), B, I, P(codes.data_ptr()), P(sc.data_ptr()),
+                                         P(of.data_ptr()), _stream()))
+    act = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    want = oracle.q8_0_quantize(act.float().cpu().numpy())
+    got = _planar_to_blob(codes.cpu().numpy(), sc.cpu().numpy(), B, I)
+    g8 = np.frombuffer(got, np.uint8).reshape(-1, 34)
+    w8 = np.frombuffer(want, np.uint8).reshape(-1, 34)
+    assert (g8 == w8).all(axis=1).mean() >= 0.99
+
+
+def test_rope_append_matches_apply_rotary_pos_emb(N, cuda_device):
+    from transformers.models.llama import modeling_llama as ml
+
+    from torchnative_b200.llama_decode import rope_inv_freq
+
+    B, Hq, Hkv, D, cap, pos, theta = 2, 8, 2, 128, 64, 37, 500000.0
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    qkv = torch.randn((B, (Hq + 2 * Hkv) * D), device=cuda_device, generator=g).to(torch.bfloat16)
+    inv = rope_inv_freq(D, theta).to(cuda_device)
+    q_out = torch.empty((B, Hq, D), device=cuda_device, dtype=torch.bfloat16)
+    kc = torch.zeros((B, Hkv, cap, D), device=cuda_device, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    N.check(N.lib().tn_llama_rope_append(P(qkv.data_ptr()), P(inv.data_ptr()), None, pos, B, Hq, Hkv, D,
+                                         P(q_out.data_ptr()), P(kc.data_ptr()), P(vc.data_ptr()), kc.stride(0),
+                                         kc.stride(1), _stream()))
+    # transformers: freqs = inv_freq x pos (float32), cos/sin -> bf16, q*cos + rotate_half(q)*sin in bf16
+    freqs = inv[None, :] * torch.tensor([[float(pos)]], device=cuda_device)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    q = qkv[:, :Hq * D].view(B, Hq, 1, D)
+    k = qkv[:, Hq * D:(Hq + Hkv) * D].view(B, Hkv, 1, D)
+    v = qkv[:, (Hq + Hkv) * D:].view(B, Hkv, 1, D)
+    qe, ke = ml.apply_rotary_pos_emb(q, k, cos[None], sin[None])
+    assert torch.equal(q_out, qe[:, :, 0])
+    assert torch.equal(kc[:, :, pos], ke[:, :, 0])
+    assert torch.equal(vc[:, :, pos], v[:, :, 0])
+    assert kc[:, :, :pos].abs().sum() == 0 and kc[:, :, pos + 1:].abs().sum() == 0
+
+
+def test_argmax_embed_picks_the_first_maximum(N, cuda_device):
+    B, V, H = 3, 1000, 64
+    logits = torch.randn((B, V), device=cuda_device).to(torch.bfloat16)
+    logits[1, 10] = 50.0
+    logits[1, 700] = 50.0  # tie: the first index wins, as torch.argmax
+    embed = torch.randn((V, H), device=cuda_device).to(torch.bfloat16)
+    tokens = torch.zeros(B, dtype=torch.int32, device=cuda_device)
+    h = torch.empty((B, H), device=cuda_device, dtype=torch.bfloat16)
+    pos = torch.tensor([5], dtype=torch.int32, device=cuda_device)
+    N.check(N.lib().tn_llama_argmax_embed(P(logits.data_ptr()), B, V, P(tokens.data_ptr()), P(embed.data_ptr()), H,
+                                          P(h.data_ptr()), P(pos.data_ptr()), _stream()))
+    want = torch.argmax(logits.float(), dim=-1)
+    assert torch.equal(tokens.long(), want) and int(tokens[1]) == 10
+    assert torch.equal(h, embed[want])
+    assert int(pos.item()) == 6
+
+
+def _host_reference_step(dec, tok, pos):
+    """One decode token from the same weights, assembled on the host: glue in
+    torch bf16 (transformers' definitions), every Q4_0 linear as the exact
+    value of (Q8_0(x), W) rounded to bf16, SDPA in float64. Returns logits (f64)."""
+    from transformers.models.llama import modeling_llama as ml
+
+    s, dev = dec.s, "cpu"
+    bf = torch.bfloat16
+
+    def linear(x_bf, blob, n, k):
+        x = x_bf.float().numpy()
+        xq = oracle.q8_0_quantize(x)
+        exact, _, _ = q4_exact.exact_linear_q4_0(xq, blob.cpu().numpy().tobytes(), x.shape[0], n, k)
+        return torch.from_numpy(exact).to(bf)
+
+    def norm(h, w):
+        return _ref_rmsnorm(h, w.cpu(), s.eps)
+
+    h = dec.embed.cpu()[tok]
+    inv = dec.inv_freq.cpu()
+    freqs = inv[None, :] * torch.tensor([[float(pos)]])
+    emb = torch.cat((freqs, freqs), dim=-1)
+    cos, sin = emb.cos().to(bf), emb.sin().to(bf)
+    B, D, Hq, Hkv = tok.shape[0], s.head_dim, s.heads, s.kv_heads
+    for li, lw in enumerate(dec.layers):
+        x = norm(h, lw["attn_norm"])
+        qkv = linear(x, lw["qkv"], s.qkv, s.hidden)
+        q = qkv[:, :Hq * D].view(B, Hq, 1, D)
+        k = qkv[:, Hq * D:(Hq + Hkv) * D].view(B, Hkv, 1, D)
+        v = qkv[:, (Hq + Hkv) * D:].view(B, Hkv, 1, D)
+        qe, ke = ml.apply_rotary_pos_emb(q, k, cos[None], sin[None])
+        kc = dec.k_cache[li].cpu()[:, :, :pos + 1].clone()
+        vc = dec.v_cache[li].cpu()[:, :, :pos + 1].clone()
+        kc[:, :, pos], vc[:, :, pos] = ke[:, :, 0], v[:, :, 0]
+        kk = kc.double().repeat_interleave(Hq // Hkv, 1)
+        vv = vc.double().repeat_interleave(Hq // Hkv, 1)
+        att = torch.softmax(qe.double() @ kk.transpose(-1, -2) / math.sqrt(D), -1) @ vv
+        o = linear(att.to(bf).reshape(B, Hq * D), lw["o"], s.hidden, Hq * D)
+        h = h + o
+        x = norm(h, lw["mlp_norm"])
+        gu = linear(x, lw["gate_up"], 2 * s.inter, s.hidden)
+        act = torch.nn.functional.silu(gu[:, :s.inter]) * gu[:, s.inter:]
+        h = h + linear(act, lw["down"], s.hidden, s.inter)
+    x = norm(h, dec.final_norm)
+    xq = oracle.q8_0_quantize(x.float().numpy())
+    exact, _, _ = q4_exact.exact_linear_q4_0(xq, dec.lm_head.cpu().numpy().tobytes(), B, s.vocab, s.hidden)
+    return exact
+
+
+def test_one_decode_step_of_a_small_q4_llama_against_the_host_reference(N, cuda_device):
+    from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
+
+    shape = LlamaShape(hidden=512, inter=1024, heads=8, kv_heads=2, head_dim=64, vocab=2048, layers=2,
+                       rope_theta=10000.0)
+    B, prompt = 2, 40
+    dec = Q4LlamaDecoder(shape, batch=B, capacity=64, device=cuda_device, seed=11)
+    dec.fill_prompt_cache(prompt)
+    tok = torch.tensor([5, 1234], dtype=torch.int32)
+    ref = _host_reference_step(dec, tok.long(), prompt)
+    dec.start(tok.to(cuda_device))
+    dec.step()
+    torch.cuda.synchronize()
+    got = dec.logits.float().cpu().numpy().astype(np.float64)
+    scale = np.max(np.abs(ref))
+    assert np.max(np.abs(got - ref)) <= 0.05 * scale, np.max(np.abs(got - ref)) / scale
+    top2 = np.sort(ref, axis=1)[:, -2:]
+    for b in range(B):
+        if top2[b, 1] - top2[b, 0] > 0.05 * scale:  # a clear winner must be the engine's token
+            assert int(dec.tokens[b]) == int(np.argmax(ref[b]))
+    assert int(dec.pos.item()) == prompt + 1
+    N.device_status(reset=True)
+
+
+def test_decode_step_replays_as_one_graph(N, cuda_device):
+    from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
+
+    shape = LlamaShape(hidden=512, inter=1024, heads=8, kv_heads=2, head_dim=64, vocab=2048, layers=2,
+                       rope_theta=10000.0)
+    dec = Q4LlamaDecoder(shape, batch=1, capacity=80, device=cuda_device, seed=12)
+    first = torch.tensor([7], dtype=torch.int32, device=cuda_device)
+    dec.fill_prompt_cache(30)
+    dec.start(first)
+    eager = []
+    for _ in range(4):
+        dec.step()
+        eager.append(int(dec.tokens[0]))
+    dec.fill_prompt_cache(30)
+    dec.start(first)
+    g = dec.capture()
+    dec.fill_prompt_cache(30)
+    dec.start(first)
+    replay = []
+    for _ in range(4):
+        g.replay()
+        replay.append(int(dec.tokens[0]))
+    assert replay == eager
+    assert int(dec.pos.item()) == 34

@@ -96,3 +96,54 @@ extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void 
     p.part_ml = p.part_o + rows * p.splits * p.D;
     return tn::launch_sdpa_decode(p, dtype, stream);
 }
+
+extern "C" int tn_sdpa_decode_cache(const void *q, const void *k_cache, const void *v_cache, void *out, float *lse,
+                                    int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t capacity,
+                                    const int64_t *q_strides, const int64_t *k_strides, const int64_t *v_strides,
+                                    const int *len_dev, int64_t len_add, double scale, void *stream_) {
+    const std::string op = "tn_sdpa_decode_cache";
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    __atomic_fetch_add(&tn::counters().sdpa_calls, 1ull, __ATOMIC_RELAXED);
+    if (dtype != TN_F32 && dtype != TN_BF16 && dtype != TN_F16)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": dtype must be float32, bfloat16 or float16");
+    if (D != 64 && D != 128)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": head dimension must be 64 or 128");
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || capacity <= 0 || !len_dev)
+        return tn::set_error(TN_ERR_SHAPE, op + ": bad shape");
+    if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || !aligned16(k_cache) || !aligned16(v_cache))
+        return tn::set_error(TN_ERR_INVALID, op + ": unit head-dim stride and 16-byte aligned caches required");
+    tn::DeviceFacts f{};
+    int st = tn::device_facts(&f);
+    if (st) return st;
+    tn::SdpaParams p{};
+    p.q = q;
+    p.k = k_cache;
+    p.v = v_cache;
+    p.out = out;
+    p.lse = lse;
+    for (int i = 0; i < 4; ++i) {
+        p.qs[i] = q_strides[i];
+        p.ks[i] = k_strides[i];
+        p.vs[i] = v_strides[i];
+    }
+    p.B = (int)B;
+    p.Hq = (int)Hq;
+    p.Hkv = (int)Hkv;
+    p.L = 1;
+    p.S = (int)capacity;
+    p.D = (int)D;
+    p.rep = (int)(Hq / Hkv);
+    p.mask_dtype = dtype;
+    p.scale = (float)((std::isnan(scale) || scale <= 0.0) ? 1.0 / std::sqrt((double)D) : scale);
+    p.S_dev = len_dev;
+    p.S_add = (int)len_add;
+    p.err = tn::device_error_word();
+    st = tn::plan_sdpa_decode(p, f.sm_count);
+    if (st) return st;
+    void *ws = nullptr;
+    st = tn::workspace(&ws, tn::sdpa_decode_workspace(p), stream, /*slot=*/2);
+    if (st) return st;
+    p.part_o = static_cast<float *>(ws);
+    p.part_ml = p.part_o + (int64_t)p.B * p.Hq * p.splits * p.D;
+    return tn::launch_sdpa_decode(p, dtype, stream);
+}

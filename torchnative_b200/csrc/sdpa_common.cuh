@@ -24,6 +24,8 @@ struct SdpaParams {
     int keys_per_split;
     float *part_o;  // [B*Hq*L][splits][D] f32 unnormalised partial outputs
     float *part_ml; // [B*Hq*L][splits][2]  running max and sum
+    const int *S_dev; // if set: the key count is min(*S_dev + S_add, S) (S is then the cache capacity)
+    int S_add;
     int *err;
 };
 

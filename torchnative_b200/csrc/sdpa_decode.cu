@@ -113,11 +113,14 @@ __global__ void __launch_bounds__(kThreads) sdpa_decode_kernel(const SdpaParams 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int split = blockIdx.x, rg = blockIdx.y % p.row_groups, kvh = blockIdx.y / p.row_groups, b = blockIdx.z;
     const int R = min(p.rows, p.rep * p.L - rg * p.rows);  // query rows of this CTA
-    const int t0 = split * p.keys_per_split, t1 = min(p.S, t0 + p.keys_per_split);
-    const int ntiles = (t1 - t0 + TK - 1) / TK;
 
     pdl_launch_dependents();
     pdl_wait();
+    // The key count may live on the device (a decode loop replayed as one CUDA
+    // graph while the cache grows); splits were planned for the capacity p.S.
+    const int S = p.S_dev ? min(*p.S_dev + p.S_add, p.S) : p.S;
+    const int t0 = split * p.keys_per_split, t1 = min(S, t0 + p.keys_per_split);
+    const int ntiles = t1 > t0 ? (t1 - t0 + TK - 1) / TK : 0;
 
     // ---- queries (widened to f32) and row state
     for (int idx = tid; idx < RMAX * D; idx += kThreads) {

@@ -1,0 +1,219 @@
+"""One greedy decode token of a Llama-shaped model with Q4_0 linears, on the
+device, as a single replayable CUDA graph.
+
+This is the caller the two hot operators sit in (transformers'
+LlamaForCausalLM driven by `generate`, with torchnative's QuantizedLinear in
+every linear): per layer RMSNorm -> q/k/v (one fused Q4_0 linear) -> RoPE and
+KV append -> SDPA against the cache -> o_proj -> residual -> RMSNorm ->
+gate/up (one fused Q4_0 linear) -> SiLU*up -> down_proj -> residual; then the
+final norm, lm_head and argmax. The KV cache is the reference's
+PreallocatedCache layout (torchnative/python/torchnative/kernels/kv_cache.py:
+51-185): one [B, Hkv, capacity, D] buffer per layer, read in place.
+
+Weights are random (synthetic, seeded): Q4_0 blobs built directly in the
+block layout (codes uniform in [-8, 7], scales f16(|N(0,1)| * 0.01)), bf16
+norms and embeddings. The position counter lives on the device, so one
+captured graph serves every step while the cache grows.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as N
+
+P = ctypes.c_void_p
+
+
+@dataclass(frozen=True)
+class LlamaShape:
+    hidden: int
+    inter: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    vocab: int
+    layers: int
+    rope_theta: float
+    eps: float = 1e-5
+
+    @property
+    def qkv(self) -> int:
+        return (self.heads + 2 * self.kv_heads) * self.head_dim
+
+
+LLAMA3_8B = LlamaShape(4096, 14336, 32, 8, 128, 128256, 32, 500000.0)
+LLAMA3_70B = LlamaShape(8192, 28672, 64, 8, 128, 128256, 80, 500000.0)
+SMOLLM2_135M = LlamaShape(576, 1536, 9, 3, 64, 49152, 30, 10000.0)
+
+
+def q4_bytes(n: int, k: int) -> int:
+    return n * k // 32 * 18
+
+
+def random_q4_blob(n: int, k: int, gen: torch.Generator, dev) -> torch.Tensor:
+    nb = k // 32
+    qs = torch.randint(0, 256, (n, nb, 16), dtype=torch.uint8, device=dev, generator=gen)
+    d = (torch.randn((n, nb, 1), device=dev, generator=gen).abs() * 0.01).to(torch.float16).view(torch.uint8)
+    return torch.cat([d, qs], dim=2).reshape(-1).contiguous()
+
+
+def rope_inv_freq(head_dim: int, theta: float) -> torch.Tensor:
+    """transformers' default rotary inv_freq: 1 / theta^(arange(0, D, 2) / D), in float32."""
+    return 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+
+
+class Q4LlamaDecoder:
+    def __init__(self, shape: LlamaShape, batch: int, capacity: int, device, seed: int = 0,
+                 layers: int | None = None):
+        self.s = shape
+        self.B, self.cap = batch, capacity
+        self.dev = torch.device(device)
+        self.n_layers = shape.layers if layers is None else layers
+        s, dev = shape, self.dev
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        bf = torch.bfloat16
+        self.layers = []
+        for _ in range(self.n_layers):
+            self.layers.append({
+                "attn_norm": (1.0 + 0.1 * torch.randn(s.hidden, device=dev, generator=gen)).to(bf),
+                "qkv": random_q4_blob(s.qkv, s.hidden, gen, dev),
+                "o": random_q4_blob(s.hidden, s.heads * s.head_dim, gen, dev),
+                "mlp_norm": (1.0 + 0.1 * torch.randn(s.hidden, device=dev, generator=gen)).to(bf),
+                "gate_up": random_q4_blob(2 * s.inter, s.hidden, gen, dev),
+                "down": random_q4_blob(s.hidden, s.inter, gen, dev),
+            })
+        self.final_norm = (1.0 + 0.1 * torch.randn(s.hidden, device=dev, generator=gen)).to(bf)
+        self.lm_head = random_q4_blob(s.vocab, s.hidden, gen, dev)
+        self.embed = (0.02 * torch.randn((s.vocab, s.hidden), device=dev, generator=gen)).to(bf)
+        self.k_cache = [torch.zeros((batch, s.kv_heads, capacity, s.head_dim), device=dev, dtype=bf)
+                        for _ in range(self.n_layers)]
+        self.v_cache = [torch.zeros_like(self.k_cache[0]) for _ in range(self.n_layers)]
+        self.inv_freq = rope_inv_freq(s.head_dim, s.rope_theta).to(dev)
+        B, H, I = batch, s.hidden, s.inter
+        kmax = max(H, I, s.heads * s.head_dim)
+        self.h = torch.zeros((B, H), device=dev, dtype=bf)
+        self.delta = torch.zeros((B, H), device=dev, dtype=bf)
+        self.codes = torch.zeros((B, kmax), device=dev, dtype=torch.int8)
+        self.scales = torch.zeros((B, kmax // 32), device=dev, dtype=torch.float32)
+        self.offsets = torch.zeros((B, kmax // 32), device=dev, dtype=torch.float32)
+        self.qkv_out = torch.zeros((B, s.qkv), device=dev, dtype=bf)
+        self.q_rot = torch.zeros((B, s.heads, 1, s.head_dim), device=dev, dtype=bf)
+        self.attn = torch.zeros((B, s.heads, 1, s.head_dim), device=dev, dtype=bf)
+        self.gu = torch.zeros((B, 2 * I), device=dev, dtype=bf)
+        self.logits = torch.zeros((B, s.vocab), device=dev, dtype=bf)
+        self.tokens = torch.zeros(B, device=dev, dtype=torch.int32)
+        self.pos = torch.zeros(1, device=dev, dtype=torch.int32)
+        st = lambda t: (ctypes.c_int64 * 4)(*[0 if t.shape[i] == 1 and i < 3 else t.stride(i) for i in range(4)])  # noqa: E731
+        self._qstr = st(self.q_rot)
+        self._kstr = st(self.k_cache[0])
+        self._graph = None
+
+    # ---- bookkeeping
+
+    @property
+    def weight_bytes(self) -> int:
+        s = self.s
+        per_layer = (q4_bytes(s.qkv, s.hidden) + q4_bytes(s.hidden, s.heads * s.head_dim) +
+                     q4_bytes(2 * s.inter, s.hidden) + q4_bytes(s.hidden, s.inter) + 2 * 2 * s.hidden)
+        return per_layer * self.n_layers + q4_bytes(s.vocab, s.hidden) + 2 * s.hidden
+
+    def kv_bytes(self, length: int) -> int:
+        s = self.s
+        return 2 * self.n_layers * self.B * s.kv_heads * length * s.head_dim * 2
+
+    kernels_per_layer = 11
+
+    @property
+    def kernels_per_step(self) -> int:
+        return self.kernels_per_layer * self.n_layers + 3
+
+    def fill_prompt_cache(self, length: int, seed: int = 1) -> None:
+        """The prompt's K/V: synthetic N(0,1) values in slots [0, length), and
+        the position set to `length` (the decode loop continues from there)."""
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(seed)
+        for kc, vc in zip(self.k_cache, self.v_cache):
+            kc[:, :, :length].normal_(generator=g)
+            vc[:, :, :length].normal_(generator=g)
+        self.pos.fill_(length)
+
+    def start(self, tokens: torch.Tensor) -> None:
+        """Embed the first tokens (one per sequence)."""
+        self.tokens.copy_(tokens.to(torch.int32))
+        N.check(N.lib().tn_llama_embed(P(self.tokens.data_ptr()), self.B, P(self.embed.data_ptr()), self.s.hidden,
+                                       P(self.h.data_ptr()), self._stream()))
+
+    # ---- the step
+
+    @staticmethod
+    def _stream():
+        return P(torch.cuda.current_stream().cuda_stream)
+
+    def _linear(self, w, y, n, k, stream):
+        N.check(N.lib().tn_q4_0_linear_q8(P(self.codes.data_ptr()), k, P(self.scales.data_ptr()),
+                                          P(self.offsets.data_ptr()), P(w.data_ptr()), None, P(y.data_ptr()),
+                                          N.TN_BF16, self.B, n, k, N.TN_WEIGHTS_STATIC, stream))
+
+    def _norm(self, delta, weight, stream):
+        N.check(N.lib().tn_llama_add_rmsnorm_q8(P(self.h.data_ptr()), None if delta is None else P(delta.data_ptr()),
+                                                P(self.h.data_ptr()), P(weight.data_ptr()), self.s.eps, self.B,
+                                                self.s.hidden, P(self.codes.data_ptr()), P(self.scales.data_ptr()),
+                                                P(self.offsets.data_ptr()), stream))
+
+    def step(self, stream=None) -> None:
+        """One token for every sequence: reads tokens' embeddings in self.h and
+        the position self.pos; leaves the next tokens in self.tokens, their
+        embeddings in self.h, and self.pos advanced by one."""
+        L, s, B = N.lib(), self.s, self.B
+        stream = stream or self._stream()
+        D, Hq, Hkv = s.head_dim, s.heads, s.kv_heads
+        for li, lw in enumerate(self.layers):
+            self._norm(None if li == 0 else self.delta, lw["attn_norm"], stream)
+            self._linear(lw["qkv"], self.qkv_out, s.qkv, s.hidden, stream)
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            N.check(L.tn_llama_rope_append(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()),
+                                           P(self.pos.data_ptr()), 0, B, Hq, Hkv, D, P(self.q_rot.data_ptr()),
+                                           P(kc.data_ptr()), P(vc.data_ptr()), kc.stride(0), kc.stride(1), stream))
+            N.check(L.tn_sdpa_decode_cache(P(self.q_rot.data_ptr()), P(kc.data_ptr()), P(vc.data_ptr()),
+                                           P(self.attn.data_ptr()), None, N.TN_BF16, B, Hq, Hkv, D, self.cap,
+                                           self._qstr, self._kstr, self._kstr, P(self.pos.data_ptr()), 1,
+                                           1.0 / math.sqrt(D), stream))
+            N.check(L.tn_q8_0_quantize_planar(P(self.attn.data_ptr()), N.TN_BF16, Hq * D, P(self.codes.data_ptr()),
+                                              Hq * D, P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B,
+                                              Hq * D, stream))
+            self._linear(lw["o"], self.delta, s.hidden, Hq * D, stream)
+            self._norm(self.delta, lw["mlp_norm"], stream)
+            self._linear(lw["gate_up"], self.gu, 2 * s.inter, s.hidden, stream)
+            N.check(L.tn_llama_silu_mul_q8(P(self.gu.data_ptr()), B, s.inter, P(self.codes.data_ptr()),
+                                           P(self.scales.data_ptr()), P(self.offsets.data_ptr()), stream))
+            self._linear(lw["down"], self.delta, s.hidden, s.inter, stream)
+        self._norm(self.delta, self.final_norm, stream)
+        self._linear(self.lm_head, self.logits, s.vocab, s.hidden, stream)
+        N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
+                                        P(self.embed.data_ptr()), s.hidden, P(self.h.data_ptr()),
+                                        P(self.pos.data_ptr()), stream))
+
+    def capture(self) -> torch.cuda.CUDAGraph:
+        """One eager step first, on the stream the capture will use (the
+        library's workspaces are per stream, and are sized by that step;
+        nothing may allocate while capturing), then the step captured as a
+        CUDA graph on that stream. The eager step advances the state, so
+        callers re-seed (fill_prompt_cache / start) afterwards."""
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side):
+            self.step()
+        side.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            self.step()
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        self._graph = g
+        self._capture_stream = side
+        return g
