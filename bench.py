@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemv"],
+    ap.add_argument("--case", default=None, choices=["gemv", "sdpa_decode"],
                     help="kernel-level case instead of the decode step: 'gemv' times the decode GEMV alone on the "
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
     ap.add_argument("--rows", type=int, default=1, help="activation rows M for --case gemv")
@@ -254,8 +254,8 @@ def run_ours(args, rank, world, local):
         for lw in dec.layers:
             _native.check(_native.lib().tn_q4_0_linear_q8(
                 P(dec.codes.data_ptr()), HIDDEN, P(dec.scales.data_ptr()), P(dec.offsets.data_ptr()),
-                P(lw["gate_up"].data_ptr()), None, P(dec.gu.data_ptr()), _native.TN_BF16, B, 2 * INTER, HIDDEN,
-                _native.TN_WEIGHTS_STATIC, cur()))
+                P(lw["gate_up"].data_ptr()), None, P(dec.act.data_ptr()), _native.TN_BF16, B, 2 * INTER, HIDDEN,
+                _native.TN_WEIGHTS_STATIC | _native.TN_EPILOGUE_SILU_MUL_PAIRS, cur()))
 
     for _ in range(args.warmup):
         g.replay()
@@ -312,11 +312,23 @@ def run_ours(args, rank, world, local):
     d1.record()
     torch.cuda.synchronize()
     dom_us = d0.elapsed_time(d1) * 1e3 / (reps * LAYERS)
+    # the step's parts, each as 32 back-to-back launches (one per layer)
+    kernel_us = {}
+    for name, kg in dec.kernel_graphs().items():
+        kg.replay()
+        torch.cuda.synchronize()
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record()
+        for _ in range(5):
+            kg.replay()
+        k1.record()
+        torch.cuda.synchronize()
+        kernel_us[name] = round(k0.elapsed_time(k1) * 1e3 / (5 * LAYERS), 2)
     _native.device_status(reset=True)
 
     peak, peak_kind = measured_peaks()
     n, k = 2 * INTER, HIDDEN
-    algo = q4_bytes(n, k) + B * (k + k // 32 * 8) + B * n * 2
+    algo = q4_bytes(n, k) + B * (k + k // 32 * 8) + B * (n // 2) * 2
     achieved = algo / (dom_us * 1e-6) / 1e9
     step_bytes = dec.weight_bytes + dec.kv_bytes(int(mean_ctx))
     result = {
@@ -340,10 +352,12 @@ def run_ours(args, rank, world, local):
                    "l2": "inputs larger than L2 (4.22 GB of weights per step)",
                    "mean_context": mean_ctx, "bytes_per_step": step_bytes,
                    "hbm_roofline_tok_s_per_gpu": B * peak * 1e9 / step_bytes},
-        "roofline": {"bound": "hbm", "kernel": "q4_gemv_q8_kernel (gate/up 28672x4096)", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": "q4_gemv_q8_kernel (gate/up 28672x4096, SiLU*up epilogue)",
+                     "achieved": achieved,
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": committed_traffic(), "algorithmic_bytes": algo, "avg_launch_us": dom_us},
         "step_hbm_frac": (step_bytes / (ms * 1e-3) / 1e9) / peak,
+        "kernel_us_back_to_back": kernel_us,
         "e2e": {"value": world * B * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                 "d2h_bytes_per_step": 4 * B},
         "gpu_launches": dec.kernels_per_step * args.steps,
@@ -408,6 +422,9 @@ def main():
     if args.case == "gemv":
         run_case_gemv(args)
         return
+    if args.case == "sdpa_decode":
+        run_case_sdpa_decode(args)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -424,6 +441,65 @@ def main():
 
         dist.destroy_process_group()
 
+
+
+def run_case_sdpa_decode(args):
+    """Kernel-level timing of the fused decode-step attention
+    (tn_sdpa_decode_step: RoPE + KV append + split-KV SDPA + merge) on the
+    Llama-3-8B shape, 32 layers' caches of PROMPT tokens (~270 MB, beyond L2)
+    rotated, batch --batch. One JSON line: us per launch and the HBM fraction
+    of its K/V bytes."""
+    import ctypes
+    import math
+
+    import torch
+
+    from torchnative_b200 import _native as N, build
+    from torchnative_b200.llama_decode import rope_inv_freq
+
+    build.build()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, Hq, Hkv, D, cap = args.batch, HEADS, KV_HEADS, HEAD_DIM, PROMPT + 64
+    g = torch.Generator(device=dev).manual_seed(3)
+    ks = [torch.randn((B, Hkv, cap, D), device=dev, generator=g).to(torch.bfloat16) for _ in range(LAYERS)]
+    vs = [torch.randn((B, Hkv, cap, D), device=dev, generator=g).to(torch.bfloat16) for _ in range(LAYERS)]
+    qkv = torch.randn((B, (Hq + 2 * Hkv) * D), device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty((B, Hq, D), device=dev, dtype=torch.bfloat16)
+    inv = rope_inv_freq(D, 500000.0).to(dev)
+    pos = torch.tensor([PROMPT], dtype=torch.int32, device=dev)
+    P = ctypes.c_void_p
+    st = (ctypes.c_int64 * 4)(*ks[0].stride())
+    s = lambda: P(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+
+    def launch(li):
+        N.check(N.lib().tn_sdpa_decode_step(P(qkv.data_ptr()), P(inv.data_ptr()), P(ks[li].data_ptr()),
+                                            P(vs[li].data_ptr()), P(out.data_ptr()), None, B, Hq, Hkv, D, cap, st, st,
+                                            P(pos.data_ptr()), 1.0 / math.sqrt(D), s()))
+
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        launch(0)
+    side.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=side):
+        for li in range(LAYERS):
+            launch(li)
+    for _ in range(args.warmup):
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (args.steps * LAYERS)
+    kv = 2 * B * Hkv * (PROMPT + 1) * D * 2
+    peak, kind = measured_peaks()
+    print(json.dumps({"case": "sdpa_decode", "B": B, "S": PROMPT + 1, "us_per_launch": us, "kv_bytes": kv,
+                      "GBps": kv / us / 1e3, "frac": kv / us / 1e3 / peak, "peak_kind": kind}), flush=True)
+    N.device_status(reset=True)
 
 
 def run_case_gemv(args):

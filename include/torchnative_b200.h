@@ -163,9 +163,36 @@ TN_API int tn_q8_0_quantize_planar(const void *x, int x_dtype, int64_t x_row_str
  * kernel may start streaming the weights before the previous kernel in the
  * stream has finished (programmatic dependent launch). 0 = always wait. */
 #define TN_WEIGHTS_STATIC 1
+/* flags: TN_EPILOGUE_SILU_MUL_PAIRS -- the weight's rows come in (gate, up)
+ * pairs (row 2i = gate_i, row 2i+1 = up_i: LlamaMLP's gate_proj and up_proj
+ * interleaved row by row, which a Q4_0 blob allows since rows are whole
+ * blocks); y receives, for each pair, bf16(bf16(silu(gate_i)) * up_i) with
+ * gate_i and up_i first rounded to bf16, i.e. N/2 columns of row stride N/2.
+ * N even, y bf16. */
+#define TN_EPILOGUE_SILU_MUL_PAIRS 2
 TN_API int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, const float *scales,
                              const float *offsets, const void *w_blob, const float *bias, void *y,
                              int y_dtype, int64_t M, int64_t N, int64_t K, int flags, void *stream);
+
+/* The linear with its activation quantisation fused into the GEMV's prologue,
+ * for decode (M <= 4 rows): every CTA builds the same planar Q8_0 tile from
+ * bf16 rows, so the kernel that would otherwise quantise (and the norm or
+ * SiLU kernel before it) disappears from the step. x_mode:
+ *   TN_X_BF16      x [M][K] as is;
+ *   TN_X_RMSNORM   transformers' LlamaRMSNorm of h = bf16(x + delta)
+ *                  (delta may be NULL): norm_weight * bf16(h32 * rsqrt(mean(h32^2) + eps));
+ *                  h is also written to h_out (if not NULL; must not alias x or delta);
+ *   TN_X_SILU_MUL  bf16(bf16(silu(gate)) * up) from rows [gate (K) | up (K)].
+ * Then the Q8_0 quantiser (k_quants.rs:676-706) and the same GEMV as
+ * tn_q4_0_linear_q8. No reference counterpart as one call: the reference runs
+ * these as separate ops in the transformers model around _quantized_linear. */
+#define TN_X_BF16 1
+#define TN_X_RMSNORM 2
+#define TN_X_SILU_MUL 3
+TN_API int tn_q4_0_linear_fused(int x_mode, const void *x, int64_t x_row_stride, const void *delta,
+                                void *h_out, const void *norm_weight, float eps, const void *w_blob,
+                                const float *bias, void *y, int y_dtype, int64_t M, int64_t N,
+                                int64_t K, int flags, void *stream);
 
 /* tn_q4_0_linear without any device allocation. No counterpart in the
  * reference: it exists for hosts that cannot let a library call cudaMalloc
@@ -227,6 +254,18 @@ TN_API int tn_sdpa_decode_cache(const void *q, const void *k_cache, const void *
                                 int64_t capacity, const int64_t *q_strides, const int64_t *k_strides,
                                 const int64_t *v_strides, const int *len_dev, int64_t len_add,
                                 double scale, void *stream);
+
+/* The attention block of one decode token in one launch (bf16): from the
+ * q/k/v projection rows qkv [B][(Hq + 2 Hkv) D] at position pos = *pos_dev,
+ * rotate q and k (as tn_llama_rope_append), append k and v to cache slot pos,
+ * attend keys [0, pos] (as tn_sdpa_decode_cache) and merge the key splits in
+ * the last CTA of each KV head (no separate combine kernel). out: [B, Hq, D].
+ * Hq / Hkv <= 8. Transformers runs these as apply_rotary_pos_emb, the cache
+ * update and sdpa_attention_forward (-> aten.rs:10092 on the reference). */
+TN_API int tn_sdpa_decode_step(const void *qkv, const float *inv_freq, void *k_cache, void *v_cache,
+                               void *out, float *lse, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                               int64_t capacity, const int64_t *k_strides, const int64_t *v_strides,
+                               const int *pos_dev, double scale, void *stream);
 
 /* ------------------------------------------------ decode-step glue (bf16) --
  * The work between the hot operators in one greedy token of transformers'

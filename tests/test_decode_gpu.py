@@ -176,8 +176,8 @@ def _host_reference_step(dec, tok, pos):
         o = linear(att.to(bf).reshape(B, Hq * D), lw["o"], s.hidden, Hq * D)
         h = h + o
         x = norm(h, lw["mlp_norm"])
-        gu = linear(x, lw["gate_up"], 2 * s.inter, s.hidden)
-        act = torch.nn.functional.silu(gu[:, :s.inter]) * gu[:, s.inter:]
+        gu = linear(x, lw["gate_up"], 2 * s.inter, s.hidden)  # rows interleaved: gate_i, up_i
+        act = torch.nn.functional.silu(gu[:, 0::2]) * gu[:, 1::2]
         h = h + linear(act, lw["down"], s.hidden, s.inter)
     x = norm(h, dec.final_norm)
     xq = oracle.q8_0_quantize(x.float().numpy())
@@ -185,13 +185,15 @@ def _host_reference_step(dec, tok, pos):
     return exact
 
 
-def test_one_decode_step_of_a_small_q4_llama_against_the_host_reference(N, cuda_device):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused-5-kernels", "separate-11-kernels"])
+def test_one_decode_step_of_a_small_q4_llama_against_the_host_reference(N, cuda_device, fused):
     from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
 
     shape = LlamaShape(hidden=512, inter=1024, heads=8, kv_heads=2, head_dim=64, vocab=2048, layers=2,
                        rope_theta=10000.0)
     B, prompt = 2, 40
     dec = Q4LlamaDecoder(shape, batch=B, capacity=64, device=cuda_device, seed=11)
+    dec.fused = fused
     dec.fill_prompt_cache(prompt)
     tok = torch.tensor([5, 1234], dtype=torch.int32)
     ref = _host_reference_step(dec, tok.long(), prompt)
@@ -209,12 +211,14 @@ def test_one_decode_step_of_a_small_q4_llama_against_the_host_reference(N, cuda_
     N.device_status(reset=True)
 
 
-def test_decode_step_replays_as_one_graph(N, cuda_device):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused-5-kernels", "separate-11-kernels"])
+def test_decode_step_replays_as_one_graph(N, cuda_device, fused):
     from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
 
     shape = LlamaShape(hidden=512, inter=1024, heads=8, kv_heads=2, head_dim=64, vocab=2048, layers=2,
                        rope_theta=10000.0)
     dec = Q4LlamaDecoder(shape, batch=1, capacity=80, device=cuda_device, seed=12)
+    dec.fused = fused
     first = torch.tensor([7], dtype=torch.int32, device=cuda_device)
     dec.fill_prompt_cache(30)
     dec.start(first)

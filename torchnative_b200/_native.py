@@ -24,6 +24,8 @@ TN_ERR_TIMEOUT = 6
 TN_F32, TN_F16, TN_BF16, TN_F64 = 0, 1, 2, 3
 TN_ACT_Q8_0, TN_ACT_FLOAT = 0, 1
 TN_WEIGHTS_STATIC = 1
+TN_EPILOGUE_SILU_MUL_PAIRS = 2
+TN_X_BF16, TN_X_RMSNORM, TN_X_SILU_MUL = 1, 2, 3
 
 # Every entry point declared in include/torchnative_b200.h, with its ctypes signature.
 _P, _I, _I64, _SZ, _D = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_double
@@ -55,11 +57,14 @@ SIGNATURES = {
     "tn_q4_0_linear": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
     "tn_q8_0_quantize_planar": (_I, [_P, _I, _I64, _P, _I64, _P, _P, _I64, _I64, _P]),
     "tn_q4_0_linear_q8": (_I, [_P, _I64, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
+    "tn_q4_0_linear_fused": (_I, [_I, _P, _I64, _P, _P, _P, ctypes.c_float, _P, _P, _P, _I, _I64, _I64, _I64, _I,
+                                  _P]),
     "tn_q4_0_linear_noalloc": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
     "tn_sdpa_flash_attention": (_I, [_P, _P, _P, _P, _I, _PI64, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64,
                                      _PI64, _PI64, _PI64, _I, _D, _P]),
     "tn_sdpa_decode_cache": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _PI64, _P,
                                   _I64, _D, _P]),
+    "tn_sdpa_decode_step": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _P, _D, _P]),
     "tn_llama_add_rmsnorm_q8": (_I, [_P, _P, _P, _P, ctypes.c_float, _I64, _I64, _P, _P, _P, _P]),
     "tn_llama_silu_mul_q8": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
     "tn_llama_rope_append": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64, _P]),

@@ -55,6 +55,16 @@ struct GemvParams {
     int nslots;
     int flags;
     int *err;
+    // Activation source (x_mode): X_PLANAR reads xq/xd/xc; the others build the
+    // planar Q8_0 tile in shared memory from bf16 rows (M <= 4), every CTA the
+    // same bytes from the same inputs.
+    int x_mode;
+    const __nv_bfloat16 *xb;     // X_BF16: x; X_NORM: h; X_SILU: [gate | up] rows
+    const __nv_bfloat16 *xdelta; // X_NORM: residual delta (or null)
+    __nv_bfloat16 *xh_out;       // X_NORM: h + delta is written here by CTA 0 (never == xb)
+    const __nv_bfloat16 *xw;     // X_NORM: RMSNorm weight
+    float eps;
+    int64_t xb_row_stride;       // elements
 };
 
 // Shared-memory layout (dynamic), as 32-bit shared-window addresses:
@@ -199,6 +209,212 @@ __device__ __forceinline__ void single_dot(const Blk &a, const Blk &bb, int b, c
     }
 }
 
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ int sat_i8r(float v) {
+    if (!(v == v)) return 0;
+    if (v <= -128.0f) return -128;
+    if (v >= 127.0f) return 127;
+    return __float2int_rz(v);
+}
+
+// One Q8_0 block (k_quants.rs:676-706) from 32 values held by one thread,
+// written into the staged planar tile (codes as two 16-byte chunks in the
+// pair-swizzled layout, then the widened scale and the offset constant).
+__device__ __forceinline__ void q8_block_to_smem(const float (&v)[32], int m, int b, const Smem &s,
+                                                 const GemvParams &p) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[8];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int q = sat_i8r(roundf(__fmul_rn(v[4 * k + e], id)));
+            sum += q;
+            word |= (uint32_t)(q & 0xff) << (8 * e);
+        }
+        w[k] = word;
+    }
+    const int pair = b >> 1, c = (b & 1) * 2;
+    const uint32_t row = s.xs + (uint32_t)m * p.nbp * 32;
+    sts128(row + xchunk(pair, c), make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]));
+    sts128(row + xchunk(pair, c + 1), make_int4((int)w[4], (int)w[5], (int)w[6], (int)w[7]));
+    stsf(s.xds + (uint32_t)(m * p.nbp + b) * 4, __half2float(__float2half_rn(d)));
+    stsf(s.xcs + (uint32_t)(m * p.nbp + b) * 4, 12582912.0f + 8.0f * (float)sum);
+}
+
+// 8 consecutive bf16 values (one 16-byte load; rows are 16-byte aligned) as f32.
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16 *src, float *v) {
+    const int4 r = __ldg(reinterpret_cast<const int4 *>(src));
+    const uint32_t u[4] = {(uint32_t)r.x, (uint32_t)r.y, (uint32_t)r.z, (uint32_t)r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(u[i] << 16);
+        v[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    }
+}
+
+enum : int { X_PLANAR = 0, X_BF16 = 1, X_NORM = 2, X_SILU = 3 };
+constexpr int kMaxFusedRows = 4;
+
+// Build the planar Q8_0 tile from bf16 rows, one 32-element block per thread:
+// x itself (X_BF16), transformers' RMSNorm of h + delta (X_NORM: w * bf16(x *
+// rsqrt(mean(x^2) + eps)), x = bf16(h + delta)), or bf16(bf16(silu(g)) * u)
+// (X_SILU). Consumer threads only; `red` is kMaxFusedRows * kConsumerWarps
+// floats of shared scratch.
+__device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p, int tid, int warp, int lane,
+                                              float *red) {
+    const int K = p.nb * 32, nthr = kConsumerWarps * 32;
+    if (p.x_mode == X_NORM && p.M == 1 && p.nb <= nthr) {
+        // The decode case: one row, at most one block per thread. Every load is
+        // issued before the first use and the block stays in registers across
+        // the CTA-wide reduction, so the prologue costs one L2 round trip.
+        const int b = tid;
+        float h[32];
+        uint32_t wp[16];
+        float ss = 0.0f;
+        if (b < p.nb) {
+            int4 xr[4], dr[4], wr[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                xr[c] = __ldg(reinterpret_cast<const int4 *>(p.xb + b * 32) + c);
+                dr[c] = p.xdelta ? __ldg(reinterpret_cast<const int4 *>(p.xdelta + b * 32) + c) : make_int4(0, 0, 0, 0);
+                wr[c] = __ldg(reinterpret_cast<const int4 *>(p.xw + b * 32) + c);
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t xu[4] = {(uint32_t)xr[c].x, (uint32_t)xr[c].y, (uint32_t)xr[c].z, (uint32_t)xr[c].w};
+                const uint32_t du[4] = {(uint32_t)dr[c].x, (uint32_t)dr[c].y, (uint32_t)dr[c].z, (uint32_t)dr[c].w};
+                wp[4 * c + 0] = (uint32_t)wr[c].x;
+                wp[4 * c + 1] = (uint32_t)wr[c].y;
+                wp[4 * c + 2] = (uint32_t)wr[c].z;
+                wp[4 * c + 3] = (uint32_t)wr[c].w;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float lo = __uint_as_float(xu[i] << 16), hi = __uint_as_float(xu[i] & 0xffff0000u);
+                    if (p.xdelta) {
+                        lo = bfr(lo + __uint_as_float(du[i] << 16));
+                        hi = bfr(hi + __uint_as_float(du[i] & 0xffff0000u));
+                    }
+                    h[8 * c + 2 * i] = lo;
+                    h[8 * c + 2 * i + 1] = hi;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ss = fmaf(h[j], h[j], ss);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if (lane == 0) red[warp] = ss;
+        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) t += red[w];
+        const float r = rsqrtf(t / (float)K + p.eps);
+        if (b < p.nb) {
+            if (p.xh_out && blockIdx.x == 0) {
+                uint32_t o[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    o[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(h[2 * i])) |
+                           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(h[2 * i + 1])) << 16);
+                int4 *dst = reinterpret_cast<int4 *>(p.xh_out + b * 32);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    dst[c] = make_int4((int)o[4 * c], (int)o[4 * c + 1], (int)o[4 * c + 2], (int)o[4 * c + 3]);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                h[2 * i] = bfr(__uint_as_float(wp[i] << 16) * bfr(h[2 * i] * r));
+                h[2 * i + 1] = bfr(__uint_as_float(wp[i] & 0xffff0000u) * bfr(h[2 * i + 1] * r));
+            }
+            q8_block_to_smem(h, 0, b, s, p);
+        } else if (b < p.nbp) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) h[j] = 0.0f;
+            q8_block_to_smem(h, 0, b, s, p);
+        }
+        return;
+    }
+    float rinv[kMaxFusedRows] = {1.0f, 1.0f, 1.0f, 1.0f};
+    if (p.x_mode == X_NORM) {
+        float ss[kMaxFusedRows] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int m = 0; m < kMaxFusedRows; ++m) {
+            if (m < p.M) {
+                for (int b = tid; b < p.nb; b += nthr) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        float x[8], dl[8];
+                        load8_bf16(p.xb + m * p.xb_row_stride + b * 32 + 8 * c, x);
+                        if (p.xdelta) load8_bf16(p.xdelta + m * p.xb_row_stride + b * 32 + 8 * c, dl);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float h = p.xdelta ? bfr(x[j] + dl[j]) : x[j];
+                            ss[m] = fmaf(h, h, ss[m]);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < kMaxFusedRows; ++m) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], off);
+            if (lane == 0) red[m * kConsumerWarps + warp] = ss[m];
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+#pragma unroll
+        for (int m = 0; m < kMaxFusedRows; ++m) {
+            float t = 0.0f;
+            for (int w = 0; w < kConsumerWarps; ++w) t += red[m * kConsumerWarps + w];
+            rinv[m] = rsqrtf(t / (float)K + p.eps);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < kMaxFusedRows; ++m) {
+        if (m >= p.M) continue;
+        for (int b = tid; b < p.nbp; b += nthr) {
+            float v[32];
+            if (b >= p.nb) {  // padding block of an odd block count
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+            } else {
+                const __nv_bfloat16 *xr = p.xb + m * p.xb_row_stride + b * 32;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float *vc = v + 8 * c;
+                    load8_bf16(xr + 8 * c, vc);
+                    if (p.x_mode == X_NORM) {
+                        float dl[8], w[8];
+                        if (p.xdelta) load8_bf16(p.xdelta + m * p.xb_row_stride + b * 32 + 8 * c, dl);
+                        load8_bf16(p.xw + b * 32 + 8 * c, w);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float h = p.xdelta ? bfr(vc[j] + dl[j]) : vc[j];
+                            if (p.xh_out && blockIdx.x == 0)
+                                p.xh_out[m * p.xb_row_stride + b * 32 + 8 * c + j] = __float2bfloat16_rn(h);
+                            vc[j] = bfr(w[j] * bfr(h * rinv[m]));
+                        }
+                    } else if (p.x_mode == X_SILU) {  // rows are [gate (K) | up (K)]
+                        float u[8];
+                        load8_bf16(xr + K + 8 * c, u);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) vc[j] = bfr(bfr(vc[j] / (1.0f + expf(-vc[j]))) * u[j]);
+                    }
+                }
+            }
+            q8_block_to_smem(v, m, b, s, p);
+        }
+    }
+}
+
 // Copy this CTA's activations into shared memory (all consumer threads).
 __device__ __forceinline__ void stage_x(const Smem &s, const GemvParams &p, int tid, int nthr) {
     const int chunks_per_row = p.nbp * 2;  // 16-byte chunks
@@ -245,6 +461,19 @@ __device__ __forceinline__ void finish_rows(float (&acc)[2][MT], const GemvParam
     for (int off = 16 >> LOGV; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
     const int idx = lane >> (5 - LOGV);
     const int r = idx / MT, m = idx % MT;
+    if (p.flags & TN_EPILOGUE_SILU_MUL_PAIRS) {
+        // Rows n0 (gate) and n0 + 1 (up) of an interleaved gate/up weight: the
+        // lanes holding up's totals sit 16 above gate's. Each projection is
+        // rounded to bf16 as nn.Linear's output would be, then LlamaMLP's
+        // act = bf16(bf16(silu(gate)) * up) goes to column n0 / 2.
+        if (p.bias) t = t + __ldg(p.bias + n0 + r);
+        const float u = __shfl_down_sync(0xffffffffu, t, 16);
+        if ((lane & ((1 << (5 - LOGV)) - 1)) == 0 && r == 0 && m < p.M) {
+            const float g = bfr(t), up = bfr(u);
+            store_out(p.y, p.y_dtype, m * p.y_row_stride + (n0 >> 1), bfr(bfr(g / (1.0f + expf(-g))) * up));
+        }
+        return;
+    }
     if ((lane & ((1 << (5 - LOGV)) - 1)) == 0 && m < p.M && (r == 0 || has_b)) {
         const int64_t n = n0 + r;
         if (p.bias) t = t + __ldg(p.bias + n);
@@ -304,7 +533,9 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
     const Smem s = carve(smem_raw, p);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t G = gridDim.x, c = blockIdx.x;
-    const int64_t r0 = c * p.N / G, r1 = (c + 1) * p.N / G;
+    // (gate, up) row pairs never straddle two CTAs: partition in pairs then
+    const int64_t gran = (p.flags & TN_EPILOGUE_SILU_MUL_PAIRS) ? 2 : 1;
+    const int64_t r0 = c * (p.N / gran) / G * gran, r1 = (c + 1) * (p.N / gran) / G * gran;
     const int nrows = (int)(r1 - r0);
     // Chunks of R = 2 * wpc consecutive rows; chunk j lives in slot j % nslots
     // and is consumed by warp group j % groups (wpc warps, two rows each).
@@ -362,7 +593,12 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
 
     // ---------------- consumers
     pdl_wait();  // the activations may come from the previous kernel in the stream
-    stage_x(s, p, threadIdx.x, kConsumerWarps * 32);
+    if (p.x_mode == X_PLANAR) {
+        stage_x(s, p, threadIdx.x, kConsumerWarps * 32);
+    } else {
+        __shared__ float red[kMaxFusedRows * kConsumerWarps];
+        stage_x_fused(s, p, threadIdx.x, warp, lane, red);
+    }
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
     const int group = warp / wpc, gw = warp % wpc;
@@ -475,34 +711,24 @@ int q4_gemv_max_rows(int64_t K) {
     const int nb = (int)(K / 32), nbp = (nb + 1) & ~1, rowbytes = 18 * nb;
     const bool staged = (K % 256 == 0);
     for (int mt = 16; mt >= 1; mt >>= 1)
-        if (plan_slots(mt, nbp, rowbytes, staged, (size_t)f.smem_optin, 128 * 1024).ok) return mt;
+        if (plan_slots(mt, nbp, rowbytes, staged, (size_t)f.smem_optin - 1024, 128 * 1024).ok) return mt;
     return 0;
 }
 
-int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
-                      const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
-                      int flags, cudaStream_t stream) {
+namespace {
+
+int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream_t stream) {
     const char *op = "torch._C._quantized_linear";
     DeviceFacts f{};
     int st = device_facts(&f);
     if (st) return st;
-    GemvParams p{};
-    p.w = w;
-    p.xq = xq;
-    p.xd = xd;
-    p.xc = xc;
-    p.bias = bias;
-    p.y = y;
-    p.xq_row_stride = xq_row_stride;
-    p.y_row_stride = y_row_stride;
     p.N = N;
-    p.y_dtype = y_dtype;
     p.M = M;
     p.nb = (int)(K / 32);
     p.nbp = (p.nb + 1) & ~1;
     p.rowbytes = 18 * p.nb;
     p.err = device_error_word();
-    const bool staged = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(w) & 15) == 0);
+    const bool staged = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(p.w) & 15) == 0);
     // Two CTAs per SM for M <= 2 (each with ~64 KB in flight): the next
     // kernel's CTAs can then start streaming while this one's last CTAs drain.
     Plan plan{false, 1, 0, 0};
@@ -511,15 +737,15 @@ int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const
         plan = plan_slots(M, p.nbp, p.rowbytes, staged, kTwoCtaBudget, 64 * 1024);
         if (plan.ok) ctas_per_sm = 2;
     }
-    if (!plan.ok) plan = plan_slots(M, p.nbp, p.rowbytes, staged, (size_t)f.smem_optin, 128 * 1024);
+    if (!plan.ok) plan = plan_slots(M, p.nbp, p.rowbytes, staged, (size_t)f.smem_optin - 1024, 128 * 1024);
     if (!plan.ok)
         return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: activation tile too large for "
                                                                    "shared memory");
     p.wpc = plan.wpc;
     p.slot_bytes = plan.slot_bytes;
     p.nslots = plan.nslots;
-    const size_t smem = smem_bytes(M, p.nbp, plan.nslots, plan.slot_bytes);
     p.flags = flags;
+    const size_t smem = smem_bytes(M, p.nbp, plan.nslots, plan.slot_bytes);
     int64_t grid = (int64_t)f.sm_count * ctas_per_sm;
     const int64_t by_rows = (N + 2 * plan.wpc - 1) / (2 * plan.wpc);
     if (by_rows < grid) grid = by_rows > 0 ? by_rows : 1;
@@ -534,6 +760,44 @@ int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const
     TN_GEMV_CASE(16)
 #undef TN_GEMV_CASE
     return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: GEMV called with M > 16");
+}
+
+}  // namespace
+
+int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
+                      const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
+                      int flags, cudaStream_t stream) {
+    GemvParams p{};
+    p.w = w;
+    p.xq = xq;
+    p.xd = xd;
+    p.xc = xc;
+    p.bias = bias;
+    p.y = y;
+    p.xq_row_stride = xq_row_stride;
+    p.y_row_stride = y_row_stride;
+    p.y_dtype = y_dtype;
+    p.x_mode = X_PLANAR;
+    return launch_gemv(p, M, N, K, flags, stream);
+}
+
+int launch_q4_gemv_fused(int x_mode, const void *xb, int64_t xb_row_stride, const void *xdelta, void *xh_out,
+                         const void *norm_w, float eps, const uint8_t *w, const float *bias, void *y, int y_dtype,
+                         int64_t y_row_stride, int M, int64_t N, int64_t K, int flags, cudaStream_t stream) {
+    GemvParams p{};
+    p.w = w;
+    p.bias = bias;
+    p.y = y;
+    p.y_row_stride = y_row_stride;
+    p.y_dtype = y_dtype;
+    p.x_mode = x_mode;
+    p.xb = static_cast<const __nv_bfloat16 *>(xb);
+    p.xdelta = static_cast<const __nv_bfloat16 *>(xdelta);
+    p.xh_out = static_cast<__nv_bfloat16 *>(xh_out);
+    p.xw = static_cast<const __nv_bfloat16 *>(norm_w);
+    p.eps = eps;
+    p.xb_row_stride = xb_row_stride;
+    return launch_gemv(p, M, N, K, flags, stream);
 }
 
 }  // namespace tn

@@ -104,14 +104,53 @@ extern "C" int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, 
     if (chunk <= 0)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": in_features " + std::to_string(K) +
                                                          " is too large for the decode kernel's shared memory");
+    const bool pairs = (flags & TN_EPILOGUE_SILU_MUL_PAIRS) != 0;
+    if (pairs && (N % 2 != 0 || y_dtype != TN_BF16))
+        return tn::set_error(TN_ERR_INVALID, op + ": the SiLU*up pair epilogue needs an even N and a bf16 output");
+    const int64_t ycols = pairs ? N / 2 : N;
     const size_t ysz = tn_dtype_size(y_dtype);
     for (int64_t m0 = 0; m0 < M; m0 += chunk) {
         const int mc = (int)((M - m0) < chunk ? (M - m0) : chunk);
         int st = tn::launch_q4_gemv_q8(static_cast<const uint8_t *>(w_blob), codes + m0 * codes_row_stride,
                                        scales + m0 * nb, offsets + m0 * nb, codes_row_stride, bias,
-                                       static_cast<uint8_t *>(y) + (size_t)m0 * N * ysz, y_dtype, N, mc, N, K, flags,
-                                       stream);
+                                       static_cast<uint8_t *>(y) + (size_t)m0 * ycols * ysz, y_dtype, ycols, mc, N,
+                                       K, flags, stream);
         if (st) return st;
     }
     return TN_OK;
+}
+
+extern "C" int tn_q4_0_linear_fused(int x_mode, const void *x, int64_t x_row_stride, const void *delta, void *h_out,
+                                    const void *norm_weight, float eps, const void *w_blob, const float *bias,
+                                    void *y, int y_dtype, int64_t M, int64_t N, int64_t K, int flags, void *stream) {
+    const std::string op = "tn_q4_0_linear_fused";
+    __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
+    if (x_mode != TN_X_BF16 && x_mode != TN_X_RMSNORM && x_mode != TN_X_SILU_MUL)
+        return tn::set_error(TN_ERR_INVALID, op + ": unknown x_mode " + std::to_string(x_mode));
+    if (y_dtype != TN_F32 && y_dtype != TN_BF16 && y_dtype != TN_F16)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": unsupported output dtype " + tn_dtype_name(y_dtype));
+    if (M < 0 || N < 0 || K <= 0 || K % 32 != 0)
+        return tn::set_error(TN_ERR_SHAPE, op + ": K must be a positive multiple of 32");
+    if (M > 4)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": at most 4 activation rows (quantise separately and call "
+                                                          "tn_q4_0_linear_q8 for more)");
+    if (M == 0 || N == 0) return TN_OK;
+    if (!x || !w_blob || !y || (x_mode == TN_X_RMSNORM && !norm_weight))
+        return tn::set_error(TN_ERR_INVALID, op + ": null device pointer");
+    if (x_mode == TN_X_RMSNORM && h_out && (h_out == x || h_out == delta))
+        return tn::set_error(TN_ERR_INVALID, op + ": h_out must not alias the inputs (every CTA reads them)");
+    if (x_row_stride < (x_mode == TN_X_SILU_MUL ? 2 * K : K))
+        return tn::set_error(TN_ERR_INVALID, op + ": row stride too small");
+    if ((reinterpret_cast<uintptr_t>(w_blob) & 1) != 0)
+        return tn::set_error(TN_ERR_INVALID, op + ": the q4_0 blob must be at least 2-byte aligned");
+    const uintptr_t a = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(delta) |
+                        reinterpret_cast<uintptr_t>(norm_weight);
+    if ((a & 15) != 0 || (x_row_stride * 2) % 16 != 0)
+        return tn::set_error(TN_ERR_INVALID, op + ": bf16 rows must be 16-byte aligned");
+    const bool pairs = (flags & TN_EPILOGUE_SILU_MUL_PAIRS) != 0;
+    if (pairs && (N % 2 != 0 || y_dtype != TN_BF16))
+        return tn::set_error(TN_ERR_INVALID, op + ": the SiLU*up pair epilogue needs an even N and a bf16 output");
+    return tn::launch_q4_gemv_fused(x_mode, x, x_row_stride, delta, h_out, norm_weight, eps,
+                                    static_cast<const uint8_t *>(w_blob), bias, y, y_dtype, pairs ? N / 2 : N, (int)M,
+                                    N, K, flags, static_cast<cudaStream_t>(stream));
 }

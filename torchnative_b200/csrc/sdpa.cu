@@ -147,3 +147,62 @@ extern "C" int tn_sdpa_decode_cache(const void *q, const void *k_cache, const vo
     p.part_ml = p.part_o + (int64_t)p.B * p.Hq * p.splits * p.D;
     return tn::launch_sdpa_decode(p, dtype, stream);
 }
+
+extern "C" int tn_sdpa_decode_step(const void *qkv, const float *inv_freq, void *k_cache, void *v_cache, void *out,
+                                   float *lse, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t capacity,
+                                   const int64_t *k_strides, const int64_t *v_strides, const int *pos_dev,
+                                   double scale, void *stream_) {
+    const std::string op = "tn_sdpa_decode_step";
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    __atomic_fetch_add(&tn::counters().sdpa_calls, 1ull, __ATOMIC_RELAXED);
+    if (D != 64 && D != 128)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": head dimension must be 64 or 128");
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || Hq / Hkv > 8 || capacity <= 0 || B > 65535)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": needs Hq % Hkv == 0 and at most 8 query heads per KV head");
+    if (!qkv || !inv_freq || !k_cache || !v_cache || !out || !pos_dev || !k_strides || !v_strides)
+        return tn::set_error(TN_ERR_INVALID, op + ": null pointer");
+    if (k_strides[3] != 1 || v_strides[3] != 1 || !aligned16(k_cache) || !aligned16(v_cache))
+        return tn::set_error(TN_ERR_INVALID, op + ": unit head-dim stride and 16-byte aligned caches required");
+    for (int i = 0; i < 3; ++i)
+        if ((k_strides[i] * 2) % 16 != 0 || (v_strides[i] * 2) % 16 != 0)
+            return tn::set_error(TN_ERR_INVALID, op + ": cache strides must be multiples of 16 bytes");
+    tn::DeviceFacts f{};
+    int st = tn::device_facts(&f);
+    if (st) return st;
+    tn::SdpaParams p{};
+    p.k = k_cache;
+    p.v = v_cache;
+    p.out = out;
+    p.lse = lse;
+    for (int i = 0; i < 4; ++i) {
+        p.ks[i] = k_strides[i];
+        p.vs[i] = v_strides[i];
+    }
+    p.B = (int)B;
+    p.Hq = (int)Hq;
+    p.Hkv = (int)Hkv;
+    p.L = 1;
+    p.S = (int)capacity;
+    p.D = (int)D;
+    p.rep = (int)(Hq / Hkv);
+    p.mask_dtype = TN_BF16;
+    p.scale = (float)((std::isnan(scale) || scale <= 0.0) ? 1.0 / std::sqrt((double)D) : scale);
+    p.S_dev = pos_dev;
+    p.S_add = 1;
+    p.qkv = static_cast<const __nv_bfloat16 *>(qkv);
+    p.inv_freq = inv_freq;
+    p.err = tn::device_error_word();
+    st = tn::plan_sdpa_decode(p, f.sm_count);
+    if (st) return st;
+    if (p.row_groups != 1) return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": internal: more than one row group");
+    void *ws = nullptr;
+    st = tn::workspace(&ws, tn::sdpa_decode_workspace(p), stream, /*slot=*/2);
+    if (st) return st;
+    p.part_o = static_cast<float *>(ws);
+    p.part_ml = p.part_o + (int64_t)p.B * p.Hq * p.splits * p.D;
+    void *cnt = nullptr;
+    st = tn::workspace_zeroed(&cnt, (size_t)p.B * p.Hkv * sizeof(int) + 256, stream, /*slot=*/3);
+    if (st) return st;
+    p.counters = static_cast<int *>(cnt);
+    return tn::launch_sdpa_decode(p, TN_BF16, stream);
+}

@@ -26,6 +26,15 @@ struct SdpaParams {
     float *part_ml; // [B*Hq*L][splits][2]  running max and sum
     const int *S_dev; // if set: the key count is min(*S_dev + S_add, S) (S is then the cache capacity)
     int S_add;
+    // Fused decode step (bf16, L = 1, one row group): q and the new k, v come
+    // from the q/k/v projection rows [B][(Hq + 2 Hkv) D]; q and k get the
+    // rotary embedding at position S - 1 (inv_freq [D/2] f32) and k, v are
+    // written to cache slot S - 1 before any key tile is read.
+    const __nv_bfloat16 *qkv;
+    const float *inv_freq;
+    // If set, the last CTA of each (b, kv head) merges the splits itself
+    // (counters start at zero and are left at zero).
+    int *counters;
     int *err;
 };
 

@@ -65,6 +65,8 @@ struct Elem<__half> {
     }
 };
 
+__device__ __forceinline__ float bfr16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
@@ -99,6 +101,83 @@ struct Layout {
 // line and the eight lanes of a quarter-warp hit eight different bank groups.
 __device__ __forceinline__ int kswz(int j, int c) { return c ^ ((j & 1) << 2); }
 
+// After a CTA wrote its split's partial: the last CTA of its (b, kv head, row
+// group) to finish merges all splits of these rows, in split order:
+// M = max m_s, out = sum e^(m_s - M) o_s / sum e^(m_s - M) l_s, lse = M + log(den).
+// `scratch` is shared memory for 2 * RMAX * splits + RMAX floats.
+template <typename T, int D>
+__device__ __forceinline__ void merge_if_last(const SdpaParams &p, int b, int kvh, int rg, int R, int tid,
+                                              float *scratch) {
+
+    // ---- the last split to finish merges all splits of these rows (in split
+    // order: M = max m_s, out = sum e^(m_s - M) o_s / sum e^(m_s - M) l_s)
+    __shared__ int last;
+    __threadfence();
+    __syncthreads();
+    int *counter = p.counters + ((int64_t)b * p.Hkv + kvh) * p.row_groups + rg;
+    if (tid == 0) last = (atomicAdd(counter, 1) == p.splits - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // Merge weights first (every split's (m, l) of every row, loaded in
+    // parallel into the drained ring), then the weighted sum of the partial
+    // outputs, four dimensions per thread.
+    float *wsm = scratch;           // [R][splits] m_s, then weights e^(m_s - M)
+    float *lsp = wsm + RMAX * p.splits;                       // [R][splits] l_s
+    float *lsm = lsp + RMAX * p.splits;                       // [R] sum of weighted l_s
+    for (int idx = tid; idx < R * p.splits; idx += kThreads) {
+        const int r = idx / p.splits, sp = idx % p.splits;
+        const int64_t row = ((int64_t)b * p.Hq + kvh * p.rep + r) * p.L;
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p.part_ml + (row * p.splits + sp) * 2));
+        wsm[idx] = ml.x;
+        lsp[idx] = ml.y;
+    }
+    __syncthreads();
+    if (tid < R) {
+        const int64_t row = ((int64_t)b * p.Hq + kvh * p.rep + tid) * p.L;
+        float M = -INFINITY;
+        for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, wsm[tid * p.splits + sp]);
+        float den = 0.0f;
+        for (int sp = 0; sp < p.splits; ++sp) {
+            const float m = wsm[tid * p.splits + sp];
+            const float w = (m == -INFINITY) ? 0.0f : expf(m - M);
+            wsm[tid * p.splits + sp] = w;
+            den = fmaf(w, lsp[tid * p.splits + sp], den);
+        }
+        lsm[tid] = den;
+        if (p.lse) p.lse[row] = logf(den) + M;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < R * (D / 4); idx += kThreads) {
+        const int r = idx / (D / 4), d4 = idx % (D / 4);
+        const int64_t row = ((int64_t)b * p.Hq + kvh * p.rep + r) * p.L;
+        const float4 *po = reinterpret_cast<const float4 *>(p.part_o + row * p.splits * D) + d4;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+        for (int sp = 0; sp < p.splits; ++sp) {
+            const float w = wsm[r * p.splits + sp];
+            const float4 o = __ldcg(po + (int64_t)sp * (D / 4));
+            acc.x = fmaf(w, o.x, acc.x);
+            acc.y = fmaf(w, o.y, acc.y);
+            acc.z = fmaf(w, o.z, acc.z);
+            acc.w = fmaf(w, o.w, acc.w);
+        }
+        const float inv = 1.0f / lsm[r];
+        const float v4[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int64_t oi = row * D + d4 * 4 + e;
+            if (std::is_same<T, float>::value)
+                static_cast<float *>(p.out)[oi] = v4[e];
+            else if (std::is_same<T, __nv_bfloat16>::value)
+                static_cast<__nv_bfloat16 *>(p.out)[oi] = __float2bfloat16_rn(v4[e]);
+            else
+                static_cast<__half *>(p.out)[oi] = __float2half_rn(v4[e]);
+        }
+    }
+    if (tid == 0) *counter = 0;
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads) sdpa_decode_kernel(const SdpaParams p) {
     using LY = Layout<T, D>;
@@ -123,14 +202,57 @@ __global__ void __launch_bounds__(kThreads) sdpa_decode_kernel(const SdpaParams 
     const int ntiles = t1 > t0 ? (t1 - t0 + TK - 1) / TK : 0;
 
     // ---- queries (widened to f32) and row state
-    for (int idx = tid; idx < RMAX * D; idx += kThreads) {
-        const int r = idx / D, d = idx % D;
-        float v = 0.0f;
-        if (r < R) {
-            const int gr = rg * p.rows + r, l = gr / p.rep, hq = kvh * p.rep + gr % p.rep;
-            v = to_f32<T>(static_cast<const T *>(p.q)[b * p.qs[0] + hq * p.qs[1] + l * p.qs[2] + d]);
+    if (p.qkv) {
+        // Fused step: rotate q (rotate_half convention, cos/sin rounded to bf16
+        // as transformers does) from the projection row; the CTA whose key
+        // range holds slot S - 1 also appends the rotated k and v there.
+        const int pos = S - 1, half = D / 2, W = (p.Hq + 2 * p.Hkv) * D;
+        const __nv_bfloat16 *row = p.qkv + (int64_t)b * W;
+        // cos/sin of inv_freq[i] * pos, rounded to bf16, once per CTA (in the
+        // score scratch, which is not used before the first tile)
+        float *cs = ssm, *sn_t = ssm + half;
+        for (int i = tid; i < half; i += kThreads) {
+            const float f = p.inv_freq[i] * (float)pos;
+            cs[i] = bfr16(cosf(f));
+            sn_t[i] = bfr16(sinf(f));
         }
-        qsm[idx] = v;
+        __syncthreads();
+        for (int idx = tid; idx < RMAX * D; idx += kThreads) {
+            const int r = idx / D, d = idx % D;
+            float v = 0.0f;
+            if (r < R) {
+                const int hq = kvh * p.rep + r;
+                const int i = d % half;
+                const float c = cs[i], sn = sn_t[i];
+                const float x1 = __bfloat162float(row[hq * D + i]), x2 = __bfloat162float(row[hq * D + i + half]);
+                v = d < half ? bfr16(bfr16(x1 * c) + bfr16(-x2 * sn)) : bfr16(bfr16(x2 * c) + bfr16(x1 * sn));
+            }
+            qsm[idx] = v;
+        }
+        if (t0 <= pos && pos < t1 && rg == 0) {
+            __nv_bfloat16 *kc = (__nv_bfloat16 *)p.k + b * p.ks[0] + kvh * p.ks[1] + (int64_t)pos * p.ks[2];
+            __nv_bfloat16 *vc = (__nv_bfloat16 *)p.v + b * p.vs[0] + kvh * p.vs[1] + (int64_t)pos * p.vs[2];
+            const __nv_bfloat16 *kr = row + (p.Hq + kvh) * D, *vr = row + (p.Hq + p.Hkv + kvh) * D;
+            for (int i = tid; i < half; i += kThreads) {
+                const float c = cs[i], sn = sn_t[i];
+                const float x1 = __bfloat162float(kr[i]), x2 = __bfloat162float(kr[i + half]);
+                kc[i] = __float2bfloat16_rn(bfr16(x1 * c) + bfr16(-x2 * sn));
+                kc[i + half] = __float2bfloat16_rn(bfr16(x2 * c) + bfr16(x1 * sn));
+                vc[i] = vr[i];
+                vc[i + half] = vr[i + half];
+            }
+        }
+        __syncthreads();  // the appended slot is written before any tile copy reads it
+    } else {
+        for (int idx = tid; idx < RMAX * D; idx += kThreads) {
+            const int r = idx / D, d = idx % D;
+            float v = 0.0f;
+            if (r < R) {
+                const int gr = rg * p.rows + r, l = gr / p.rep, hq = kvh * p.rep + gr % p.rep;
+                v = to_f32<T>(static_cast<const T *>(p.q)[b * p.qs[0] + hq * p.qs[1] + l * p.qs[2] + d]);
+            }
+            qsm[idx] = v;
+        }
     }
     if (tid < RMAX) {
         stat[tid] = -INFINITY;       // m
@@ -284,6 +406,8 @@ __global__ void __launch_bounds__(kThreads) sdpa_decode_kernel(const SdpaParams 
             p.part_ml[(row * p.splits + split) * 2 + 1] = stat[RMAX + r];
         }
     }
+    if (!p.counters) return;
+    merge_if_last<T, D>(p, b, kvh, rg, R, tid, reinterpret_cast<float *>(ring));
 }
 
 // Merge the splits of one output row: M = max m_s, w_s = exp(m_s - M),
@@ -329,6 +453,326 @@ __global__ void __launch_bounds__(128) sdpa_combine_kernel(const SdpaParams p) {
     if (lane == 0 && p.lse) p.lse[row] = logf(den) + M;
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core variant for bf16 / f16 (the decode path of the model): the same
+// split-KV algorithm with QK^T and PV on mma.sync.m16n8k16 (f32 accumulate).
+// The query rows of the CTA (rep heads of one KV head, <= 16) are the MMA's
+// M = 16 rows; each of the 4 warps walks its own 16-key tiles through its own
+// 3-stage cp.async ring with no CTA-wide barrier per tile (FlashAttention-2's
+// register layout: the score fragment is re-used as the PV A fragment). The
+// probabilities enter PV rounded to the input dtype; scores, the softmax and
+// every sum stay f32. Warps merge their (m, l, o) in shared memory; the CTA
+// writes the split's partial and the last CTA merges the splits, as above.
+// ---------------------------------------------------------------------------
+
+constexpr int TKM = 16;     // keys per warp tile
+constexpr int NST = 3;      // per-warp ring depth
+constexpr int MMA_WARPS = 4;
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                        uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// Byte offset of 16-byte chunk c of row j in a [rows][D] 16-bit tile: chunks
+// XOR-swizzled by the row's low 3 bits, so the 8 rows an ldmatrix phase reads
+// at one column land in 8 different bank groups.
+template <int D>
+__device__ __forceinline__ uint32_t tile_off(int j, int c) {
+    return (uint32_t)(j * (D * 2) + ((c ^ (j & 7)) * 16));
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const SdpaParams p) {
+    constexpr int CPR = D * 2 / 16;                // 16-byte chunks per row
+    constexpr int TILE = TKM * D * 2;              // bytes of one K (or V) tile
+    constexpr int NT = D / 8;                      // output n-tiles
+    constexpr int KS = D / 16;                     // k-steps of QK^T
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *qb = smem;                                            // [16][D] T, swizzled
+    float *tabs = reinterpret_cast<float *>(smem + 16 * D * 2);    // RoPE cos/sin [D]
+    uint8_t *rings = smem + 16 * D * 2 + D * 4;                    // MMA_WARPS x NST x (K, V)
+    float *cmb = reinterpret_cast<float *>(rings);                 // after the rings drain: warp merge
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int split = blockIdx.x, rg = blockIdx.y % p.row_groups, kvh = blockIdx.y / p.row_groups, b = blockIdx.z;
+    const int R = min(p.rows, p.rep * p.L - rg * p.rows);
+
+    pdl_launch_dependents();
+    pdl_wait();
+    const int S = p.S_dev ? min(*p.S_dev + p.S_add, p.S) : p.S;
+    const int t0 = split * p.keys_per_split, t1 = min(S, t0 + p.keys_per_split);
+    const uint32_t qb_u = smem_u32(qb);
+
+    // ---- query rows -> qb (16-bit, rows >= R zero), with the fused RoPE/append
+    if (p.qkv) {
+        const int pos = S - 1, half = D / 2, W = (p.Hq + 2 * p.Hkv) * D;
+        const __nv_bfloat16 *row = p.qkv + (int64_t)b * W;
+        for (int i = tid; i < half; i += MMA_WARPS * 32) {
+            const float f = p.inv_freq[i] * (float)pos;
+            tabs[i] = bfr16(cosf(f));
+            tabs[half + i] = bfr16(sinf(f));
+        }
+        __syncthreads();
+        for (int idx = tid; idx < 16 * D; idx += MMA_WARPS * 32) {
+            const int r = idx / D, d = idx % D;
+            float v = 0.0f;
+            if (r < R) {
+                const int hq = kvh * p.rep + r, i = d % half;
+                const float c = tabs[i], sn = tabs[half + i];
+                const float x1 = __bfloat162float(row[hq * D + i]), x2 = __bfloat162float(row[hq * D + i + half]);
+                v = d < half ? bfr16(bfr16(x1 * c) + bfr16(-x2 * sn)) : bfr16(bfr16(x2 * c) + bfr16(x1 * sn));
+            }
+            reinterpret_cast<T *>(qb + tile_off<D>(r, d / 8))[d % 8] = (T)v;
+        }
+        if (t0 <= pos && pos < t1 && rg == 0) {
+            __nv_bfloat16 *kc = (__nv_bfloat16 *)p.k + b * p.ks[0] + kvh * p.ks[1] + (int64_t)pos * p.ks[2];
+            __nv_bfloat16 *vc = (__nv_bfloat16 *)p.v + b * p.vs[0] + kvh * p.vs[1] + (int64_t)pos * p.vs[2];
+            const __nv_bfloat16 *kr = row + (p.Hq + kvh) * D, *vr = row + (p.Hq + p.Hkv + kvh) * D;
+            for (int i = tid; i < half; i += MMA_WARPS * 32) {
+                const float c = tabs[i], sn = tabs[half + i];
+                const float x1 = __bfloat162float(kr[i]), x2 = __bfloat162float(kr[i + half]);
+                kc[i] = __float2bfloat16_rn(bfr16(x1 * c) + bfr16(-x2 * sn));
+                kc[i + half] = __float2bfloat16_rn(bfr16(x2 * c) + bfr16(x1 * sn));
+                vc[i] = vr[i];
+                vc[i + half] = vr[i + half];
+            }
+        }
+    } else {
+        for (int idx = tid; idx < 16 * D; idx += MMA_WARPS * 32) {
+            const int r = idx / D, d = idx % D;
+            T v = (T)0.0f;
+            if (r < R) {
+                const int gr = rg * p.rows + r, l = gr / p.rep, hq = kvh * p.rep + gr % p.rep;
+                v = static_cast<const T *>(p.q)[b * p.qs[0] + hq * p.qs[1] + l * p.qs[2] + d];
+            }
+            reinterpret_cast<T *>(qb + tile_off<D>(r, d / 8))[d % 8] = v;
+        }
+    }
+    __syncthreads();  // qb complete; the appended slot is written before any tile copy reads it
+
+    // ---- per-warp tiles: w, w + 4, ... of the split's 16-key tiles
+    const int ntiles = t1 > t0 ? (t1 - t0 + TKM - 1) / TKM : 0;
+    const T *kbase = static_cast<const T *>(p.k) + b * p.ks[0] + kvh * p.ks[1];
+    const T *vbase = static_cast<const T *>(p.v) + b * p.vs[0] + kvh * p.vs[1];
+    const uint32_t ring_u = smem_u32(rings) + warp * NST * 2 * TILE;
+    auto issue = [&](int tile, int stage) {
+        const uint32_t kst = ring_u + stage * 2 * TILE, vst = kst + TILE;
+        for (int idx = lane; idx < TKM * CPR; idx += 32) {
+            const int j = idx / CPR, c = idx % CPR;
+            const int t = t0 + tile * TKM + j;
+            const bool ok = t < t1;
+            const int ts = ok ? t : t0;
+            cp_async16(kst + tile_off<D>(j, c), kbase + (int64_t)ts * p.ks[2] + c * 8, ok ? 16u : 0u);
+            cp_async16(vst + tile_off<D>(j, c), vbase + (int64_t)ts * p.vs[2] + c * 8, ok ? 16u : 0u);
+        }
+    };
+#pragma unroll
+    for (int s2 = 0; s2 < NST - 1; ++s2) {
+        const int tile = warp + s2 * MMA_WARPS;
+        if (tile < ntiles) issue(tile, s2);
+        cp_async_commit();
+    }
+
+    // Q fragments (A operand, rows g / g+8, all k-steps), loaded once
+    uint32_t qa[KS][4];
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+        const int c0 = 2 * kk, c1 = 2 * kk + 1;
+        qa[kk][0] = *reinterpret_cast<const uint32_t *>(qb + tile_off<D>(g, c0) + 4 * t4);
+        qa[kk][1] = *reinterpret_cast<const uint32_t *>(qb + tile_off<D>(g + 8, c0) + 4 * t4);
+        qa[kk][2] = *reinterpret_cast<const uint32_t *>(qb + tile_off<D>(g, c1) + 4 * t4);
+        qa[kk][3] = *reinterpret_cast<const uint32_t *>(qb + tile_off<D>(g + 8, c1) + 4 * t4);
+    }
+    int lrow[2];  // query position of rows g, g+8 (causal masking)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int gr = rg * p.rows + g + 8 * h;
+        lrow[h] = gr / p.rep;
+    }
+
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
+
+    int it = 0;
+    for (int tile = warp; tile < ntiles; tile += MMA_WARPS, ++it) {
+        {   // keep NST - 1 tiles ahead
+            const int nxt = tile + (NST - 1) * MMA_WARPS;
+            if (nxt < ntiles) issue(nxt, (it + NST - 1) % NST);
+            cp_async_commit();
+        }
+        cp_async_wait<NST - 1>();
+        __syncwarp();
+        const int stage = it % NST;
+        const uint32_t kst = ring_u + stage * 2 * TILE, vst = kst + TILE;
+
+        // S = Q K^T for 16 keys: n-tiles 0 (keys 0-7) and 1 (keys 8-15)
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            const int mat = lane >> 3, rr = lane & 7;
+            const int key = rr + ((mat & 2) ? 8 : 0), c = 2 * kk + (mat & 1);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(kst + tile_off<D>(key, c), b0, b1, b2, b3);
+            mma16816<T>(sc[0], qa[kk], b0, b1);
+            mma16816<T>(sc[1], qa[kk], b2, b3);
+        }
+        // scale, mask, online softmax for rows g (h = 0) and g + 8 (h = 1)
+        const int tb = t0 + tile * TKM;
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e >> 1, key = tb + 8 * n + 2 * t4 + (e & 1);
+                float v = sc[n][e] * p.scale;
+                const bool masked = key >= t1 || (p.causal && key > lrow[h]);
+                v = masked ? -INFINITY : v + 0.0f;
+                sc[n][e] = v;
+                mx[h] = fmaxf(mx[h], v);
+            }
+        }
+        float alpha[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+            const float m_new = fmaxf(m_run[h], mx[h]);
+            alpha[h] = (m_run[h] == -INFINITY) ? 0.0f : expf(m_run[h] - m_new);
+            m_run[h] = m_new;
+        }
+        float ps[2][4];
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e >> 1;
+                ps[n][e] = (m_run[h] == -INFINITY) ? 0.0f : expf(sc[n][e] - m_run[h]);
+            }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            l_run[h] = l_run[h] * alpha[h] + ps[0][2 * h] + ps[0][2 * h + 1] + ps[1][2 * h] + ps[1][2 * h + 1];
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            o[n][0] *= alpha[0];
+            o[n][1] *= alpha[0];
+            o[n][2] *= alpha[1];
+            o[n][3] *= alpha[1];
+        }
+        // O += P V: P as the A fragment (keys 0-15 = k), V through ldmatrix.trans
+        uint32_t pa[4];
+        pa[0] = pack2<T>(ps[0][0], ps[0][1]);
+        pa[1] = pack2<T>(ps[0][2], ps[0][3]);
+        pa[2] = pack2<T>(ps[1][0], ps[1][1]);
+        pa[3] = pack2<T>(ps[1][2], ps[1][3]);
+#pragma unroll
+        for (int n2 = 0; n2 < NT / 2; ++n2) {
+            const int mat = lane >> 3, rr = lane & 7;
+            const int key = rr + ((mat & 1) ? 8 : 0), c = 2 * n2 + (mat >> 1);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(vst + tile_off<D>(key, c), b0, b1, b2, b3);
+            mma16816<T>(o[2 * n2], pa, b0, b1);
+            mma16816<T>(o[2 * n2 + 1], pa, b2, b3);
+        }
+        __syncwarp();  // this stage is refilled NST - 1 tiles later
+    }
+    cp_async_wait<0>();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+        l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+    }
+    __syncthreads();  // every warp's ring is drained: reuse it for the warp merge
+
+    // ---- merge the 4 warps: cmb = [warp][16] m, [warp][16] l, [warp][16][D] o
+    float *wm = cmb, *wl = cmb + MMA_WARPS * 16, *wo = cmb + 2 * MMA_WARPS * 16;
+    if (t4 == 0) {
+        wm[warp * 16 + g] = m_run[0];
+        wm[warp * 16 + g + 8] = m_run[1];
+        wl[warp * 16 + g] = l_run[0];
+        wl[warp * 16 + g + 8] = l_run[1];
+    }
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+        float *r0p = wo + (warp * 16 + g) * D + 8 * n + 2 * t4, *r1p = wo + (warp * 16 + g + 8) * D + 8 * n + 2 * t4;
+        r0p[0] = o[n][0];
+        r0p[1] = o[n][1];
+        r1p[0] = o[n][2];
+        r1p[1] = o[n][3];
+    }
+    __syncthreads();
+    for (int idx = tid; idx < R * D; idx += MMA_WARPS * 32) {
+        const int r = idx / D, d = idx % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < MMA_WARPS; ++w) M = fmaxf(M, wm[w * 16 + r]);
+        float acc = 0.0f, l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < MMA_WARPS; ++w) {
+            const float mw = wm[w * 16 + r];
+            const float a = (mw == -INFINITY) ? 0.0f : expf(mw - M);
+            acc = fmaf(a, wo[(w * 16 + r) * D + d], acc);
+            l = fmaf(a, wl[w * 16 + r], l);
+        }
+        const int gr = rg * p.rows + r, lq = gr / p.rep, hq = kvh * p.rep + gr % p.rep;
+        const int64_t row = ((int64_t)b * p.Hq + hq) * p.L + lq;
+        p.part_o[(row * p.splits + split) * D + d] = acc;
+        if (d == 0) {
+            p.part_ml[(row * p.splits + split) * 2 + 0] = M;
+            p.part_ml[(row * p.splits + split) * 2 + 1] = l;
+        }
+    }
+    if (!p.counters) return;
+    merge_if_last<T, D>(p, b, kvh, rg, R, tid, cmb);
+}
+
+template <int D>
+size_t decode_mma_smem() {
+    const size_t rings = (size_t)MMA_WARPS * NST * 2 * TKM * D * 2;
+    const size_t merge = (size_t)(2 * MMA_WARPS * 16 + MMA_WARPS * 16 * D) * 4;
+    return 16 * D * 2 + D * 4 + (rings > merge ? rings : merge) + 128;
+}
+
 template <typename T, int D>
 size_t decode_smem() {
     using LY = Layout<T, D>;
@@ -336,15 +780,22 @@ size_t decode_smem() {
     return (size_t)(RMAX * D + RMAX * TK + 4 * RMAX) * 4 + (ring > o ? ring : o) + 128;
 }
 
-template <typename T, int D>
+template <typename T, int D, bool MMA>
 int launch_typed(const SdpaParams &p, cudaStream_t stream) {
-    const size_t smem = decode_smem<T, D>();
+    size_t smem;
+    void (*kernel)(const SdpaParams);
+    if constexpr (MMA) {
+        smem = decode_mma_smem<D>();
+        kernel = sdpa_decode_mma_kernel<T, D>;
+    } else {
+        smem = decode_smem<T, D>();
+        kernel = sdpa_decode_kernel<T, D>;
+    }
     static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        int st = check_cuda(cudaFuncSetAttribute(sdpa_decode_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem),
+        int st = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                             "aten._scaled_dot_product_flash_attention_for_cpu", "cudaFuncSetAttribute");
         if (st) return st;
         configured[dev] = 1;
@@ -354,24 +805,23 @@ int launch_typed(const SdpaParams &p, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.splits, p.row_groups * p.Hkv, p.B);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(MMA ? MMA_WARPS * 32 : kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int st = check_cuda(cudaLaunchKernelEx(&cfg, sdpa_decode_kernel<T, D>, p),
-                        "aten._scaled_dot_product_flash_attention_for_cpu", "cudaLaunchKernelEx (decode)");
+    int st = check_cuda(cudaLaunchKernelEx(&cfg, kernel, p), "aten._scaled_dot_product_flash_attention_for_cpu",
+                        "cudaLaunchKernelEx (decode)");
     if (st) return st;
+    __atomic_fetch_add(&counters().sdpa_decode_launches, 1ull, __ATOMIC_RELAXED);
+    if (p.counters) return TN_OK;
     const int64_t rows = (int64_t)p.B * p.Hq * p.L;
     cudaLaunchConfig_t cfg2 = cfg;
     cfg2.gridDim = dim3((unsigned)((rows + 3) / 4));
     cfg2.blockDim = dim3(128);
     cfg2.dynamicSmemBytes = 0;
-    st = check_cuda(cudaLaunchKernelEx(&cfg2, sdpa_combine_kernel<T, D>, p),
-                    "aten._scaled_dot_product_flash_attention_for_cpu", "cudaLaunchKernelEx (combine)");
-    if (st) return st;
-    __atomic_fetch_add(&counters().sdpa_decode_launches, 1ull, __ATOMIC_RELAXED);
-    return TN_OK;
+    return check_cuda(cudaLaunchKernelEx(&cfg2, sdpa_combine_kernel<T, D>, p),
+                      "aten._scaled_dot_product_flash_attention_for_cpu", "cudaLaunchKernelEx (combine)");
 }
 
 }  // namespace
@@ -381,8 +831,9 @@ int plan_sdpa_decode(SdpaParams &p, int sm_count) {
     p.rows = R < RMAX ? R : RMAX;
     p.row_groups = (R + p.rows - 1) / p.rows;
     const int64_t base = (int64_t)p.B * p.Hkv * p.row_groups;
-    // enough CTAs for ~4 per SM, but no split shorter than 4 tiles
-    int64_t want = (4LL * sm_count + base - 1) / base;
+    // about one CTA per SM, and no split shorter than 4 tiles: fewer, longer
+    // splits keep the merge (one partial per split) short
+    int64_t want = (1LL * sm_count + base - 1) / base;
     const int64_t max_splits = (p.S + 4 * TK - 1) / (4 * TK);
     if (want > max_splits) want = max_splits;
     if (want < 1) want = 1;
@@ -399,14 +850,20 @@ size_t sdpa_decode_workspace(const SdpaParams &p) {
 }
 
 int launch_sdpa_decode(const SdpaParams &p, int dtype, cudaStream_t stream) {
+    // bf16 / f16 without an additive mask: tensor cores; f32 (whose products
+    // must stay f32) and masked calls: the SIMT kernel.
+    const bool mma = dtype != TN_F32 && !p.mask;
     if (p.D == 128) {
-        if (dtype == TN_F32) return launch_typed<float, 128>(p, stream);
-        if (dtype == TN_BF16) return launch_typed<__nv_bfloat16, 128>(p, stream);
-        return launch_typed<__half, 128>(p, stream);
+        if (dtype == TN_F32) return launch_typed<float, 128, false>(p, stream);
+        if (dtype == TN_BF16)
+            return mma ? launch_typed<__nv_bfloat16, 128, true>(p, stream)
+                       : launch_typed<__nv_bfloat16, 128, false>(p, stream);
+        return mma ? launch_typed<__half, 128, true>(p, stream) : launch_typed<__half, 128, false>(p, stream);
     }
-    if (dtype == TN_F32) return launch_typed<float, 64>(p, stream);
-    if (dtype == TN_BF16) return launch_typed<__nv_bfloat16, 64>(p, stream);
-    return launch_typed<__half, 64>(p, stream);
+    if (dtype == TN_F32) return launch_typed<float, 64, false>(p, stream);
+    if (dtype == TN_BF16)
+        return mma ? launch_typed<__nv_bfloat16, 64, true>(p, stream) : launch_typed<__nv_bfloat16, 64, false>(p, stream);
+    return mma ? launch_typed<__half, 64, true>(p, stream) : launch_typed<__half, 64, false>(p, stream);
 }
 
 }  // namespace tn

@@ -25,6 +25,9 @@ tn_counters &counters();
 
 // Workspace from the caching allocator, grown on demand, one per (device, stream).
 int workspace(void **ptr, size_t bytes, cudaStream_t stream, int slot);
+// The same, zero-filled (stream-ordered) whenever it is (re)allocated; users
+// that need zeros keep it zeroed themselves between calls.
+int workspace_zeroed(void **ptr, size_t bytes, cudaStream_t stream, int slot);
 
 // Device facts cached per device.
 struct DeviceFacts {

@@ -112,6 +112,22 @@ int *device_error_word() {
     return g_error_word[dev];
 }
 
+int workspace_zeroed(void **ptr, size_t bytes, cudaStream_t stream, int slot) {
+    int dev = 0;
+    int st = check_cuda(cudaGetDevice(&dev), "workspace", "cudaGetDevice");
+    if (st) return st;
+    bool grew = false;
+    {
+        std::lock_guard<std::mutex> lk(g_ws_mu);
+        Workspace &w = g_ws[std::make_tuple(dev, stream, slot)];
+        grew = w.size < bytes;
+    }
+    st = workspace(ptr, bytes, stream, slot);
+    if (st) return st;
+    if (grew) return check_cuda(cudaMemsetAsync(*ptr, 0, bytes, stream), "workspace", "cudaMemsetAsync");
+    return TN_OK;
+}
+
 int workspace(void **ptr, size_t bytes, cudaStream_t stream, int slot) {
     int dev = 0;
     int st = check_cuda(cudaGetDevice(&dev), "workspace", "cudaGetDevice");

@@ -85,6 +85,8 @@ class Q4LlamaDecoder:
                 "qkv": random_q4_blob(s.qkv, s.hidden, gen, dev),
                 "o": random_q4_blob(s.hidden, s.heads * s.head_dim, gen, dev),
                 "mlp_norm": (1.0 + 0.1 * torch.randn(s.hidden, device=dev, generator=gen)).to(bf),
+                # gate_proj and up_proj interleaved row by row (row 2i = gate_i,
+                # row 2i+1 = up_i), so one GEMV writes SiLU(gate) * up directly
                 "gate_up": random_q4_blob(2 * s.inter, s.hidden, gen, dev),
                 "down": random_q4_blob(s.hidden, s.inter, gen, dev),
             })
@@ -98,6 +100,7 @@ class Q4LlamaDecoder:
         B, H, I = batch, s.hidden, s.inter
         kmax = max(H, I, s.heads * s.head_dim)
         self.h = torch.zeros((B, H), device=dev, dtype=bf)
+        self.h2 = torch.zeros((B, H), device=dev, dtype=bf)  # the residual's other half (ping-pong)
         self.delta = torch.zeros((B, H), device=dev, dtype=bf)
         self.codes = torch.zeros((B, kmax), device=dev, dtype=torch.int8)
         self.scales = torch.zeros((B, kmax // 32), device=dev, dtype=torch.float32)
@@ -105,7 +108,7 @@ class Q4LlamaDecoder:
         self.qkv_out = torch.zeros((B, s.qkv), device=dev, dtype=bf)
         self.q_rot = torch.zeros((B, s.heads, 1, s.head_dim), device=dev, dtype=bf)
         self.attn = torch.zeros((B, s.heads, 1, s.head_dim), device=dev, dtype=bf)
-        self.gu = torch.zeros((B, 2 * I), device=dev, dtype=bf)
+        self.act = torch.zeros((B, I), device=dev, dtype=bf)
         self.logits = torch.zeros((B, s.vocab), device=dev, dtype=bf)
         self.tokens = torch.zeros(B, device=dev, dtype=torch.int32)
         self.pos = torch.zeros(1, device=dev, dtype=torch.int32)
@@ -113,6 +116,11 @@ class Q4LlamaDecoder:
         self._qstr = st(self.q_rot)
         self._kstr = st(self.k_cache[0])
         self._graph = None
+        # Up to 4 rows, RMSNorm and the activation quantisation run inside the
+        # Q4_0 GEMVs, SiLU*up in the gate/up GEMV's epilogue, and RoPE/append/
+        # split-merge inside the SDPA launch: 6 kernels a layer. Larger batches
+        # use the separate kernels.
+        self.fused = batch <= 4
 
     # ---- bookkeeping
 
@@ -127,11 +135,13 @@ class Q4LlamaDecoder:
         s = self.s
         return 2 * self.n_layers * self.B * s.kv_heads * length * s.head_dim * 2
 
-    kernels_per_layer = 11
+    @property
+    def kernels_per_layer(self) -> int:
+        return 6 if self.fused else 11
 
     @property
     def kernels_per_step(self) -> int:
-        return self.kernels_per_layer * self.n_layers + 3
+        return self.kernels_per_layer * self.n_layers + (2 if self.fused else 3)
 
     def fill_prompt_cache(self, length: int, seed: int = 1) -> None:
         """The prompt's K/V: synthetic N(0,1) values in slots [0, length), and
@@ -155,10 +165,10 @@ class Q4LlamaDecoder:
     def _stream():
         return P(torch.cuda.current_stream().cuda_stream)
 
-    def _linear(self, w, y, n, k, stream):
+    def _linear(self, w, y, n, k, stream, flags=0):
         N.check(N.lib().tn_q4_0_linear_q8(P(self.codes.data_ptr()), k, P(self.scales.data_ptr()),
                                           P(self.offsets.data_ptr()), P(w.data_ptr()), None, P(y.data_ptr()),
-                                          N.TN_BF16, self.B, n, k, N.TN_WEIGHTS_STATIC, stream))
+                                          N.TN_BF16, self.B, n, k, N.TN_WEIGHTS_STATIC | flags, stream))
 
     def _norm(self, delta, weight, stream):
         N.check(N.lib().tn_llama_add_rmsnorm_q8(P(self.h.data_ptr()), None if delta is None else P(delta.data_ptr()),
@@ -170,6 +180,8 @@ class Q4LlamaDecoder:
         """One token for every sequence: reads tokens' embeddings in self.h and
         the position self.pos; leaves the next tokens in self.tokens, their
         embeddings in self.h, and self.pos advanced by one."""
+        if self.fused:
+            return self._step_fused(stream or self._stream())
         L, s, B = N.lib(), self.s, self.B
         stream = stream or self._stream()
         D, Hq, Hkv = s.head_dim, s.heads, s.kv_heads
@@ -189,15 +201,95 @@ class Q4LlamaDecoder:
                                               Hq * D, stream))
             self._linear(lw["o"], self.delta, s.hidden, Hq * D, stream)
             self._norm(self.delta, lw["mlp_norm"], stream)
-            self._linear(lw["gate_up"], self.gu, 2 * s.inter, s.hidden, stream)
-            N.check(L.tn_llama_silu_mul_q8(P(self.gu.data_ptr()), B, s.inter, P(self.codes.data_ptr()),
-                                           P(self.scales.data_ptr()), P(self.offsets.data_ptr()), stream))
+            self._linear(lw["gate_up"], self.act, 2 * s.inter, s.hidden, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS)
+            N.check(L.tn_q8_0_quantize_planar(P(self.act.data_ptr()), N.TN_BF16, s.inter, P(self.codes.data_ptr()),
+                                              s.inter, P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B,
+                                              s.inter, stream))
             self._linear(lw["down"], self.delta, s.hidden, s.inter, stream)
         self._norm(self.delta, self.final_norm, stream)
         self._linear(self.lm_head, self.logits, s.vocab, s.hidden, stream)
         N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
                                         P(self.embed.data_ptr()), s.hidden, P(self.h.data_ptr()),
                                         P(self.pos.data_ptr()), stream))
+
+    def _fused_linear(self, mode, x, x_stride, delta, h_out, norm_w, w, y, n, k, stream, flags=0):
+        N.check(N.lib().tn_q4_0_linear_fused(mode, P(x.data_ptr()), x_stride,
+                                             None if delta is None else P(delta.data_ptr()),
+                                             None if h_out is None else P(h_out.data_ptr()),
+                                             None if norm_w is None else P(norm_w.data_ptr()), self.s.eps,
+                                             P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, self.B, n, k,
+                                             N.TN_WEIGHTS_STATIC | flags, stream))
+
+    def _step_fused(self, stream) -> None:
+        L, s, B = N.lib(), self.s, self.B
+        D, Hq, Hkv, H, I = s.head_dim, s.heads, s.kv_heads, s.hidden, s.inter
+        ha, hb = self.h, self.h2
+        for li, lw in enumerate(self.layers):
+            # residual: hb = ha + (previous layer's down_proj); qkv = Q4(RMSNorm(hb))
+            self._fused_linear(N.TN_X_RMSNORM, ha, H, None if li == 0 else self.delta, hb, lw["attn_norm"],
+                               lw["qkv"], self.qkv_out, s.qkv, H, stream)
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            N.check(L.tn_sdpa_decode_step(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()), P(kc.data_ptr()),
+                                          P(vc.data_ptr()), P(self.attn.data_ptr()), None, B, Hq, Hkv, D, self.cap,
+                                          self._kstr, self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D),
+                                          stream))
+            self._fused_linear(N.TN_X_BF16, self.attn, Hq * D, None, None, None, lw["o"], self.delta, H, Hq * D,
+                               stream)
+            # residual: ha = hb + o_proj; act = SiLU(gate) * up of Q4(RMSNorm(ha))
+            self._fused_linear(N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act,
+                               2 * I, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS)
+            # the activation quantiser once (not in each of the down GEMV's CTAs:
+            # 448 blocks per CTA cost more than a launch), then the planar GEMV
+            N.check(L.tn_q8_0_quantize_planar(P(self.act.data_ptr()), N.TN_BF16, I, P(self.codes.data_ptr()), I,
+                                              P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, I, stream))
+            self._linear(lw["down"], self.delta, H, I, stream)
+        self._fused_linear(N.TN_X_RMSNORM, ha, H, self.delta, hb, self.final_norm, self.lm_head, self.logits,
+                           s.vocab, H, stream)
+        N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
+                                        P(self.embed.data_ptr()), s.hidden, P(ha.data_ptr()),
+                                        P(self.pos.data_ptr()), stream))
+
+    def kernel_graphs(self) -> dict:
+        """For timing the step's parts: one CUDA graph per kind of launch in
+        the fused step, each running that launch once per layer with the
+        step's own arguments (so 32 back-to-back launches over 32 layers'
+        weights). Reads and writes the step's buffers; re-seed afterwards."""
+        if not self.fused:
+            return {}
+        L, s, B = N.lib(), self.s, self.B
+        D, Hq, Hkv, H, I = s.head_dim, s.heads, s.kv_heads, s.hidden, s.inter
+        ha, hb = self.h, self.h2
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        parts = {
+            "qkv_rmsnorm_gemv": lambda lw, li, st: self._fused_linear(
+                N.TN_X_RMSNORM, ha, H, self.delta, hb, lw["attn_norm"], lw["qkv"], self.qkv_out, s.qkv, H, st),
+            "sdpa_decode_step": lambda lw, li, st: N.check(L.tn_sdpa_decode_step(
+                P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()), P(self.k_cache[li].data_ptr()),
+                P(self.v_cache[li].data_ptr()), P(self.attn.data_ptr()), None, B, Hq, Hkv, D, self.cap, self._kstr,
+                self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D), st)),
+            "o_gemv": lambda lw, li, st: self._fused_linear(
+                N.TN_X_BF16, self.attn, Hq * D, None, None, None, lw["o"], self.delta, H, Hq * D, st),
+            "gate_up_rmsnorm_gemv_silu": lambda lw, li, st: self._fused_linear(
+                N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act, 2 * I, H, st,
+                N.TN_EPILOGUE_SILU_MUL_PAIRS),
+            "act_q8": lambda lw, li, st: N.check(L.tn_q8_0_quantize_planar(
+                P(self.act.data_ptr()), N.TN_BF16, I, P(self.codes.data_ptr()), I, P(self.scales.data_ptr()),
+                P(self.offsets.data_ptr()), B, I, st)),
+            "down_gemv": lambda lw, li, st: self._linear(lw["down"], self.delta, H, I, st),
+        }
+        graphs = {}
+        for name, fn in parts.items():
+            with torch.cuda.stream(side):
+                fn(self.layers[0], 0, self._stream())
+            side.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                for li, lw in enumerate(self.layers):
+                    fn(lw, li, self._stream())
+            graphs[name] = g
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        return graphs
 
     def capture(self) -> torch.cuda.CUDAGraph:
         """One eager step first, on the stream the capture will use (the
