@@ -83,6 +83,12 @@ CASES = [
     ("causal L=3 S=9 (upper-left)", 1, 4, 2, 3, 9, 64, True),
     ("causal L > S", 1, 4, 2, 9, 3, 64, True),
     ("llama3-like decode long S=5000", 1, 32, 8, 1, 5000, 128, False),
+    # prefill shapes (bf16/f16 here run the tcgen05 kernel: D = 128, many query rows)
+    ("llama3-like causal prefill L=S=300", 1, 32, 8, 300, 300, 128, True),
+    ("llama3-like causal prefill L=S=513 B=2", 2, 8, 2, 513, 513, 128, True),
+    ("non-causal L=200 S=700", 1, 4, 1, 200, 700, 128, False),
+    ("causal L=260 S=100 (rows past the last key)", 1, 2, 2, 260, 100, 128, True),
+    ("causal L=130 S=400 (upper-left with S > L)", 1, 4, 4, 130, 400, 128, True),
 ]
 
 
@@ -138,6 +144,18 @@ def test_refusals_in_the_reference_wording(att, cuda_device):
         att.scaled_dot_product_flash_attention_for_cpu(q.cpu(), q.cpu(), q.cpu())
     out, lse = att.scaled_dot_product_flash_attention_for_cpu(q[:, :, :0], q, q)
     assert out.shape == (1, 4, 0, 64) and lse.shape == (1, 4, 0)
+
+
+def test_prefill_runs_the_tcgen05_kernel(att, cuda_device):
+    from torchnative_b200 import _native
+
+    q = torch.randn(1, 32, 512, 128, device=cuda_device, dtype=torch.bfloat16)
+    k = torch.randn(1, 8, 512, 128, device=cuda_device, dtype=torch.bfloat16)
+    before = _native.counters()
+    att.scaled_dot_product_flash_attention_for_cpu(q, k, k, 0.0, True)
+    after = _native.counters()
+    assert after["sdpa_prefill_launches"] == before["sdpa_prefill_launches"] + 1
+    _native.device_status(reset=True)
 
 
 def test_counters_show_the_fused_kernel_ran(att, cuda_device):

@@ -86,6 +86,11 @@ extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void 
     p.scale = (float)sc;
     p.err = tn::device_error_word();
 
+    // Many query rows (prefill): the tcgen05 flash kernel, where it applies.
+    const bool tma_ok = aligned16(q) && (q_strides[0] * 2) % 16 == 0 && (q_strides[1] * 2) % 16 == 0 &&
+                        (q_strides[2] * 2) % 16 == 0;
+    if (dtype != TN_F32 && D == 128 && !attn_mask && p.rep * L > 16 && tma_ok && aligned16(out))
+        return tn::launch_sdpa_prefill(p, dtype, stream);
     st = tn::plan_sdpa_decode(p, f.sm_count);
     if (st) return st;
     void *ws = nullptr;

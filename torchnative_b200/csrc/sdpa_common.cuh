@@ -39,6 +39,9 @@ struct SdpaParams {
 };
 
 int launch_sdpa_decode(const SdpaParams &p, int dtype, cudaStream_t stream);
+// Prefill on tcgen05 tensor cores: bf16/f16, D = 128, no additive mask, TMA-
+// compatible q/k/v (16-byte aligned base and strides).
+int launch_sdpa_prefill(const SdpaParams &p, int dtype, cudaStream_t stream);
 size_t sdpa_decode_workspace(const SdpaParams &p);
 int plan_sdpa_decode(SdpaParams &p, int sm_count);
 

@@ -302,3 +302,38 @@ int tn_reset_counters(void) {
 }
 
 }  // extern "C"
+
+// ---- tensor maps -------------------------------------------------------------
+
+#include "tc05.cuh"
+
+namespace tn {
+
+int encode_map_4d_b16(CUtensorMap *map, const void *base, const uint64_t dims[4], const uint64_t strides_bytes[3],
+                      uint32_t box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!encode) {
+            void *fn = nullptr;
+            cudaDriverEntryPointQueryResult q{};
+            cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+            if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+                return set_error(TN_ERR_CUDA, "tensor map: cuTensorMapEncodeTiled is not available from the driver");
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        }
+    }
+    cuuint64_t gdim[4] = {dims[0], dims[1], dims[2], dims[3]};
+    cuuint64_t gstride[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+    cuuint32_t box[4] = {64, box_rows, 1, 1};
+    cuuint32_t estride[4] = {1, 1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(TN_ERR_INVALID, "tensor map: cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
+    return TN_OK;
+}
+
+}  // namespace tn
