@@ -53,11 +53,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemv", "sdpa_decode"],
+    ap.add_argument("--case", default=None, choices=["gemv", "sdpa_decode", "sdpa_prefill"],
                     help="kernel-level case instead of the decode step: 'gemv' times the decode GEMV alone on the "
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
     ap.add_argument("--rows", type=int, default=1, help="activation rows M for --case gemv")
     ap.add_argument("--batch", type=int, default=1, help="sequences decoded together (BASELINE: 1 and 16)")
+    ap.add_argument("--seqs", default="512,4096,16384", help="sequence lengths for --case sdpa_prefill")
     return ap.parse_args()
 
 
@@ -425,6 +426,9 @@ def main():
     if args.case == "sdpa_decode":
         run_case_sdpa_decode(args)
         return
+    if args.case == "sdpa_prefill":
+        run_case_sdpa_prefill(args)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -499,6 +503,49 @@ def run_case_sdpa_decode(args):
     peak, kind = measured_peaks()
     print(json.dumps({"case": "sdpa_decode", "B": B, "S": PROMPT + 1, "us_per_launch": us, "kv_bytes": kv,
                       "GBps": kv / us / 1e3, "frac": kv / us / 1e3 / peak, "peak_kind": kind}), flush=True)
+    N.device_status(reset=True)
+
+
+def run_case_sdpa_prefill(args):
+    """Kernel-level timing of causal prefill SDPA (32
+    query / 8 KV heads, D = 128, bf16) at batch --batch and the sequence
+    lengths of --seqs. One JSON line per length: TFLOP/s of the causal work
+    (4 * B * Hq * D * S(S+1)/2) against the measured dense bf16 peak."""
+    import ctypes
+
+    import torch
+
+    from torchnative_b200 import _native as N, attention, build
+
+    build.build()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak = 1590.0
+    kind = "fallback"
+    pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pp):
+        with open(pp) as fh:
+            peak, kind = float(json.load(fh)["bf16_tflops"]), "measured"
+    B = args.batch
+    for S in [int(x) for x in args.seqs.split(",")]:
+        g = torch.Generator(device=dev).manual_seed(S)
+        q = torch.randn((B, HEADS, S, HEAD_DIM), device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn((B, KV_HEADS, S, HEAD_DIM), device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn((B, KV_HEADS, S, HEAD_DIM), device=dev, generator=g).to(torch.bfloat16)
+        for _ in range(args.warmup):
+            attention.scaled_dot_product_flash_attention_for_cpu(q, k, v, 0.0, True)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            attention.scaled_dot_product_flash_attention_for_cpu(q, k, v, 0.0, True)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        flops = 4.0 * B * HEADS * HEAD_DIM * S * (S + 1) / 2
+        print(json.dumps({"case": "sdpa_prefill", "B": B, "S": S, "ms": ms, "TFLOPs": flops / ms / 1e9,
+                          "frac": flops / ms / 1e9 / peak, "peak": peak, "peak_kind": kind}), flush=True)
+        del q, k, v
     N.device_status(reset=True)
 
 

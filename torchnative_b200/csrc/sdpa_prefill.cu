@@ -26,7 +26,7 @@ constexpr int PANEL = BM * 128;         // one 64-column panel of a 128-row tile
 constexpr int TILE = 2 * PANEL;         // a 128 x 128 16-bit tile
 constexpr int OFF_Q = 0, OFF_K0 = TILE, OFF_V0 = 2 * TILE, OFF_K1 = 3 * TILE, OFF_V1 = 4 * TILE, OFF_P = 5 * TILE;
 constexpr int OFF_BAR = 6 * TILE;
-constexpr size_t PREFILL_SMEM = 6 * TILE + 256 + 1024;  // + barriers, TMEM slot, alignment slack
+constexpr size_t PREFILL_SMEM = 6 * TILE + 64 + 2 * 128 * 4 + 1024;  // + barriers, exchange, alignment
 
 struct PrefillArgs {
     int B, Hq, Hkv, L, S, rep, causal, bf16;
@@ -49,7 +49,7 @@ __device__ __forceinline__ uint32_t pack_t(float lo, float hi, int bf16) {
     return *reinterpret_cast<const uint32_t *>(&v);
 }
 
-__global__ void __launch_bounds__(128, 1) sdpa_prefill_kernel(const __grid_constant__ CUtensorMap mq,
+__global__ void __launch_bounds__(256, 1) sdpa_prefill_kernel(const __grid_constant__ CUtensorMap mq,
                                                               const __grid_constant__ CUtensorMap mk,
                                                               const __grid_constant__ CUtensorMap mv,
                                                               const PrefillArgs a) {
@@ -57,19 +57,25 @@ __global__ void __launch_bounds__(128, 1) sdpa_prefill_kernel(const __grid_const
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb = smem_u32(base);
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + OFF_BAR);
-    uint64_t *q_full = bars, *kv_full = bars + 1 /*[2]*/, *s_done = bars + 3, *o_done = bars + 4;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 5);
+    uint64_t *q_full = bars, *k_full = bars + 1 /*[2]*/, *v_full = bars + 3 /*[2]*/, *s_done = bars + 5,
+             *o_done = bars + 6;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 7);
+    float *xch = reinterpret_cast<float *>(base + OFF_BAR + 64);  // [2][128] row partials between the warpgroups
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    // Two warpgroups: both own every query row (thread r of a warpgroup owns
+    // TMEM lane r = row q0 + r); warpgroup 0 works on key/dim columns 0-63,
+    // warpgroup 1 on 64-127, and they trade row maxima and sums through `xch`.
+    const int tid = threadIdx.x, warp = tid >> 5, wg = tid >> 7, r = tid & 127;
     const int qt = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
     const int hkv = hq / a.rep, q0 = qt * BM;
-    const int row = q0 + tid;  // this thread's query row
+    const int row = q0 + r;
     const int last_key = a.causal ? min(q0 + BM - 1, a.S - 1) : a.S - 1;
     const int ntiles = last_key / BN + 1;
+    const float c2 = a.scale * 1.4426950408889634f;  // scale * log2(e): p = 2^(s*c2 - m2)
 
     if (warp == 0) tc05::alloc(tmem_slot, 256);
     if (tid == 0) {
-        for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 7; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
         tc05::prefetch_map(&mq);
         tc05::prefetch_map(&mk);
@@ -78,130 +84,148 @@ __global__ void __launch_bounds__(128, 1) sdpa_prefill_kernel(const __grid_const
     tc05::fence_before();
     __syncthreads();
     tc05::fence_after();
-    const uint32_t tmem = *tmem_slot, tS = tmem, tO = tmem + 128;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + wg * 64, tO = tmem + 128 + lane_off + wg * 64;
 
     pdl_launch_dependents();
     pdl_wait();
 
-    int issued = 0;  // K/V tiles requested (thread 0)
-    auto load_kv = [&](int j) {
+    // K and V rings of two stages each, tracked separately: K_{j+2} may replace
+    // K_j once S_j is computed, V_{j+1} replaces V_{j-1} once PV_{j-1} is done.
+    int k_issued = 0, v_issued = 0;  // tiles requested (thread 0)
+    auto load_k = [&](int j) {
         const int st = j & 1;
-        const uint32_t kd = sb + (st ? OFF_K1 : OFF_K0), vd = sb + (st ? OFF_V1 : OFF_V0);
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
-        for (int p = 0; p < 2; ++p) {
-            tc05::tma_load_4d(kd + p * PANEL, &mk, p * 64, j * BN, hkv, b, &kv_full[st]);
-            tc05::tma_load_4d(vd + p * PANEL, &mv, p * 64, j * BN, hkv, b, &kv_full[st]);
+        const uint32_t kd = sb + (st ? OFF_K1 : OFF_K0);
+        mbar_arrive_expect_tx(&k_full[st], TILE);
+        for (int p = 0; p < 2; ++p) tc05::tma_load_4d(kd + p * PANEL, &mk, p * 64, j * BN, hkv, b, &k_full[st]);
+    };
+    auto load_v = [&](int j) {
+        const int st = j & 1;
+        const uint32_t vd = sb + (st ? OFF_V1 : OFF_V0);
+        mbar_arrive_expect_tx(&v_full[st], TILE);
+        for (int p = 0; p < 2; ++p) tc05::tma_load_4d(vd + p * PANEL, &mv, p * 64, j * BN, hkv, b, &v_full[st]);
+    };
+    const uint32_t id_qk = tc05::idesc_f16(a.bf16 != 0, BM, BN, false);
+    const uint32_t id_pv = tc05::idesc_f16(a.bf16 != 0, BM, HD, true);
+    bool bad = false, aborted = false;
+    // S_j = Q K_j^T into TMEM columns [0, 128), by thread 0.
+    auto issue_qk = [&](int j) {
+        const int st = j & 1;
+        bool ok = !bad && (j > 0 || mbar_wait(q_full, 0)) && mbar_wait(&k_full[st], (j >> 1) & 1);
+        if (!ok) {
+            record_device_error(a.err, DEV_ERR_WAIT_FULL);
+            bad = true;
+        } else {
+            tc05::fence_after();
+            const uint32_t kb = sb + (st ? OFF_K1 : OFF_K0);
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk) {
+                const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
+                tc05::mma_ss(tmem, tc05::desc_sw128(sb + OFF_Q + off, 16, 1024), tc05::desc_sw128(kb + off, 16, 1024),
+                             id_qk, kk > 0);
+            }
         }
+        tc05::commit(s_done);  // arrives even if nothing was issued
     };
     if (tid == 0) {
         mbar_arrive_expect_tx(q_full, TILE);
         for (int p = 0; p < 2; ++p) tc05::tma_load_4d(sb + OFF_Q + p * PANEL, &mq, p * 64, q0, hq, b, q_full);
-        load_kv(0);
-        issued = 1;
-        if (ntiles > 1) {
-            load_kv(1);
-            issued = 2;
+        for (int j = 0; j < 2 && j < ntiles; ++j) {
+            load_k(j);
+            load_v(j);
         }
+        k_issued = v_issued = ntiles < 2 ? ntiles : 2;
+        issue_qk(0);
     }
 
-    const uint32_t id_qk = tc05::idesc_f16(a.bf16 != 0, BM, BN, false);
-    const uint32_t id_pv = tc05::idesc_f16(a.bf16 != 0, BM, HD, true);
-    float m_run = -INFINITY, l_run = 0.0f;
-    // A bounded wait that gives up sets `bad`; the CTA leaves the loop together
-    // at the next barrier (__syncthreads_or), then drains and frees TMEM.
-    bool bad = false, aborted = false;
-
+    float m2 = -INFINITY, l_part = 0.0f;  // running max (log2 units, scaled) and this half's sum
     for (int j = 0; j < ntiles; ++j) {
-        const int st = j & 1;
-        // ---- S = Q K_j^T (one thread issues)
-        if (tid == 0) {
-            bool ok = !bad && (j > 0 || mbar_wait(q_full, 0)) && mbar_wait(&kv_full[st], (j >> 1) & 1);
-            if (!ok) {
-                record_device_error(a.err, DEV_ERR_WAIT_FULL);
-                bad = true;
-            } else {
-                tc05::fence_after();
-                const uint32_t kb = sb + (st ? OFF_K1 : OFF_K0);
-#pragma unroll
-                for (int kk = 0; kk < HD / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * PANEL + (kk & 3) * 32;
-                    tc05::mma_ss(tS, tc05::desc_sw128(sb + OFF_Q + off, 16, 1024), tc05::desc_sw128(kb + off, 16, 1024),
-                                 id_qk, kk > 0);
-                }
-            }
-            tc05::commit(s_done);  // arrives even if nothing was issued
-        }
+        // ---- S_j, this warpgroup's 64 keys of row r
         if (!mbar_wait(s_done, j & 1)) {
             record_device_error(a.err, DEV_ERR_WAIT_FULL);
             bad = true;
         }
         tc05::fence_after();
-
-        // ---- scores of this row, masked; online softmax
-        float s[BN];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
+        if (tid == 0 && k_issued < ntiles && k_issued == j + 2 && !bad) {  // S_j done: K stage j&1 is free
+            load_k(k_issued);
+            ++k_issued;
+        }
+        float sv[64];
+        {
             float v[32];
-            tc05::ld32(tS + lane_off + c * 32, v);
+            tc05::ld32(tS, v);
             tc05::wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
+            for (int i = 0; i < 32; ++i) sv[i] = v[i];
+            tc05::ld32(tS + 32, v);
+            tc05::wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sv[32 + i] = v[i];
         }
         float mx = -INFINITY;
+        const int kbase = j * BN + wg * 64;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-            const int key = j * BN + c;
+        for (int c = 0; c < 64; ++c) {
+            const int key = kbase + c;
             const bool masked = key >= a.S || (a.causal && key > row);
-            const float v = masked ? -INFINITY : s[c] * a.scale + 0.0f;
-            s[c] = v;
-            mx = fmaxf(mx, v);
+            sv[c] = masked ? -INFINITY : sv[c] * c2;
+            mx = fmaxf(mx, sv[c]);
         }
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
+        xch[wg * 128 + r] = mx;
+        tc05::fence_before();
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        // S_j is in registers everywhere: the tensor core may overwrite it with S_{j+1}
+        if (tid == 0 && j + 1 < ntiles) {
+            tc05::fence_after();
+            issue_qk(j + 1);
+        }
+        mx = fmaxf(mx, xch[(wg ^ 1) * 128 + r]);
+        const float m_new = fmaxf(m2, mx);
+        const float alpha = (m2 == -INFINITY) ? 0.0f : exp2f(m2 - m_new);
         float sum = 0.0f;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-            const float p = (m_new == -INFINITY) ? 0.0f : expf(s[c] - m_new);
-            s[c] = p;
+        for (int c = 0; c < 64; ++c) {
+            const float p = (m_new == -INFINITY) ? 0.0f : exp2f(sv[c] - m_new);
+            sv[c] = p;
             sum += p;
         }
-        l_run = l_run * alpha + sum;
-        m_run = m_new;
+        l_part = l_part * alpha + sum;
+        m2 = m_new;
 
-        // ---- the previous PV product is done before O is rescaled and P rewritten
+        // ---- PV_{j-1} finished: its K/V stage is free, O can be rescaled, P rewritten
         if (j > 0) {
             if (!mbar_wait(o_done, (j - 1) & 1)) {
                 record_device_error(a.err, DEV_ERR_WAIT_FULL);
                 bad = true;
             }
             tc05::fence_after();
-            if (tid == 0 && issued < ntiles && !bad) {  // the stage PV(j-1) read is free
-                load_kv(issued);
-                ++issued;
+            if (tid == 0 && v_issued < ntiles && v_issued == j + 1 && !bad) {  // PV_{j-1} done: V stage free
+                load_v(v_issued);
+                ++v_issued;
             }
             if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-                for (int c = 0; c < HD / 32; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     float v[32];
-                    tc05::ld32(tO + lane_off + c * 32, v);
+                    tc05::ld32(tO + c * 32, v);
                     tc05::wait_ld();
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] *= alpha;
-                    tc05::st32(tO + lane_off + c * 32, v);
+                    tc05::st32(tO + c * 32, v);
                 }
                 tc05::wait_st();
             }
         }
-        // P row -> shared memory, 128-byte swizzled K-major (keys = K)
+        // P (this warpgroup's 64 keys = one panel) -> shared memory, swizzled K-major
         {
-            const uint32_t prow = sb + OFF_P + tid * 128;
+            const uint32_t prow = sb + OFF_P + wg * PANEL + r * 128;
 #pragma unroll
-            for (int ch = 0; ch < BN / 8; ++ch) {
-                const int panel = ch >> 3, cc = ch & 7;
-                const uint32_t addr = prow + panel * PANEL + ((cc ^ (tid & 7)) << 4);
-                st_shared_v4(addr, pack_t(s[ch * 8 + 0], s[ch * 8 + 1], a.bf16), pack_t(s[ch * 8 + 2], s[ch * 8 + 3], a.bf16),
-                             pack_t(s[ch * 8 + 4], s[ch * 8 + 5], a.bf16), pack_t(s[ch * 8 + 6], s[ch * 8 + 7], a.bf16));
+            for (int cc = 0; cc < 8; ++cc) {
+                const uint32_t addr = prow + ((cc ^ (r & 7)) << 4);
+                st_shared_v4(addr, pack_t(sv[cc * 8 + 0], sv[cc * 8 + 1], a.bf16),
+                             pack_t(sv[cc * 8 + 2], sv[cc * 8 + 3], a.bf16), pack_t(sv[cc * 8 + 4], sv[cc * 8 + 5], a.bf16),
+                             pack_t(sv[cc * 8 + 6], sv[cc * 8 + 7], a.bf16));
             }
         }
         fence_proxy_async_smem();
@@ -210,49 +234,62 @@ __global__ void __launch_bounds__(128, 1) sdpa_prefill_kernel(const __grid_const
             aborted = true;
             break;
         }
-
         // ---- O += P V_j
         if (tid == 0) {
             tc05::fence_after();
+            const int st = j & 1;
             const uint32_t vb = sb + (st ? OFF_V1 : OFF_V0);
+            if (!mbar_wait(&v_full[st], (j >> 1) & 1)) {
+                record_device_error(a.err, DEV_ERR_WAIT_FULL);
+                bad = true;
+            }
+            tc05::fence_after();
 #pragma unroll
             for (int kk = 0; kk < BN / 16; ++kk) {
                 const uint32_t poff = (kk >> 2) * PANEL + (kk & 3) * 32;
-                tc05::mma_ss(tO, tc05::desc_sw128(sb + OFF_P + poff, 16, 1024),
+                tc05::mma_ss(tmem + 128, tc05::desc_sw128(sb + OFF_P + poff, 16, 1024),
                              tc05::desc_sw128(vb + kk * 2048, PANEL, 1024), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
             }
             tc05::commit(o_done);
         }
     }
 
-    // ---- out = O / l, lse = m + log l
+    // ---- out = O / l, lse = m + log l (the two halves' sums added)
+    xch[wg * 128 + r] = l_part;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const float l_run = l_part + xch[(wg ^ 1) * 128 + r];
     if (!aborted && mbar_wait(o_done, (ntiles - 1) & 1)) {
         tc05::fence_after();
         const float inv = 1.0f / l_run;
         const int64_t orow = ((int64_t)b * a.Hq + hq) * a.L + row;
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
             float v[32];
-            tc05::ld32(tO + lane_off + c * 32, v);
+            tc05::ld32(tO + c * 32, v);
             tc05::wait_ld();
             if (row < a.L) {
                 uint32_t w[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) w[i] = pack_t(v[2 * i] * inv, v[2 * i + 1] * inv, a.bf16);
-                int4 *dst = reinterpret_cast<int4 *>(static_cast<uint8_t *>(a.out) + (orow * HD + c * 32) * 2);
+                int4 *dst = reinterpret_cast<int4 *>(static_cast<uint8_t *>(a.out) + (orow * HD + wg * 64 + c * 32) * 2);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
                     dst[i] = make_int4((int)w[4 * i], (int)w[4 * i + 1], (int)w[4 * i + 2], (int)w[4 * i + 3]);
             }
         }
-        if (row < a.L && a.lse) a.lse[orow] = logf(l_run) + m_run;
+        if (row < a.L && a.lse && wg == 0) a.lse[orow] = m2 * 0.6931471805599453f + logf(l_run);
     } else if (!aborted) {
         record_device_error(a.err, DEV_ERR_WAIT_FULL);
     }
     // Drain: no TMA copy may still be writing this CTA's shared memory.
     if (tid == 0) {
-        for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
-            if (!mbar_wait(&kv_full[j & 1], (j >> 1) & 1)) {
+        for (int j = k_issued > 2 ? k_issued - 2 : 0; j < k_issued; ++j)
+            if (!mbar_wait(&k_full[j & 1], (j >> 1) & 1)) {
+                record_device_error(a.err, DEV_ERR_DRAIN);
+                break;
+            }
+        for (int j = v_issued > 2 ? v_issued - 2 : 0; j < v_issued; ++j)
+            if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1)) {
                 record_device_error(a.err, DEV_ERR_DRAIN);
                 break;
             }
@@ -315,7 +352,7 @@ int launch_sdpa_prefill(const SdpaParams &p, int dtype, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((p.L + BM - 1) / BM), (unsigned)p.Hq, (unsigned)p.B);
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = PREFILL_SMEM;
     cfg.stream = stream;
     cfg.attrs = attr;
