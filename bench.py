@@ -57,6 +57,7 @@ def parse():
                     help="kernel-level case instead of the decode step: 'gemv' times the decode GEMV alone on the "
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
     ap.add_argument("--rows", type=int, default=1, help="activation rows M for --case gemv")
+    ap.add_argument("--shape", default=None, help="one N,K for --case gemv (default: BASELINE's four shapes)")
     ap.add_argument("--batch", type=int, default=1, help="sequences decoded together (BASELINE: 1 and 16)")
     ap.add_argument("--seqs", default="512,4096,16384", help="sequence lengths for --case sdpa_prefill")
     return ap.parse_args()
@@ -568,7 +569,10 @@ def run_case_gemv(args):
     peak, peak_kind = measured_peaks()
     P = ctypes.c_void_p
     L = N.lib()
-    for n, k in ((14336, 4096), (4096, 14336), (6144, 4096), (28672, 4096)):
+    shapes = ((14336, 4096), (4096, 14336), (6144, 4096), (28672, 4096))
+    if args.shape:
+        shapes = (tuple(int(x) for x in args.shape.split(",")),)
+    for n, k in shapes:
         wbytes = q4_bytes(n, k)
         copies = max(2, -(-300_000_000 // wbytes))
         ws = [random_q4_blob(n, k, gen, dev) for _ in range(copies)]

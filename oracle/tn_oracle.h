@@ -10,7 +10,7 @@
  *
  * Parity pinning: the Q4_0/Q8_0 codec functions are checked byte for byte and
  * bit for bit against llama.cpp gguf-py's answers frozen in
- * tests/golden/q4_golden.json (extracted from the reference's
+ * tests/golden/q4_gguf_golden.json (extracted from the reference's
  * scripts/q4quality/golden_gguf_py.json), and against the installed gguf-py
  * codec on seeded inputs. The SDPA restatement is checked against upstream
  * torch 2.11's CPU kernel on the reference's golden SDPA cases

@@ -89,6 +89,8 @@ CASES = [
     ("non-causal L=200 S=700", 1, 4, 1, 200, 700, 128, False),
     ("causal L=260 S=100 (rows past the last key)", 1, 2, 2, 260, 100, 128, True),
     ("causal L=130 S=400 (upper-left with S > L)", 1, 4, 4, 130, 400, 128, True),
+    ("smollm2-like causal prefill L=S=700", 1, 9, 3, 700, 700, 64, True),
+    ("qwen3-like causal prefill L=S=1100", 1, 16, 8, 1100, 1100, 128, True),
 ]
 
 
@@ -108,6 +110,70 @@ def test_additive_mask_and_explicit_scale(att, cuda_device, dtype):
     mask[..., 2] = float("-inf")
     _check(att, cuda_device, q, k, v, dtype, False, mask=mask.to(torch.float32), label="mask f32")
     _check(att, cuda_device, q, k, v, dtype, True, mask=mask.to(DT[dtype]), scale=0.1, label="mask + causal")
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+def test_masked_prefill_per_head_mask(att, cuda_device, dtype):
+    """Many query rows with an additive [B, Hq, L, S] mask: the FP32-pipe flash
+    kernel (the tcgen05 kernel takes no mask)."""
+    q, k, v = _inputs(1790, 2, 8, 2, 200, 300, 128, dtype)
+    g = torch.Generator().manual_seed(7)
+    mask = torch.rand((2, 8, 200, 300), generator=g) * 4 - 2
+    mask[:, :, :, 250:] = float("-inf")
+    _check(att, cuda_device, q, k, v, dtype, False, mask=mask.to(torch.float32), label="per-head mask f32")
+    _check(att, cuda_device, q, k, v, dtype, True, mask=mask.to(DT[dtype]), label="per-head mask + causal")
+
+
+def test_unaligned_query_view_matches_the_contiguous_call(att, cuda_device):
+    """q sliced out of a wider buffer (row stride 129 elements: no TMA
+    descriptor can describe it) runs on the FP32-pipe kernel and agrees with
+    the tcgen05 kernel on the contiguous copy within the device rule."""
+    g = torch.Generator().manual_seed(11)
+    B, Hq, Hkv, L, D = 1, 8, 2, 320, 128
+    buf = (torch.rand((B, Hq, L, D + 1), generator=g) * 2 - 1).to(torch.bfloat16).to(cuda_device)
+    qv = buf[..., 1:]
+    assert qv.stride(2) == D + 1
+    k = (torch.rand((B, Hkv, L, D), generator=g) * 2 - 1).to(torch.bfloat16).to(cuda_device)
+    v = (torch.rand((B, Hkv, L, D), generator=g) * 2 - 1).to(torch.bfloat16).to(cuda_device)
+    o1, l1 = att.scaled_dot_product_flash_attention_for_cpu(qv, k, v, 0.0, True)
+    q = qv.contiguous()
+    o2, l2 = att.scaled_dot_product_flash_attention_for_cpu(q, k, v, 0.0, True)
+    f64, f64_lse = sdpa_ref.f64_reference(q.double().cpu().numpy(), k.double().cpu().numpy(),
+                                          v.double().cpu().numpy(), True, None)
+    cpu, _ = oracle.sdpa(_np_storage(q.cpu(), "bfloat16"), _np_storage(k.cpu(), "bfloat16"),
+                         _np_storage(v.cpu(), "bfloat16"), dtype="bfloat16", is_causal=True, threads=8)
+    bound = sdpa_ref.device_bound(sdpa_ref.from_storage(cpu, "bfloat16"), f64)
+    for o in (o1, o2):
+        assert float(np.max(np.abs(o.double().cpu().numpy() - f64))) <= bound
+    assert float((l1 - l2).abs().max()) <= 1e-4
+
+
+@pytest.mark.parametrize("dtype,d", [("float32", 64), ("float16", 64), ("float32", 128)])
+def test_long_prefill_rows_sampled(att, cuda_device, dtype, d):
+    """L = S = 16448 with 32 query heads: more 8-row groups than a grid's y
+    dimension holds (the split-KV kernel's layout), one FP32-pipe launch here.
+    Sampled rows are checked against the oracle run on that row alone (row i of
+    an upper-left causal call equals a one-row call over keys 0..i)."""
+    B, Hq, Hkv, L = 1, 32, 8, 16448
+    g = torch.Generator().manual_seed(23)
+    q = (torch.rand((B, Hq, L, d), generator=g) * 2 - 1).to(DT[dtype])
+    k = (torch.rand((B, Hkv, L, d), generator=g) * 2 - 1).to(DT[dtype])
+    v = (torch.rand((B, Hkv, L, d), generator=g) * 2 - 1).to(DT[dtype])
+    out, lse = att.scaled_dot_product_flash_attention_for_cpu(q.to(cuda_device), k.to(cuda_device),
+                                                              v.to(cuda_device), 0.0, True)
+    out, lse = out.float().cpu(), lse.cpu()
+    for h, i in [(0, 0), (5, 63), (31, 64), (12, 4097), (17, 9999), (31, L - 1)]:
+        hk = h // (Hq // Hkv)
+        qi, ki, vi = q[:, h:h + 1, i:i + 1], k[:, hk:hk + 1, :i + 1], v[:, hk:hk + 1, :i + 1]
+        f64, f64_lse = sdpa_ref.f64_reference(qi.double().numpy(), ki.double().numpy(), vi.double().numpy(),
+                                              False, None)
+        cpu, cpu_lse = oracle.sdpa(_np_storage(qi.contiguous(), dtype), _np_storage(ki.contiguous(), dtype),
+                                   _np_storage(vi.contiguous(), dtype), dtype=dtype, is_causal=False, threads=1)
+        bound = sdpa_ref.device_bound(sdpa_ref.from_storage(cpu, dtype), f64)
+        got = out[:, h:h + 1, i:i + 1].double().numpy()
+        assert float(np.max(np.abs(got - f64))) <= bound, (h, i)
+        lb = sdpa_ref.device_bound(cpu_lse.astype(np.float64), f64_lse)
+        assert abs(float(lse[0, h, i]) - float(f64_lse[0, 0, 0])) <= lb, (h, i)
 
 
 def test_kv_cache_view_is_read_in_place(att, cuda_device):

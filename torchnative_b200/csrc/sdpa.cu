@@ -53,7 +53,7 @@ extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void 
             return tn::set_error(TN_ERR_INVALID, op + ": key/value strides must be multiples of 16 bytes");
     if (!aligned16(k) || !aligned16(v))
         return tn::set_error(TN_ERR_INVALID, op + ": key/value must be 16-byte aligned");
-    if (B > 65535 || Hkv > 65535 || S > (int64_t)1 << 30 || L > (int64_t)1 << 30)
+    if (B > 65535 || Hq > 65535 || S > (int64_t)1 << 30 || L > (int64_t)1 << 30)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": size beyond the kernel's grid limits");
 
     tn::DeviceFacts f{};
@@ -91,6 +91,10 @@ extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void 
                         (q_strides[2] * 2) % 16 == 0;
     if (dtype != TN_F32 && D == 128 && !attn_mask && p.rep * L > 16 && tma_ok && aligned16(out))
         return tn::launch_sdpa_prefill(p, dtype, stream);
+    // Other calls with many query rows per head: the FP32-pipe flash kernel
+    // (one pass over K/V per 64 query rows, where the split-KV kernel would
+    // re-read K/V for every 8 rows).
+    if (L > 16) return tn::launch_sdpa_prefill_simt(p, dtype, stream);
     st = tn::plan_sdpa_decode(p, f.sm_count);
     if (st) return st;
     void *ws = nullptr;
