@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemv", "sdpa_decode", "sdpa_prefill"],
+    ap.add_argument("--case", default=None, choices=["gemv", "gemm", "sdpa_decode", "sdpa_prefill"],
                     help="kernel-level case instead of the decode step: 'gemv' times the decode GEMV alone on the "
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
     ap.add_argument("--rows", type=int, default=1, help="activation rows M for --case gemv")
@@ -424,6 +424,8 @@ def main():
     if args.case == "gemv":
         run_case_gemv(args)
         return
+    if args.case == "gemm":
+        return run_case_gemm(args)
     if args.case == "sdpa_decode":
         run_case_sdpa_decode(args)
         return
@@ -613,6 +615,60 @@ def run_case_gemv(args):
         del ws
         torch.cuda.empty_cache()
     N.device_status(reset=True)
+
+
+def run_case_gemm(args):
+    """Kernel-level timing of the prefill Q4_0 linear (tn_q4_0_linear with bf16
+    activations: the f16-code Q8_0 quantiser plus the tcgen05 GEMM) on
+    BASELINE's (N, K) shapes at --rows M (default 2048). One JSON line per
+    shape: TFLOP/s of 2*M*N*K against the measured dense bf16 peak."""
+    import ctypes
+
+    import torch
+
+    from torchnative_b200 import _native as N_, build
+
+    build.build()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6)
+    M = args.rows if args.rows > 16 else 2048
+    peak = 1590.0
+    kind = "fallback"
+    pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pp):
+        with open(pp) as fh:
+            peak, kind = float(json.load(fh)["bf16_tflops"]), "measured"
+    P = ctypes.c_void_p
+    shapes = ((14336, 4096), (4096, 14336), (6144, 4096))
+    if args.shape:
+        shapes = (tuple(int(x) for x in args.shape.split(",")),)
+    for n, k in shapes:
+        w = random_q4_blob(n, k, gen, dev)
+        x = torch.randn((M, k), device=dev, generator=gen).to(torch.bfloat16)
+        y = torch.empty((M, n), device=dev, dtype=torch.bfloat16)
+        s = lambda: P(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+
+        def launch():
+            N_.check(N_.lib().tn_q4_0_linear(P(x.data_ptr()), N_.TN_BF16, k, P(w.data_ptr()), None,
+                                             P(y.data_ptr()), N_.TN_BF16, M, n, k, N_.TN_ACT_Q8_0, s()))
+
+        for _ in range(args.warmup):
+            launch()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            launch()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        fl = 2.0 * M * n * k
+        print(json.dumps({"case": "gemm", "M": M, "N": n, "K": k, "ms": ms, "TFLOPs": fl / ms / 1e9,
+                          "frac": fl / ms / 1e9 / peak, "peak": peak, "peak_kind": kind}), flush=True)
+        del w, x, y
+    N_.device_status(reset=True)
 
 
 if __name__ == "__main__":

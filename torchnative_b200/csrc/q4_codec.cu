@@ -148,6 +148,40 @@ __global__ void q8_0_quantize_planar_kernel(const void *__restrict__ x, int64_t 
     xc[r * nb + b] = 12582912.0f + 8.0f * static_cast<float>(sum);
 }
 
+// Planar Q8_0 for the tensor-core GEMM: the codes written as f16 (exact:
+// |code| <= 127) so they are an MMA operand as they stand, and the widened
+// scale xd[rows][nb] = f32(f16 d). Within each 32-block the codes are stored
+// in the order the GEMM's weight unpacking produces (a block's sum does not
+// depend on the order of its terms, all of them exact integers): 16-byte chunk
+// c holds elements 4c + {0, 2, 16, 18, 1, 3, 17, 19}.
+template <typename T>
+__global__ void q8_0_quantize_planar_f16_kernel(const void *__restrict__ x, int64_t row_stride,
+                                                __half *__restrict__ xq, float *__restrict__ xd, int64_t rows,
+                                                int64_t nb, int64_t xq_row_stride) {
+    pdl_launch_dependents();
+    pdl_wait();
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= rows * nb) return;
+    int64_t r = i / nb, b = i % nb;
+    int8_t codes[32];
+    int sum;
+    uint32_t db = q8_0_block<T>(x, r * row_stride + b * 32, codes, &sum);
+    uint4 *dst = reinterpret_cast<uint4 *>(xq + r * xq_row_stride + b * 32);
+    constexpr int kPairLo[4] = {0, 16, 1, 17};  // pair e of chunk c: elements 4c + kPairLo[e] and + 2
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int i0 = 4 * c + kPairLo[e];
+            const __half2 h = __halves2half2(__int2half_rn(codes[i0]), __int2half_rn(codes[i0 + 2]));
+            w[e] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+        dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    xd[r * nb + b] = half_bits_to_f32(db);
+}
+
 int check_dtype_in(const char *op, int dtype) {
     if (dtype == TN_F32 || dtype == TN_BF16 || dtype == TN_F16) return TN_OK;
     return set_error(TN_ERR_NOT_IMPLEMENTED,
@@ -190,6 +224,41 @@ int launch_q8_planar(const void *x, int x_dtype, int64_t row_stride, int8_t *xq,
     if (st) return st;
     __atomic_fetch_add(&counters().q8_quant_launches, 1ull, __ATOMIC_RELAXED);
     return check_launch("torch._C._quantized_linear (activation Q8_0)");
+}
+
+int launch_q8_planar_f16(const void *x, int x_dtype, int64_t row_stride, __half *xq, float *xd, int64_t rows,
+                         int64_t nb, int64_t xq_row_stride, cudaStream_t stream) {
+    int64_t n = rows * nb;
+    if (n == 0) return TN_OK;
+    int threads = 128;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((n + threads - 1) / threads));
+    cfg.blockDim = dim3(threads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    switch (x_dtype) {
+    case TN_F32:
+        e = cudaLaunchKernelEx(&cfg, q8_0_quantize_planar_f16_kernel<float>, x, row_stride, xq, xd, rows, nb,
+                               xq_row_stride);
+        break;
+    case TN_BF16:
+        e = cudaLaunchKernelEx(&cfg, q8_0_quantize_planar_f16_kernel<__nv_bfloat16>, x, row_stride, xq, xd, rows, nb,
+                               xq_row_stride);
+        break;
+    default:
+        e = cudaLaunchKernelEx(&cfg, q8_0_quantize_planar_f16_kernel<__half>, x, row_stride, xq, xd, rows, nb,
+                               xq_row_stride);
+        break;
+    }
+    int st = check_cuda(e, "torch._C._quantized_linear (activation Q8_0, f16 codes)", "cudaLaunchKernelEx");
+    if (st) return st;
+    __atomic_fetch_add(&counters().q8_quant_launches, 1ull, __ATOMIC_RELAXED);
+    return TN_OK;
 }
 
 }  // namespace tn

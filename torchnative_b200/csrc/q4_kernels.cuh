@@ -10,6 +10,20 @@ namespace tn {
 int launch_q8_planar(const void *x, int x_dtype, int64_t row_stride, int8_t *xq, float *xd, float *xc, int64_t rows,
                      int64_t nb, int64_t xq_row_stride, cudaStream_t stream);
 
+// Planar Q8_0 with the codes as f16 (the tensor-core GEMM's A operand):
+// xq [rows][xq_row_stride] f16, xd [rows][nb] f32.
+int launch_q8_planar_f16(const void *x, int x_dtype, int64_t row_stride, __half *xq, float *xd, int64_t rows,
+                         int64_t nb, int64_t xq_row_stride, cudaStream_t stream);
+
+// Prefill Q4_0 x Q8_0 GEMM on tcgen05 (M > 16): codes f16 [M][xq_row_stride],
+// xd [M][K/32]; needs K % 256 == 0 and a 16-byte aligned blob.
+bool q4_gemm_applies(const void *w_blob, int64_t M, int64_t N, int64_t K);
+// Activation-row count from which tn_q4_0_linear takes the GEMM instead of
+// row chunks of the decode GEMV.
+constexpr int64_t kQ4GemmMinRows = 48;
+int launch_q4_gemm(const __half *xq, int64_t xq_row_stride, const float *xd, const uint8_t *w, const float *bias,
+                   void *y, int y_dtype, int64_t y_row_stride, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+
 // Largest activation-row count (<= 16) one GEMV launch holds in shared memory
 // for this K; 0 if even one row does not fit.
 int q4_gemv_max_rows(int64_t K);

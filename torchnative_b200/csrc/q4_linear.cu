@@ -36,10 +36,23 @@ extern "C" int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, 
                                   "(the reference's arithmetic)");
 
     const int64_t nb = K / 32;
+    void *ws = nullptr;
+    int st;
+    if (M >= tn::kQ4GemmMinRows && tn::q4_gemm_applies(w_blob, M, N, K)) {
+        // Many rows: f16 Q8 codes [M][K] and scales [M][nb] for the tensor-core GEMM.
+        const size_t codes16 = ((size_t)M * K * 2 + 255) & ~size_t(255);
+        st = tn::workspace(&ws, codes16 + (size_t)M * nb * 4 + 256, stream, /*slot=*/0);
+        if (st) return st;
+        __half *xq16 = static_cast<__half *>(ws);
+        float *xd16 = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + codes16);
+        st = tn::launch_q8_planar_f16(x, x_dtype, x_row_stride, xq16, xd16, M, nb, K, stream);
+        if (st) return st;
+        return tn::launch_q4_gemm(xq16, K, xd16, static_cast<const uint8_t *>(w_blob), bias, y, y_dtype, N, M, N, K,
+                                  stream);
+    }
     // Workspace: codes [M][K] int8, scales [M][nb] f32, offsets [M][nb] f32.
     const size_t codes = (size_t)M * K, scal = (size_t)M * nb * 4;
-    void *ws = nullptr;
-    int st = tn::workspace(&ws, codes + 2 * scal + 256, stream, /*slot=*/0);
+    st = tn::workspace(&ws, codes + 2 * scal + 256, stream, /*slot=*/0);
     if (st) return st;
     int8_t *xq = static_cast<int8_t *>(ws);
     float *xd = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + ((codes + 15) & ~size_t(15)));

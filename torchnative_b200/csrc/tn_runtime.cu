@@ -309,21 +309,32 @@ int tn_reset_counters(void) {
 
 namespace tn {
 
-int encode_map_4d_b16(CUtensorMap *map, const void *base, const uint64_t dims[4], const uint64_t strides_bytes[3],
-                      uint32_t box_rows) {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(int *status) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     static std::mutex mu;
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        if (!encode) {
-            void *fn = nullptr;
-            cudaDriverEntryPointQueryResult q{};
-            cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-            if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
-                return set_error(TN_ERR_CUDA, "tensor map: cuTensorMapEncodeTiled is not available from the driver");
-            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    std::lock_guard<std::mutex> lk(mu);
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+            *status = set_error(TN_ERR_CUDA, "tensor map: cuTensorMapEncodeTiled is not available from the driver");
+            return nullptr;
         }
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
+    return encode;
+}
+
+}  // namespace
+
+int encode_map_4d_b16(CUtensorMap *map, const void *base, const uint64_t dims[4], const uint64_t strides_bytes[3],
+                      uint32_t box_rows) {
+    int st = TN_OK;
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder(&st);
+    if (!encode) return st;
     cuuint64_t gdim[4] = {dims[0], dims[1], dims[2], dims[3]};
     cuuint64_t gstride[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
     cuuint32_t box[4] = {64, box_rows, 1, 1};
@@ -333,6 +344,27 @@ int encode_map_4d_b16(CUtensorMap *map, const void *base, const uint64_t dims[4]
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return set_error(TN_ERR_INVALID, "tensor map: cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
+    return TN_OK;
+}
+
+int encode_map_2d(CUtensorMap *map, const void *base, int elem_bytes, uint64_t inner, uint64_t outer,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+    int st = TN_OK;
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder(&st);
+    if (!encode) return st;
+    const CUtensorMapDataType dt = elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+    cuuint64_t gdim[2] = {inner, outer};
+    cuuint64_t gstride[1] = {row_stride_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult r = encode(map, dt, 2, const_cast<void *>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(TN_ERR_INVALID, "tensor map: cuTensorMapEncodeTiled (2-D) failed with CUresult " +
+                                             std::to_string((int)r));
     return TN_OK;
 }
 
