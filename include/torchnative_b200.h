@@ -299,6 +299,13 @@ TN_API int tn_llama_argmax_embed(const void *logits, int64_t rows, int64_t V, in
 TN_API int tn_llama_embed(const int *tokens, int64_t rows, const void *embed, int64_t H, void *h,
                           void *stream);
 
+/* ---- tensor parallelism (column-sharded linears, KV-head-group attention) -----
+ * The reference has no multi-GPU path; this is the layout step of the
+ * north star's per-layer all-gather: an all-gather of per-rank [rows][cols]
+ * blocks of 16-bit elements lands as src [G][rows][cols]; dst [rows][G*cols]
+ * is what the next layer reads. src and dst must not overlap. */
+TN_API int tn_tp_unshard(const void *src, void *dst, int64_t G, int64_t rows, int64_t cols, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

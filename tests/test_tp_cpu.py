@@ -1,0 +1,114 @@
+"""Tensor-parallel sharding on the CPU (no GPU): world-size-2 gloo ranks each
+take their shard of the Q4_0 weights with torchnative_b200.tp, run the oracle
+(the reference's CPU arithmetic) on it, and all-gather; the gathered rows equal
+the unsharded oracle output bit for bit, because a column shard changes which
+rank computes an output, never how."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import oracle
+from tests import q4_exact
+from torchnative_b200 import tp as tpm
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _blob(rng, n, k) -> torch.Tensor:
+    return torch.frombuffer(bytearray(q4_exact.random_q4_0_blob(rng, n, k)), dtype=torch.uint8)
+
+
+def _gather_np(group, arr: np.ndarray, world: int) -> np.ndarray:
+    """rank-major concatenation along the last axis, through TPGroup.all_gather."""
+    rows, c = arr.shape
+    local = torch.from_numpy(np.ascontiguousarray(arr))
+    full = torch.empty(world * rows * c, dtype=local.dtype)
+    group.all_gather(full, local)
+    return full.view(world, rows, c).permute(1, 0, 2).reshape(rows, world * c).numpy()
+
+
+def _worker(rank, world, port, failures):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = tpm.TPGroup(rank, world, None)
+        rng = np.random.default_rng(5)  # same weights and inputs on every rank
+        B, H, I, Hq, Hkv, D = 2, 256, 512, 8, 4, 32
+        x = rng.standard_normal((B, H)).astype(np.float32)
+        # column-sharded linear (o / down / lm_head)
+        w = _blob(rng, H, H)
+        local = tpm.shard_rows(w, H, H, rank, world)
+        y_l = oracle.q4_0_linear(x, local.numpy().tobytes(), H // world)
+        y = _gather_np(g, y_l, world)
+        assert np.array_equal(y, oracle.q4_0_linear(x, w.numpy().tobytes(), H)), "row shards"
+        # interleaved gate/up pairs
+        gu = _blob(rng, 2 * I, H)
+        gu_l = tpm.shard_gate_up_pairs(gu, I, H, rank, world)
+        full = oracle.q4_0_linear(x, gu.numpy().tobytes(), 2 * I)
+        part = oracle.q4_0_linear(x, gu_l.numpy().tobytes(), 2 * I // world)
+        c = 2 * I // world
+        assert np.array_equal(part, full[:, rank * c:(rank + 1) * c]), "gate/up pairs"
+        # fused q/k/v of this rank's KV-head group, then attention on the local heads
+        n = (Hq + 2 * Hkv) * D
+        qkv = _blob(rng, n, H)
+        qkv_l = tpm.shard_qkv(qkv, Hq, Hkv, D, H, rank, world)
+        full = oracle.q4_0_linear(x, qkv.numpy().tobytes(), n)
+        part = oracle.q4_0_linear(x, qkv_l.numpy().tobytes(), n // world)
+        hq, hkv = Hq // world, Hkv // world
+        q_f, k_f, v_f = full[:, :Hq * D], full[:, Hq * D:(Hq + Hkv) * D], full[:, (Hq + Hkv) * D:]
+        assert np.array_equal(part[:, :hq * D], q_f[:, rank * hq * D:(rank + 1) * hq * D])
+        assert np.array_equal(part[:, hq * D:(hq + hkv) * D], k_f[:, rank * hkv * D:(rank + 1) * hkv * D])
+        assert np.array_equal(part[:, (hq + hkv) * D:], v_f[:, rank * hkv * D:(rank + 1) * hkv * D])
+        S = 40
+        kc = rng.standard_normal((B, Hkv, S, D)).astype(np.float32)
+        vc = rng.standard_normal((B, Hkv, S, D)).astype(np.float32)
+        q = q_f.reshape(B, Hq, 1, D)
+        o_full, _ = oracle.sdpa(q, kc, vc, dtype="float32")
+        o_l, _ = oracle.sdpa(np.ascontiguousarray(q[:, rank * hq:(rank + 1) * hq]),
+                             np.ascontiguousarray(kc[:, rank * hkv:(rank + 1) * hkv]),
+                             np.ascontiguousarray(vc[:, rank * hkv:(rank + 1) * hkv]), dtype="float32")
+        o = _gather_np(g, o_l.reshape(B, hq * D), world)
+        assert np.array_equal(o, o_full.reshape(B, Hq * D)), "KV-head-group attention"
+    except AssertionError as e:
+        failures.put(f"rank {rank}: {e}")
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_rebuild_the_unsharded_outputs():
+    ctx = mp.get_context("spawn")
+    failures = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, failures)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    msgs = []
+    while not failures.empty():
+        msgs.append(failures.get())
+    assert not msgs, msgs
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def test_shard_refusals():
+    w = torch.zeros(10 * 18, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="does not divide"):
+        tpm.shard_rows(w, 10, 32, 0, 4)
+    with pytest.raises(ValueError, match="whole 32-element blocks"):
+        tpm.row_slice(w, 10, 40, 0, 1)
+    with pytest.raises(ValueError, match="is not"):
+        tpm.row_slice(w[:-1], 10, 32, 0, 1)
+    assert tpm.shard_rows(w, 10, 32, 1, 2).numel() == 5 * 18

@@ -1,0 +1,118 @@
+"""Tensor parallelism on the GPU: the layout step of the per-layer all-gather
+(one GPU), and a 2-rank NCCL decode that must produce the single-GPU token
+stream of the same seeded model (skipped with fewer than 2 GPUs)."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(hidden=512, inter=1024, heads=8, kv_heads=4, head_dim=64, vocab=4096, layers=2, rope_theta=10000.0)
+
+
+def test_unshard_is_the_rank_major_transpose(cuda_device):
+    from torchnative_b200 import _native as N, build
+
+    build.build()
+    G, rows, c = 4, 3, 200
+    src = torch.randn(G * rows * c, device=cuda_device).to(torch.bfloat16)
+    dst = torch.empty(rows, G * c, device=cuda_device, dtype=torch.bfloat16)
+    import ctypes
+
+    P = ctypes.c_void_p
+    N.check(N.lib().tn_tp_unshard(P(src.data_ptr()), P(dst.data_ptr()), G, rows, c,
+                                  P(torch.cuda.current_stream().cuda_stream)))
+    want = src.view(G, rows, c).permute(1, 0, 2).reshape(rows, G * c)
+    assert torch.equal(dst, want)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(rank, world, port, batch, steps, out):
+    import datetime
+
+    import torch.distributed as dist
+
+    from torchnative_b200 import build
+    from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
+    from torchnative_b200.tp import TPGroup
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        build.build()
+        shape = LlamaShape(**SMALL)
+        dec = Q4LlamaDecoder(shape, batch=batch, capacity=64, device=f"cuda:{rank}", seed=3,
+                             tp=TPGroup(rank, world, dist.group.WORLD))
+        first = torch.arange(batch, device=f"cuda:{rank}", dtype=torch.int32) * 7 + 1
+        dec.fill_prompt_cache(16)
+        dec.start(first)
+        g = dec.capture()
+        dec.fill_prompt_cache(16)
+        dec.start(first)
+        toks = []
+        for _ in range(steps):
+            g.replay()
+            toks.append(dec.tokens.clone())
+        torch.cuda.synchronize()
+        if rank == 0:
+            out.put(torch.stack(toks).cpu().tolist())
+        # a graph holding NCCL calls must be gone before the process group is
+        dec._graph = None
+        del g, dec
+        torch.cuda.synchronize()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_two_rank_decode_matches_one_gpu(cuda_device, batch):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from torchnative_b200 import build
+    from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
+
+    build.build()
+    steps = 6
+    dec = Q4LlamaDecoder(LlamaShape(**SMALL), batch=batch, capacity=64, device=cuda_device, seed=3)
+    first = torch.arange(batch, device=cuda_device, dtype=torch.int32) * 7 + 1
+    dec.fill_prompt_cache(16)
+    dec.start(first)
+    g = dec.capture()
+    dec.fill_prompt_cache(16)
+    dec.start(first)
+    want = []
+    for _ in range(steps):
+        g.replay()
+        want.append(dec.tokens.clone())
+    want = torch.stack(want).cpu().tolist()
+    dec._graph = None
+    del g, dec
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_run, args=(r, 2, port, batch, steps, out), daemon=True) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        got = out.get(timeout=300)
+        for p in procs:
+            p.join(timeout=120)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    finally:
+        for p in procs:  # never leave a rank behind (it would hold the test process at exit)
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
+    assert got == want

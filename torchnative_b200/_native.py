@@ -70,6 +70,7 @@ SIGNATURES = {
     "tn_llama_rope_append": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64, _P]),
     "tn_llama_argmax_embed": (_I, [_P, _I64, _I64, _P, _P, _I64, _P, _P, _P]),
     "tn_llama_embed": (_I, [_P, _I64, _P, _I64, _P, _P]),
+    "tn_tp_unshard": (_I, [_P, _P, _I64, _I64, _I64, _P]),
 }
 
 _lib = None

@@ -193,6 +193,19 @@ __global__ void embed_kernel(const int *__restrict__ tokens, const __nv_bfloat16
     for (int i = threadIdx.x; i < H; i += blockDim.x) h[(int64_t)row * H + i] = embed[(int64_t)tok * H + i];
 }
 
+// Tensor-parallel gather layout fix: an all-gather of per-rank [rows][c]
+// blocks lands as [G][rows][c]; the next layer reads [rows][G * c].
+__global__ void tp_unshard_kernel(const uint16_t *__restrict__ src, uint16_t *__restrict__ dst, int G, int rows,
+                                  int c) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int64_t n = (int64_t)G * rows * c;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i % c, r = (i / c) % rows, g = i / ((int64_t)c * rows);
+        dst[r * (int64_t)G * c + g * c + j] = src[i];
+    }
+}
+
 template <typename K, typename... Args>
 int launch_pdl(K kernel, dim3 grid, dim3 block, cudaStream_t stream, const char *what, Args... args) {
     cudaLaunchAttribute attr[1];
@@ -259,4 +272,14 @@ extern "C" int tn_llama_embed(const int *tokens, int64_t rows, const void *embed
     if (rows <= 0) return TN_OK;
     return launch_pdl(tn::embed_kernel, dim3((unsigned)rows), dim3(256), (cudaStream_t)stream, "tn_llama_embed",
                       tokens, (const __nv_bfloat16 *)embed, (int)H, (__nv_bfloat16 *)h);
+}
+
+extern "C" int tn_tp_unshard(const void *src, void *dst, int64_t G, int64_t rows, int64_t cols, void *stream) {
+    if (G <= 0 || rows < 0 || cols < 0) return tn::set_error(TN_ERR_SHAPE, "tn_tp_unshard: negative size");
+    if (rows == 0 || cols == 0) return TN_OK;
+    if (!src || !dst || src == dst) return tn::set_error(TN_ERR_INVALID, "tn_tp_unshard: src and dst must be distinct");
+    const int64_t n = G * rows * cols;
+    const unsigned blocks = (unsigned)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184);
+    return launch_pdl(tn::tp_unshard_kernel, dim3(blocks), dim3(256), (cudaStream_t)stream, "tn_tp_unshard",
+                      (const uint16_t *)src, (uint16_t *)dst, (int)G, (int)rows, (int)cols);
 }

@@ -68,19 +68,37 @@ def rope_inv_freq(head_dim: int, theta: float) -> torch.Tensor:
 
 
 class Q4LlamaDecoder:
+    """The decode step on one GPU, or on rank `tp.rank` of a tensor-parallel
+    group (`tp` a torchnative_b200.tp.TPGroup): then every Q4_0 linear holds
+    its column shard, attention its KV-head group, and one all-gather after
+    each sharded output rebuilds the full row (the weights are generated in
+    full from the seed and sliced, so every group size runs the same model)."""
+
     def __init__(self, shape: LlamaShape, batch: int, capacity: int, device, seed: int = 0,
-                 layers: int | None = None):
+                 layers: int | None = None, tp=None):
+        from . import tp as tpm
+
         self.s = shape
         self.B, self.cap = batch, capacity
         self.dev = torch.device(device)
         self.n_layers = shape.layers if layers is None else layers
+        self.tp = tp if tp is not None and tp.world > 1 else None
+        G, r = (self.tp.world, self.tp.rank) if self.tp else (1, 0)
+        self.G = G
         s, dev = shape, self.dev
+        for n, what in ((s.heads, "query heads"), (s.kv_heads, "key/value heads"), (s.hidden, "hidden size"),
+                        (s.inter, "intermediate size"), (s.vocab, "vocabulary")):
+            if n % G != 0:
+                raise ValueError(f"{what} ({n}) does not divide by the tensor-parallel size {G}")
+        self.hq, self.hkv = s.heads // G, s.kv_heads // G   # local heads
+        self.h_l, self.i_l, self.v_l = s.hidden // G, s.inter // G, s.vocab // G
+        self.qkv_l = (self.hq + 2 * self.hkv) * s.head_dim
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
         bf = torch.bfloat16
         self.layers = []
         for _ in range(self.n_layers):
-            self.layers.append({
+            lw = {
                 "attn_norm": (1.0 + 0.1 * torch.randn(s.hidden, device=dev, generator=gen)).to(bf),
                 "qkv": random_q4_blob(s.qkv, s.hidden, gen, dev),
                 "o": random_q4_blob(s.hidden, s.heads * s.head_dim, gen, dev),
@@ -89,11 +107,19 @@ class Q4LlamaDecoder:
                 # row 2i+1 = up_i), so one GEMV writes SiLU(gate) * up directly
                 "gate_up": random_q4_blob(2 * s.inter, s.hidden, gen, dev),
                 "down": random_q4_blob(s.hidden, s.inter, gen, dev),
-            })
+            }
+            if G > 1:
+                lw["qkv"] = tpm.shard_qkv(lw["qkv"], s.heads, s.kv_heads, s.head_dim, s.hidden, r, G)
+                lw["o"] = tpm.shard_rows(lw["o"], s.hidden, s.heads * s.head_dim, r, G)
+                lw["gate_up"] = tpm.shard_gate_up_pairs(lw["gate_up"], s.inter, s.hidden, r, G)
+                lw["down"] = tpm.shard_rows(lw["down"], s.hidden, s.inter, r, G)
+            self.layers.append(lw)
         self.final_norm = (1.0 + 0.1 * torch.randn(s.hidden, device=dev, generator=gen)).to(bf)
         self.lm_head = random_q4_blob(s.vocab, s.hidden, gen, dev)
+        if G > 1:
+            self.lm_head = tpm.shard_rows(self.lm_head, s.vocab, s.hidden, r, G)
         self.embed = (0.02 * torch.randn((s.vocab, s.hidden), device=dev, generator=gen)).to(bf)
-        self.k_cache = [torch.zeros((batch, s.kv_heads, capacity, s.head_dim), device=dev, dtype=bf)
+        self.k_cache = [torch.zeros((batch, self.hkv, capacity, s.head_dim), device=dev, dtype=bf)
                         for _ in range(self.n_layers)]
         self.v_cache = [torch.zeros_like(self.k_cache[0]) for _ in range(self.n_layers)]
         self.inv_freq = rope_inv_freq(s.head_dim, s.rope_theta).to(dev)
@@ -105,11 +131,21 @@ class Q4LlamaDecoder:
         self.codes = torch.zeros((B, kmax), device=dev, dtype=torch.int8)
         self.scales = torch.zeros((B, kmax // 32), device=dev, dtype=torch.float32)
         self.offsets = torch.zeros((B, kmax // 32), device=dev, dtype=torch.float32)
-        self.qkv_out = torch.zeros((B, s.qkv), device=dev, dtype=bf)
-        self.q_rot = torch.zeros((B, s.heads, 1, s.head_dim), device=dev, dtype=bf)
+        self.qkv_out = torch.zeros((B, self.qkv_l), device=dev, dtype=bf)
+        self.q_rot = torch.zeros((B, self.hq, 1, s.head_dim), device=dev, dtype=bf)
         self.attn = torch.zeros((B, s.heads, 1, s.head_dim), device=dev, dtype=bf)
         self.act = torch.zeros((B, I), device=dev, dtype=bf)
         self.logits = torch.zeros((B, s.vocab), device=dev, dtype=bf)
+        if G > 1:  # each rank's slice of the sharded outputs, gathered into the full buffers above
+            self.attn_l = torch.zeros((B, self.hq, 1, s.head_dim), device=dev, dtype=bf)
+            self.delta_l = torch.zeros((B, self.h_l), device=dev, dtype=bf)
+            self.act_l = torch.zeros((B, self.i_l), device=dev, dtype=bf)
+            self.logits_l = torch.zeros((B, self.v_l), device=dev, dtype=bf)
+            self.gather_scratch = torch.zeros(G * B * max(self.h_l, self.i_l, self.v_l, self.hq * s.head_dim),
+                                              device=dev, dtype=bf)
+        else:
+            self.attn_l, self.delta_l, self.act_l, self.logits_l = self.attn, self.delta, self.act, self.logits
+            self.gather_scratch = None
         self.tokens = torch.zeros(B, device=dev, dtype=torch.int32)
         self.pos = torch.zeros(1, device=dev, dtype=torch.int32)
         st = lambda t: (ctypes.c_int64 * 4)(*[0 if t.shape[i] == 1 and i < 3 else t.stride(i) for i in range(4)])  # noqa: E731
@@ -122,35 +158,52 @@ class Q4LlamaDecoder:
         # use the separate kernels.
         self.fused = batch <= 4
 
+    def _gather(self, local: torch.Tensor, full: torch.Tensor, stream) -> None:
+        """The all-gather after a sharded output (nothing on one GPU)."""
+        if self.tp is None:
+            return
+        from . import tp as tpm
+
+        tpm.gather_rows(self.tp, local.reshape(self.B, -1), full.view(self.B, -1), self.gather_scratch, stream)
+
     # ---- bookkeeping
 
     @property
     def weight_bytes(self) -> int:
-        s = self.s
-        per_layer = (q4_bytes(s.qkv, s.hidden) + q4_bytes(s.hidden, s.heads * s.head_dim) +
-                     q4_bytes(2 * s.inter, s.hidden) + q4_bytes(s.hidden, s.inter) + 2 * 2 * s.hidden)
-        return per_layer * self.n_layers + q4_bytes(s.vocab, s.hidden) + 2 * s.hidden
+        """HBM bytes of this rank's weights read per step (its shards, plus the
+        replicated norms)."""
+        s, G = self.s, self.G
+        per_layer = (q4_bytes(self.qkv_l, s.hidden) + q4_bytes(self.h_l, s.heads * s.head_dim) +
+                     q4_bytes(2 * self.i_l, s.hidden) + q4_bytes(self.h_l, s.inter) + 2 * 2 * s.hidden)
+        return per_layer * self.n_layers + q4_bytes(self.v_l, s.hidden) + 2 * s.hidden
 
     def kv_bytes(self, length: int) -> int:
         s = self.s
-        return 2 * self.n_layers * self.B * s.kv_heads * length * s.head_dim * 2
+        return 2 * self.n_layers * self.B * self.hkv * length * s.head_dim * 2
 
     @property
     def kernels_per_layer(self) -> int:
-        return 6 if self.fused else 11
+        """Our kernels per layer (the all-gathers are NCCL's)."""
+        unshard = 4 if (self.tp is not None and self.B > 1) else 0
+        return (6 if self.fused else 11) + unshard
 
     @property
     def kernels_per_step(self) -> int:
-        return self.kernels_per_layer * self.n_layers + (2 if self.fused else 3)
+        unshard = 1 if (self.tp is not None and self.B > 1) else 0
+        return self.kernels_per_layer * self.n_layers + (2 if self.fused else 3) + unshard
 
     def fill_prompt_cache(self, length: int, seed: int = 1) -> None:
         """The prompt's K/V: synthetic N(0,1) values in slots [0, length), and
         the position set to `length` (the decode loop continues from there)."""
         g = torch.Generator(device=self.dev)
         g.manual_seed(seed)
+        s = self.s
+        h0 = (self.tp.rank if self.tp else 0) * self.hkv  # this rank's KV heads of the full cache
         for kc, vc in zip(self.k_cache, self.v_cache):
-            kc[:, :, :length].normal_(generator=g)
-            vc[:, :, :length].normal_(generator=g)
+            for c in (kc, vc):
+                full = torch.empty((self.B, s.kv_heads, length, s.head_dim), device=self.dev, dtype=c.dtype)
+                full.normal_(generator=g)
+                c[:, :, :length].copy_(full[:, h0:h0 + self.hkv])
         self.pos.fill_(length)
 
     def start(self, tokens: torch.Tensor) -> None:
@@ -184,30 +237,36 @@ class Q4LlamaDecoder:
             return self._step_fused(stream or self._stream())
         L, s, B = N.lib(), self.s, self.B
         stream = stream or self._stream()
-        D, Hq, Hkv = s.head_dim, s.heads, s.kv_heads
+        D, Hq, Hkv = s.head_dim, self.hq, self.hkv  # local heads
         for li, lw in enumerate(self.layers):
             self._norm(None if li == 0 else self.delta, lw["attn_norm"], stream)
-            self._linear(lw["qkv"], self.qkv_out, s.qkv, s.hidden, stream)
+            self._linear(lw["qkv"], self.qkv_out, self.qkv_l, s.hidden, stream)
             kc, vc = self.k_cache[li], self.v_cache[li]
             N.check(L.tn_llama_rope_append(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()),
                                            P(self.pos.data_ptr()), 0, B, Hq, Hkv, D, P(self.q_rot.data_ptr()),
                                            P(kc.data_ptr()), P(vc.data_ptr()), kc.stride(0), kc.stride(1), stream))
             N.check(L.tn_sdpa_decode_cache(P(self.q_rot.data_ptr()), P(kc.data_ptr()), P(vc.data_ptr()),
-                                           P(self.attn.data_ptr()), None, N.TN_BF16, B, Hq, Hkv, D, self.cap,
+                                           P(self.attn_l.data_ptr()), None, N.TN_BF16, B, Hq, Hkv, D, self.cap,
                                            self._qstr, self._kstr, self._kstr, P(self.pos.data_ptr()), 1,
                                            1.0 / math.sqrt(D), stream))
-            N.check(L.tn_q8_0_quantize_planar(P(self.attn.data_ptr()), N.TN_BF16, Hq * D, P(self.codes.data_ptr()),
-                                              Hq * D, P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B,
-                                              Hq * D, stream))
-            self._linear(lw["o"], self.delta, s.hidden, Hq * D, stream)
+            self._gather(self.attn_l, self.attn, stream)
+            HD = s.heads * D
+            N.check(L.tn_q8_0_quantize_planar(P(self.attn.data_ptr()), N.TN_BF16, HD, P(self.codes.data_ptr()),
+                                              HD, P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, HD,
+                                              stream))
+            self._linear(lw["o"], self.delta_l, self.h_l, HD, stream)
+            self._gather(self.delta_l, self.delta, stream)
             self._norm(self.delta, lw["mlp_norm"], stream)
-            self._linear(lw["gate_up"], self.act, 2 * s.inter, s.hidden, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS)
+            self._linear(lw["gate_up"], self.act_l, 2 * self.i_l, s.hidden, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS)
+            self._gather(self.act_l, self.act, stream)
             N.check(L.tn_q8_0_quantize_planar(P(self.act.data_ptr()), N.TN_BF16, s.inter, P(self.codes.data_ptr()),
                                               s.inter, P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B,
                                               s.inter, stream))
-            self._linear(lw["down"], self.delta, s.hidden, s.inter, stream)
+            self._linear(lw["down"], self.delta_l, self.h_l, s.inter, stream)
+            self._gather(self.delta_l, self.delta, stream)
         self._norm(self.delta, self.final_norm, stream)
-        self._linear(self.lm_head, self.logits, s.vocab, s.hidden, stream)
+        self._linear(self.lm_head, self.logits_l, self.v_l, s.hidden, stream)
+        self._gather(self.logits_l, self.logits, stream)
         N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
                                         P(self.embed.data_ptr()), s.hidden, P(self.h.data_ptr()),
                                         P(self.pos.data_ptr()), stream))
@@ -222,29 +281,35 @@ class Q4LlamaDecoder:
 
     def _step_fused(self, stream) -> None:
         L, s, B = N.lib(), self.s, self.B
-        D, Hq, Hkv, H, I = s.head_dim, s.heads, s.kv_heads, s.hidden, s.inter
+        D, Hq, Hkv, H, I = s.head_dim, self.hq, self.hkv, s.hidden, s.inter  # local heads
+        HD = s.heads * D
         ha, hb = self.h, self.h2
         for li, lw in enumerate(self.layers):
             # residual: hb = ha + (previous layer's down_proj); qkv = Q4(RMSNorm(hb))
             self._fused_linear(N.TN_X_RMSNORM, ha, H, None if li == 0 else self.delta, hb, lw["attn_norm"],
-                               lw["qkv"], self.qkv_out, s.qkv, H, stream)
+                               lw["qkv"], self.qkv_out, self.qkv_l, H, stream)
             kc, vc = self.k_cache[li], self.v_cache[li]
             N.check(L.tn_sdpa_decode_step(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()), P(kc.data_ptr()),
-                                          P(vc.data_ptr()), P(self.attn.data_ptr()), None, B, Hq, Hkv, D, self.cap,
+                                          P(vc.data_ptr()), P(self.attn_l.data_ptr()), None, B, Hq, Hkv, D, self.cap,
                                           self._kstr, self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D),
                                           stream))
-            self._fused_linear(N.TN_X_BF16, self.attn, Hq * D, None, None, None, lw["o"], self.delta, H, Hq * D,
+            self._gather(self.attn_l, self.attn, stream)
+            self._fused_linear(N.TN_X_BF16, self.attn, HD, None, None, None, lw["o"], self.delta_l, self.h_l, HD,
                                stream)
+            self._gather(self.delta_l, self.delta, stream)
             # residual: ha = hb + o_proj; act = SiLU(gate) * up of Q4(RMSNorm(ha))
-            self._fused_linear(N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act,
-                               2 * I, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS)
+            self._fused_linear(N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act_l,
+                               2 * self.i_l, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS)
+            self._gather(self.act_l, self.act, stream)
             # the activation quantiser once (not in each of the down GEMV's CTAs:
             # 448 blocks per CTA cost more than a launch), then the planar GEMV
             N.check(L.tn_q8_0_quantize_planar(P(self.act.data_ptr()), N.TN_BF16, I, P(self.codes.data_ptr()), I,
                                               P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, I, stream))
-            self._linear(lw["down"], self.delta, H, I, stream)
-        self._fused_linear(N.TN_X_RMSNORM, ha, H, self.delta, hb, self.final_norm, self.lm_head, self.logits,
-                           s.vocab, H, stream)
+            self._linear(lw["down"], self.delta_l, self.h_l, I, stream)
+            self._gather(self.delta_l, self.delta, stream)
+        self._fused_linear(N.TN_X_RMSNORM, ha, H, self.delta, hb, self.final_norm, self.lm_head, self.logits_l,
+                           self.v_l, H, stream)
+        self._gather(self.logits_l, self.logits, stream)
         N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
                                         P(self.embed.data_ptr()), s.hidden, P(ha.data_ptr()),
                                         P(self.pos.data_ptr()), stream))
@@ -254,7 +319,7 @@ class Q4LlamaDecoder:
         the fused step, each running that launch once per layer with the
         step's own arguments (so 32 back-to-back launches over 32 layers'
         weights). Reads and writes the step's buffers; re-seed afterwards."""
-        if not self.fused:
+        if not self.fused or self.tp is not None:
             return {}
         L, s, B = N.lib(), self.s, self.B
         D, Hq, Hkv, H, I = s.head_dim, s.heads, s.kv_heads, s.hidden, s.inter

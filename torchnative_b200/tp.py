@@ -1,0 +1,118 @@
+"""Tensor parallelism for the Q4_0 decode step: the load-time sharding hook and
+the per-layer all-gather.
+
+Across G GPUs of one box the path is split only where it shards by itself:
+
+* every Q4_0 linear is column-sharded along N (its output features). A GGML
+  Q4_0 row is K/32 whole 18-byte blocks, so rank r's rows [r N/G, (r+1) N/G)
+  are one contiguous byte slice of the blob -- no re-quantisation, the same
+  bytes `_quantized_to` (torch_c/src/quant.rs:384-405) would move;
+* attention is split by KV-head group: rank r owns KV heads
+  [r Hkv/G, (r+1) Hkv/G) and the Hq/Hkv query heads that read each of them
+  (the GQA map of aten.rs:17106-17130), so no exchange is needed inside
+  attention. The fused q/k/v weight is sliced per section (q rows, k rows,
+  v rows) so the local projection has the same [q | k | v] layout;
+* after each sharded linear one NCCL all-gather over NVLink/NVSwitch
+  rebuilds the full activation row on every rank (4 per layer: attention
+  output, o_proj, SiLU(gate)*up, down_proj; plus the lm_head logits), and the
+  replicated parts (residual, RMSNorm, argmax) run on every rank.
+
+The reference has no multi-GPU path; the hook sits where its model-load path
+adopts quantised weights (torchnative/python/torchnative/quant/hf.py:340 and
+quant/__init__.py:183-237).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as N
+
+P = ctypes.c_void_p
+
+
+def q4_row_bytes(k: int) -> int:
+    if k % 32 != 0:
+        raise ValueError(f"a q4_0 row is whole 32-element blocks, got in_features {k}")
+    return k // 32 * 18
+
+
+def row_slice(blob: torch.Tensor, n: int, k: int, start: int, stop: int) -> torch.Tensor:
+    """Rows [start, stop) of an [n, k] Q4_0 blob (uint8, flat) as a new
+    contiguous blob."""
+    rb = q4_row_bytes(k)
+    if blob.numel() != n * rb:
+        raise ValueError(f"q4_0 blob of {blob.numel()} bytes is not [{n}, {k}] ({n * rb} bytes)")
+    if not 0 <= start <= stop <= n:
+        raise ValueError(f"row range [{start}, {stop}) outside [0, {n})")
+    return blob[start * rb:stop * rb].clone()
+
+
+def _split(n: int, world: int, what: str) -> int:
+    if n % world != 0:
+        raise ValueError(f"{what} ({n}) does not divide by the tensor-parallel size {world}")
+    return n // world
+
+
+def shard_rows(blob: torch.Tensor, n: int, k: int, rank: int, world: int) -> torch.Tensor:
+    """Column-sharded linear: rank r's output features [r n/G, (r+1) n/G)."""
+    c = _split(n, world, "out_features")
+    return row_slice(blob, n, k, rank * c, (rank + 1) * c)
+
+
+def shard_qkv(blob: torch.Tensor, heads: int, kv_heads: int, head_dim: int, k: int, rank: int,
+              world: int) -> torch.Tensor:
+    """The fused [q | k | v] projection of rank r's KV-head group: query heads
+    [r Hq/G, (r+1) Hq/G), key and value heads [r Hkv/G, (r+1) Hkv/G)."""
+    hq, hkv = _split(heads, world, "query heads"), _split(kv_heads, world, "key/value heads")
+    n = (heads + 2 * kv_heads) * head_dim
+    q0 = rank * hq * head_dim
+    k0 = heads * head_dim + rank * hkv * head_dim
+    v0 = (heads + kv_heads) * head_dim + rank * hkv * head_dim
+    return torch.cat([row_slice(blob, n, k, q0, q0 + hq * head_dim),
+                      row_slice(blob, n, k, k0, k0 + hkv * head_dim),
+                      row_slice(blob, n, k, v0, v0 + hkv * head_dim)])
+
+
+def shard_gate_up_pairs(blob: torch.Tensor, inter: int, k: int, rank: int, world: int) -> torch.Tensor:
+    """gate/up interleaved row by row (2i = gate_i, 2i+1 = up_i): rank r's
+    pairs [r I/G, (r+1) I/G) are rows [2 r I/G, 2 (r+1) I/G)."""
+    c = _split(inter, world, "intermediate size")
+    return row_slice(blob, 2 * inter, k, 2 * rank * c, 2 * (rank + 1) * c)
+
+
+@dataclass
+class TPGroup:
+    """One tensor-parallel group: this process's rank, the group size and the
+    torch.distributed process group (NCCL on GPUs, gloo in CPU tests)."""
+    rank: int
+    world: int
+    group: object = None
+
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        """out = concatenation over ranks of inp (rank-major). NCCL: one
+        all_gather_into_tensor on the current stream (captured with the step
+        inside a CUDA-graph capture); gloo (CPU tests): the list form."""
+        import torch.distributed as dist
+
+        if dist.get_backend(self.group) == "gloo":
+            parts = list(out.view(self.world, -1).unbind(0))
+            dist.all_gather(parts, inp.reshape(-1), group=self.group)
+            return
+        dist.all_gather_into_tensor(out, inp, group=self.group)
+
+
+def gather_rows(tp: TPGroup, local: torch.Tensor, full: torch.Tensor, scratch: torch.Tensor | None,
+                stream) -> None:
+    """full[b] = concat over ranks of rank r's local[b] ([rows, c] each, 16-bit
+    elements): one all-gather, plus the layout step when rows > 1."""
+    rows, c = local.shape
+    if rows == 1:
+        tp.all_gather(full.view(-1), local.view(-1))
+        return
+    buf = scratch.view(-1)[:tp.world * rows * c]
+    tp.all_gather(buf, local.reshape(-1))
+    N.check(N.lib().tn_tp_unshard(P(buf.data_ptr()), P(full.data_ptr()), tp.world, rows, c, stream))
