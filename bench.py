@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--shape", default=None, help="one N,K for --case gemv (default: BASELINE's four shapes)")
     ap.add_argument("--batch", type=int, default=1, help="sequences decoded together (BASELINE: 1 and 16)")
     ap.add_argument("--seqs", default="512,4096,16384", help="sequence lengths for --case sdpa_prefill")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="tensor-parallel all-gather: peer-memory kernel or NCCL")
     return ap.parse_args()
 
 
@@ -253,7 +255,7 @@ def run_ours(args, rank, world, local):
         from torchnative_b200.tp import TPGroup
 
         tp = TPGroup(rank, world, dist.group.WORLD)
-    dec = Q4LlamaDecoder(LLAMA3_8B, batch=B, capacity=cap, device=dev, seed=1234, tp=tp)
+    dec = Q4LlamaDecoder(LLAMA3_8B, batch=B, capacity=cap, device=dev, seed=1234, tp=tp, exchange=args.exchange)
     P = ctypes.c_void_p
     cur = lambda: P(torch.cuda.current_stream().cuda_stream)  # noqa: E731
     first = torch.randint(0, LLAMA3_8B.vocab, (B,), device=dev, dtype=torch.int32)
@@ -367,8 +369,9 @@ def run_ours(args, rank, world, local):
                                "growing one slot per step; one CUDA graph per token",
                    "model": "Llama-3-8B-shaped (32 layers, 4096 hidden, 32/8 heads, D 128, MLP 14336, vocab 128256)",
                    "global_batch": B, "seq_len": PROMPT,
-                   "parallelism": f"tp{world} (column-sharded Q4_0 linears, KV-head-group attention, NCCL all-gather "
-                                  "after each sharded output)" if world > 1 else "tp1",
+                   "parallelism": f"tp{world} (column-sharded Q4_0 linears, KV-head-group attention, "
+                                  f"{'peer-memory' if args.exchange == 'p2p' else 'NCCL'} all-gather after each "
+                                  "sharded output)" if world > 1 else "tp1",
                    "l2": "inputs larger than L2 (4.22 GB of weights per step)",
                    "mean_context": mean_ctx, "bytes_per_step": step_bytes,
                    "hbm_roofline_tok_s": B * peak * 1e9 / step_bytes},
@@ -383,10 +386,13 @@ def run_ours(args, rank, world, local):
         "gpu_launches": dec.kernels_per_step * args.steps,
         "clocks": clocks.summary(),
     }
-    # graphs holding NCCL calls go before the process group does
+    # graphs holding NCCL calls go before the process group does; no rank frees
+    # its exchange region while a peer may still write it
     dec._graph = None
     del g, gd
     torch.cuda.synchronize()
+    barrier(world)
+    dec.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         blobs = {"qkv": dec.layers[0]["qkv"].cpu().numpy(), "o": dec.layers[0]["o"].cpu().numpy(),
                  "gate_up": dec.layers[0]["gate_up"].cpu().numpy(), "down": dec.layers[0]["down"].cpu().numpy()}

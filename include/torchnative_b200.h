@@ -306,6 +306,32 @@ TN_API int tn_llama_embed(const int *tokens, int64_t rows, const void *embed, in
  * is what the next layer reads. src and dst must not overlap. */
 TN_API int tn_tp_unshard(const void *src, void *dst, int64_t G, int64_t rows, int64_t cols, void *stream);
 
+/* The same all-gather over peer memory (NVLink / NVSwitch) instead of a
+ * library collective. Each rank allocates one exchange region (zeroed; its
+ * first tn_tp_region_data_offset() bytes hold the step epoch and the
+ * per-gather counters) and shares it through a CUDA IPC handle of
+ * TN_IPC_HANDLE_BYTES bytes; every other rank opens it. tn_tp_allgather then
+ * stores this rank's [rows][cols] slice of 16-bit elements (local, row stride
+ * local_row_stride elements) into row r, columns [rank*cols, (rank+1)*cols)
+ * of the [rows][dst_row_stride] buffer at byte `dst_offset` of every rank's
+ * data area, signals, and returns (in stream order) once every rank's slice
+ * has arrived in this rank's region. `slot` numbers the gathers of one step
+ * (each used once per step; consecutive gathers must use different buffers);
+ * tn_tp_step_end advances the epoch after the step's last gather. bases[g] is
+ * rank g's region as mapped in this process (its own base for g == rank).
+ * Waits are bounded: a rank that never signals makes the call record
+ * TN_ERR_TIMEOUT for tn_device_status instead of hanging. */
+#define TN_IPC_HANDLE_BYTES 64
+TN_API int tn_tp_region_alloc(size_t bytes, void **base, void *ipc_handle);
+TN_API int tn_tp_region_open(const void *ipc_handle, void **peer_base);
+TN_API int tn_tp_region_close(void *peer_base);
+TN_API int tn_tp_region_free(void *base);
+TN_API int64_t tn_tp_region_data_offset(void);
+TN_API int tn_tp_allgather(void *const *bases, int rank, int world, const void *local, int64_t local_row_stride,
+                           int64_t rows, int64_t cols, int64_t dst_offset, int64_t dst_row_stride, int slot,
+                           void *stream);
+TN_API int tn_tp_step_end(void *local_base, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -2,6 +2,7 @@
 (one GPU), and a 2-rank NCCL decode that must produce the single-GPU token
 stream of the same seeded model (skipped with fewer than 2 GPUs)."""
 
+import ctypes
 import os
 import socket
 
@@ -30,13 +31,85 @@ def test_unshard_is_the_rank_major_transpose(cuda_device):
     assert torch.equal(dst, want)
 
 
+def _gather_worker(rank, world, port, out):
+    """Each rank's slice holds (rank, row, column) codes; after every gather
+    each rank's region holds all slices at their columns, for several steps."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from torchnative_b200 import _native as N, build
+    from torchnative_b200.tp import PeerExchange, TPGroup
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        build.build()
+        dev = torch.device("cuda", rank)
+        rows, c = 3, 40
+        x = PeerExchange(TPGroup(rank, world, dist.group.WORLD), 2 * rows * c * world * 2 + 1024, dev)
+        full_a, off_a = x.buffer(rows, world * c, torch.int16)
+        full_b, off_b = x.buffer(rows, world * c, torch.int16)
+        ok, detail = True, ""
+        s = torch.cuda.current_stream().cuda_stream
+        for step in range(3):
+            for k, (full, off) in enumerate(((full_a, off_a), (full_b, off_b))):
+                r_i = torch.arange(rows, device=dev).view(rows, 1)
+                c_i = torch.arange(c, device=dev).view(1, c)
+                local = (1000 * (rank + 1) + 100 * k + 10 * step + r_i * c + c_i).to(torch.int16)
+                x.allgather(local, off, world * c, ctypes.c_void_p(s))
+                torch.cuda.synchronize()
+                want = torch.cat([(1000 * (g + 1) + 100 * k + 10 * step + r_i * c + c_i).to(torch.int16)
+                                  for g in range(world)], dim=1)
+                if ok and not torch.equal(full, want):
+                    ok, detail = False, f"step {step} buffer {k}: got {full.tolist()} want {want.tolist()}"
+            x.step_end(ctypes.c_void_p(s))
+        try:
+            N.device_status(reset=True)
+            st = "ok"
+        except Exception as e:  # a bounded wait that gave up
+            st = str(e)
+        if rank == 0:
+            out.put((ok, detail, st))
+        torch.cuda.synchronize()
+        dist.barrier()
+        x.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_allgather_two_ranks(cuda_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, out), daemon=True) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        ok, detail, st = out.get(timeout=300)
+        for p in procs:
+            p.join(timeout=120)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
+    assert st == "ok", st
+    assert ok, detail
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _run(rank, world, port, batch, steps, out):
+def _run(rank, world, port, batch, steps, exchange, out):
     import datetime
 
     import torch.distributed as dist
@@ -53,7 +126,7 @@ def _run(rank, world, port, batch, steps, out):
         build.build()
         shape = LlamaShape(**SMALL)
         dec = Q4LlamaDecoder(shape, batch=batch, capacity=64, device=f"cuda:{rank}", seed=3,
-                             tp=TPGroup(rank, world, dist.group.WORLD))
+                             tp=TPGroup(rank, world, dist.group.WORLD), exchange=exchange)
         first = torch.arange(batch, device=f"cuda:{rank}", dtype=torch.int32) * 7 + 1
         dec.fill_prompt_cache(16)
         dec.start(first)
@@ -67,17 +140,20 @@ def _run(rank, world, port, batch, steps, out):
         torch.cuda.synchronize()
         if rank == 0:
             out.put(torch.stack(toks).cpu().tolist())
-        # a graph holding NCCL calls must be gone before the process group is
+        # a graph holding NCCL calls must be gone before the process group is,
+        # and no rank may free its exchange region while a peer still writes it
         dec._graph = None
-        del g, dec
+        del g
         torch.cuda.synchronize()
         dist.barrier()
+        dec.close()
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
 @pytest.mark.parametrize("batch", [1, 2])
-def test_two_rank_decode_matches_one_gpu(cuda_device, batch):
+def test_two_rank_decode_matches_one_gpu(cuda_device, batch, exchange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from torchnative_b200 import build
@@ -102,7 +178,7 @@ def test_two_rank_decode_matches_one_gpu(cuda_device, batch):
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, 2, port, batch, steps, out), daemon=True) for r in range(2)]
+    procs = [ctx.Process(target=_run, args=(r, 2, port, batch, steps, exchange, out), daemon=True) for r in range(2)]
     for p in procs:
         p.start()
     try:

@@ -71,6 +71,13 @@ SIGNATURES = {
     "tn_llama_argmax_embed": (_I, [_P, _I64, _I64, _P, _P, _I64, _P, _P, _P]),
     "tn_llama_embed": (_I, [_P, _I64, _P, _I64, _P, _P]),
     "tn_tp_unshard": (_I, [_P, _P, _I64, _I64, _I64, _P]),
+    "tn_tp_region_alloc": (_I, [ctypes.c_size_t, _P, _P]),
+    "tn_tp_region_open": (_I, [_P, _P]),
+    "tn_tp_region_close": (_I, [_P]),
+    "tn_tp_region_free": (_I, [_P]),
+    "tn_tp_region_data_offset": (_I64, []),
+    "tn_tp_allgather": (_I, [_P, _I, _I, _P, _I64, _I64, _I64, _I64, _I64, _I, _P]),
+    "tn_tp_step_end": (_I, [_P, _P]),
 }
 
 _lib = None

@@ -75,7 +75,7 @@ class Q4LlamaDecoder:
     full from the seed and sliced, so every group size runs the same model)."""
 
     def __init__(self, shape: LlamaShape, batch: int, capacity: int, device, seed: int = 0,
-                 layers: int | None = None, tp=None):
+                 layers: int | None = None, tp=None, exchange: str = "p2p"):
         from . import tp as tpm
 
         self.s = shape
@@ -127,15 +127,32 @@ class Q4LlamaDecoder:
         kmax = max(H, I, s.heads * s.head_dim)
         self.h = torch.zeros((B, H), device=dev, dtype=bf)
         self.h2 = torch.zeros((B, H), device=dev, dtype=bf)  # the residual's other half (ping-pong)
-        self.delta = torch.zeros((B, H), device=dev, dtype=bf)
+        # Gather destinations: with the peer-memory exchange they live in this
+        # rank's IPC region, where every rank writes its slice directly.
+        self.xchg = None
+        if self.tp is not None and exchange == "p2p":
+            nbytes = 2 * B * (s.heads * s.head_dim + H + I + s.vocab) + 4 * 256
+            self.xchg = tpm.PeerExchange(self.tp, nbytes, dev)
+            attn2d, self._off_attn = self.xchg.buffer(B, s.heads * s.head_dim)
+            self.attn = attn2d.view(B, s.heads, 1, s.head_dim)
+            self.delta, self._off_delta = self.xchg.buffer(B, H)
+            self.act, self._off_act = self.xchg.buffer(B, I)
+            self.logits, self._off_logits = self.xchg.buffer(B, s.vocab)
+            for t in (self.attn, self.delta, self.act, self.logits):
+                t.zero_()
+        elif self.tp is not None and exchange != "nccl":
+            raise ValueError(f"unknown exchange {exchange!r} (p2p or nccl)")
+        else:
+            self.delta = torch.zeros((B, H), device=dev, dtype=bf)
         self.codes = torch.zeros((B, kmax), device=dev, dtype=torch.int8)
         self.scales = torch.zeros((B, kmax // 32), device=dev, dtype=torch.float32)
         self.offsets = torch.zeros((B, kmax // 32), device=dev, dtype=torch.float32)
         self.qkv_out = torch.zeros((B, self.qkv_l), device=dev, dtype=bf)
         self.q_rot = torch.zeros((B, self.hq, 1, s.head_dim), device=dev, dtype=bf)
-        self.attn = torch.zeros((B, s.heads, 1, s.head_dim), device=dev, dtype=bf)
-        self.act = torch.zeros((B, I), device=dev, dtype=bf)
-        self.logits = torch.zeros((B, s.vocab), device=dev, dtype=bf)
+        if self.xchg is None:
+            self.attn = torch.zeros((B, s.heads, 1, s.head_dim), device=dev, dtype=bf)
+            self.act = torch.zeros((B, I), device=dev, dtype=bf)
+            self.logits = torch.zeros((B, s.vocab), device=dev, dtype=bf)
         if G > 1:  # each rank's slice of the sharded outputs, gathered into the full buffers above
             self.attn_l = torch.zeros((B, self.hq, 1, s.head_dim), device=dev, dtype=bf)
             self.delta_l = torch.zeros((B, self.h_l), device=dev, dtype=bf)
@@ -162,9 +179,27 @@ class Q4LlamaDecoder:
         """The all-gather after a sharded output (nothing on one GPU)."""
         if self.tp is None:
             return
+        local2d, full2d = local.reshape(self.B, -1), full.view(self.B, -1)
+        if self.xchg is not None:
+            off = {self.attn.data_ptr(): self._off_attn, self.delta.data_ptr(): self._off_delta,
+                   self.act.data_ptr(): self._off_act, self.logits.data_ptr(): self._off_logits}[full.data_ptr()]
+            self.xchg.allgather(local2d, off, full2d.shape[1], stream)
+            return
         from . import tp as tpm
 
-        tpm.gather_rows(self.tp, local.reshape(self.B, -1), full.view(self.B, -1), self.gather_scratch, stream)
+        tpm.gather_rows(self.tp, local2d, full2d, self.gather_scratch, stream)
+
+    def _step_end(self, stream) -> None:
+        if self.xchg is not None:
+            self.xchg.step_end(stream)
+
+    def close(self) -> None:
+        """Release the peer-memory exchange (call on every rank after a
+        barrier, with no step in flight and no graph left that uses it)."""
+        self._graph = None
+        if self.xchg is not None:
+            self.xchg.close()
+            self.xchg = None
 
     # ---- bookkeeping
 
@@ -183,14 +218,21 @@ class Q4LlamaDecoder:
 
     @property
     def kernels_per_layer(self) -> int:
-        """Our kernels per layer (the all-gathers are NCCL's)."""
-        unshard = 4 if (self.tp is not None and self.B > 1) else 0
-        return (6 if self.fused else 11) + unshard
+        """Our kernels per layer: the peer-memory all-gathers are ours, NCCL's
+        are not (they add the layout step at batch > 1)."""
+        if self.xchg is not None:
+            extra = 4
+        else:
+            extra = 4 if (self.tp is not None and self.B > 1) else 0
+        return (6 if self.fused else 11) + extra
 
     @property
     def kernels_per_step(self) -> int:
-        unshard = 1 if (self.tp is not None and self.B > 1) else 0
-        return self.kernels_per_layer * self.n_layers + (2 if self.fused else 3) + unshard
+        if self.xchg is not None:
+            extra = 2  # the logits gather and the epoch step
+        else:
+            extra = 1 if (self.tp is not None and self.B > 1) else 0
+        return self.kernels_per_layer * self.n_layers + (2 if self.fused else 3) + extra
 
     def fill_prompt_cache(self, length: int, seed: int = 1) -> None:
         """The prompt's K/V: synthetic N(0,1) values in slots [0, length), and
@@ -270,6 +312,7 @@ class Q4LlamaDecoder:
         N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
                                         P(self.embed.data_ptr()), s.hidden, P(self.h.data_ptr()),
                                         P(self.pos.data_ptr()), stream))
+        self._step_end(stream)
 
     def _fused_linear(self, mode, x, x_stride, delta, h_out, norm_w, w, y, n, k, stream, flags=0):
         N.check(N.lib().tn_q4_0_linear_fused(mode, P(x.data_ptr()), x_stride,
@@ -313,6 +356,7 @@ class Q4LlamaDecoder:
         N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
                                         P(self.embed.data_ptr()), s.hidden, P(ha.data_ptr()),
                                         P(self.pos.data_ptr()), stream))
+        self._step_end(stream)
 
     def kernel_graphs(self) -> dict:
         """For timing the step's parts: one CUDA graph per kind of launch in

@@ -116,3 +116,77 @@ def gather_rows(tp: TPGroup, local: torch.Tensor, full: torch.Tensor, scratch: t
     buf = scratch.view(-1)[:tp.world * rows * c]
     tp.all_gather(buf, local.reshape(-1))
     N.check(N.lib().tn_tp_unshard(P(buf.data_ptr()), P(full.data_ptr()), tp.world, rows, c, stream))
+
+
+class _DevicePointer:
+    """A raw device pointer presented through the CUDA array interface, so
+    torch can view memory this library allocated (16-bit elements as int16)."""
+
+    def __init__(self, ptr: int, numel: int):
+        self.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<i2", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerExchange:
+    """This rank's exchange region and its peers' (CUDA IPC, plain peer
+    mappings), for tn_tp_allgather. Buffers handed out by `buffer()` are the
+    gather destinations: every rank writes its slice of them directly."""
+
+    def __init__(self, tp: TPGroup, nbytes: int, device):
+        import torch.distributed as dist
+
+        self.tp, self.dev = tp, torch.device(device)
+        lib = N.lib()
+        handle = (ctypes.c_uint8 * 64)()
+        base = ctypes.c_void_p()
+        N.check(lib.tn_tp_region_alloc(nbytes, ctypes.byref(base), handle))
+        self.base = base.value
+        self.nbytes = nbytes
+        self.data_off = int(lib.tn_tp_region_data_offset())
+        handles = [None] * tp.world
+        dist.all_gather_object(handles, bytes(handle), group=tp.group)
+        self.bases = (ctypes.c_void_p * tp.world)()
+        self._opened = []
+        for g in range(tp.world):
+            if g == tp.rank:
+                self.bases[g] = self.base
+                continue
+            h = (ctypes.c_uint8 * 64).from_buffer_copy(handles[g])
+            peer = ctypes.c_void_p()
+            N.check(lib.tn_tp_region_open(h, ctypes.byref(peer)))
+            self.bases[g] = peer.value
+            self._opened.append(peer.value)
+        self._next = 0
+        self.slot = 0
+
+    def buffer(self, rows: int, cols: int, dtype=torch.bfloat16) -> tuple[torch.Tensor, int]:
+        """A [rows, cols] 16-bit gather destination in this rank's region and
+        its byte offset in the data area (256-byte aligned)."""
+        off = self._next
+        size = rows * cols * 2
+        if off + size > self.nbytes:
+            raise ValueError("exchange region too small")
+        self._next = (off + size + 255) // 256 * 256
+        t = torch.as_tensor(_DevicePointer(self.base + self.data_off + off, rows * cols), device=self.dev)
+        return t.view(dtype).view(rows, cols), off
+
+    def allgather(self, local: torch.Tensor, dst_off: int, full_cols: int, stream) -> None:
+        """One gather of this step: local [rows, c] -> every rank's [rows, full_cols] at dst_off."""
+        rows, c = local.shape
+        N.check(N.lib().tn_tp_allgather(self.bases, self.tp.rank, self.tp.world, P(local.data_ptr()),
+                                        local.stride(0), rows, c, dst_off, full_cols, self.slot, stream))
+        self.slot += 1
+
+    def step_end(self, stream) -> None:
+        N.check(N.lib().tn_tp_step_end(P(self.base), stream))
+        self.slot = 0
+
+    def close(self) -> None:
+        """After a barrier that no rank passes with a gather in flight."""
+        lib = N.lib()
+        for p in self._opened:
+            lib.tn_tp_region_close(P(p))
+        self._opened = []
+        if self.base:
+            lib.tn_tp_region_free(P(self.base))
+            self.base = 0
