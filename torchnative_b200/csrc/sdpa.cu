@@ -95,7 +95,7 @@ extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void 
     // (one pass over K/V per 64 query rows, where the split-KV kernel would
     // re-read K/V for every 8 rows).
     if (L > 16) return tn::launch_sdpa_prefill_simt(p, dtype, stream);
-    st = tn::plan_sdpa_decode(p, f.sm_count);
+    st = tn::plan_sdpa_decode(p, f.sm_count, dtype);
     if (st) return st;
     void *ws = nullptr;
     st = tn::workspace(&ws, tn::sdpa_decode_workspace(p), stream, /*slot=*/1);
@@ -147,7 +147,7 @@ extern "C" int tn_sdpa_decode_cache(const void *q, const void *k_cache, const vo
     p.S_dev = len_dev;
     p.S_add = (int)len_add;
     p.err = tn::device_error_word();
-    st = tn::plan_sdpa_decode(p, f.sm_count);
+    st = tn::plan_sdpa_decode(p, f.sm_count, dtype);
     if (st) return st;
     void *ws = nullptr;
     st = tn::workspace(&ws, tn::sdpa_decode_workspace(p), stream, /*slot=*/2);
@@ -201,7 +201,7 @@ extern "C" int tn_sdpa_decode_step(const void *qkv, const float *inv_freq, void 
     p.qkv = static_cast<const __nv_bfloat16 *>(qkv);
     p.inv_freq = inv_freq;
     p.err = tn::device_error_word();
-    st = tn::plan_sdpa_decode(p, f.sm_count);
+    st = tn::plan_sdpa_decode(p, f.sm_count, TN_BF16);
     if (st) return st;
     if (p.row_groups != 1) return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": internal: more than one row group");
     void *ws = nullptr;

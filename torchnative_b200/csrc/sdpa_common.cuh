@@ -46,6 +46,6 @@ int launch_sdpa_prefill(const SdpaParams &p, int dtype, cudaStream_t stream);
 // grid (ceil(L / 64), Hq, B).
 int launch_sdpa_prefill_simt(const SdpaParams &p, int dtype, cudaStream_t stream);
 size_t sdpa_decode_workspace(const SdpaParams &p);
-int plan_sdpa_decode(SdpaParams &p, int sm_count);
+int plan_sdpa_decode(SdpaParams &p, int sm_count, int dtype);
 
 }  // namespace tn

@@ -104,14 +104,15 @@ __device__ __forceinline__ int kswz(int j, int c) { return c ^ ((j & 1) << 2); }
 // After a CTA wrote its split's partial: the last CTA of its (b, kv head, row
 // group) to finish merges all splits of these rows, in split order:
 // M = max m_s, out = sum e^(m_s - M) o_s / sum e^(m_s - M) l_s, lse = M + log(den).
-// `scratch` is shared memory for 2 * RMAX * splits + RMAX floats.
+// `scratch` is `scratch_bytes` of drained shared memory. When the rows'
+// partial outputs fit there next to the merge weights, one bulk copy per row
+// brings them in (a single memory latency for the whole merge); otherwise
+// each thread streams its dimensions through L2.
 template <typename T, int D>
 __device__ __forceinline__ void merge_if_last(const SdpaParams &p, int b, int kvh, int rg, int R, int tid,
-                                              float *scratch) {
-
-    // ---- the last split to finish merges all splits of these rows (in split
-    // order: M = max m_s, out = sum e^(m_s - M) o_s / sum e^(m_s - M) l_s)
+                                              float *scratch, size_t scratch_bytes) {
     __shared__ int last;
+    __shared__ __align__(8) uint64_t staged_bar;
     __threadfence();
     __syncthreads();
     int *counter = p.counters + ((int64_t)b * p.Hkv + kvh) * p.row_groups + rg;
@@ -119,12 +120,27 @@ __device__ __forceinline__ void merge_if_last(const SdpaParams &p, int b, int kv
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // Merge weights first (every split's (m, l) of every row, loaded in
-    // parallel into the drained ring), then the weighted sum of the partial
-    // outputs, four dimensions per thread.
-    float *wsm = scratch;           // [R][splits] m_s, then weights e^(m_s - M)
-    float *lsp = wsm + RMAX * p.splits;                       // [R][splits] l_s
-    float *lsm = lsp + RMAX * p.splits;                       // [R] sum of weighted l_s
+    float *wsm = scratch;                 // [R][splits] m_s, then weights e^(m_s - M)
+    float *lsp = wsm + RMAX * p.splits;   // [R][splits] l_s
+    float *lsm = lsp + RMAX * p.splits;   // [R] sum of weighted l_s
+    const size_t ml_bytes = ((size_t)(2 * RMAX * p.splits + RMAX) * 4 + 127) & ~size_t(127);
+    const size_t row_bytes = (size_t)p.splits * D * 4;
+    float *pos_ = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(scratch) + ml_bytes);
+    const bool staged = ml_bytes + (size_t)R * row_bytes <= scratch_bytes;
+    const int64_t row0 = ((int64_t)b * p.Hq + kvh * p.rep) * p.L;  // R consecutive rows (L = 1 or one head)
+    const bool contiguous = p.L == 1 && rg == 0;
+    bool have = false;
+    if (staged && contiguous) {
+        if (tid == 0) {
+            mbar_init(&staged_bar, 1);
+            fence_mbar_init();
+            // the partials were written through the generic proxy by other CTAs
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            mbar_arrive_expect_tx(&staged_bar, (uint32_t)(R * row_bytes));
+            bulk_g2s(pos_, p.part_o + row0 * p.splits * D, (uint32_t)(R * row_bytes), &staged_bar);
+        }
+        have = true;
+    }
     for (int idx = tid; idx < R * p.splits; idx += kThreads) {
         const int r = idx / p.splits, sp = idx % p.splits;
         const int64_t row = ((int64_t)b * p.Hq + kvh * p.rep + r) * p.L;
@@ -133,34 +149,60 @@ __device__ __forceinline__ void merge_if_last(const SdpaParams &p, int b, int kv
         lsp[idx] = ml.y;
     }
     __syncthreads();
-    if (tid < R) {
-        const int64_t row = ((int64_t)b * p.Hq + kvh * p.rep + tid) * p.L;
-        float M = -INFINITY;
-        for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, wsm[tid * p.splits + sp]);
-        float den = 0.0f;
-        for (int sp = 0; sp < p.splits; ++sp) {
-            const float m = wsm[tid * p.splits + sp];
-            const float w = (m == -INFINITY) ? 0.0f : expf(m - M);
-            wsm[tid * p.splits + sp] = w;
-            den = fmaf(w, lsp[tid * p.splits + sp], den);
+    // one warp per row: the splits' maximum, weights and weighted sum across lanes
+    {
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int r = warp; r < R; r += kThreads / 32) {
+            const int64_t row = ((int64_t)b * p.Hq + kvh * p.rep + r) * p.L;
+            float M = -INFINITY;
+            for (int sp = lane; sp < p.splits; sp += 32) M = fmaxf(M, wsm[r * p.splits + sp]);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            float den = 0.0f;
+            for (int sp = lane; sp < p.splits; sp += 32) {
+                const float m = wsm[r * p.splits + sp];
+                const float w = (m == -INFINITY) ? 0.0f : expf(m - M);
+                wsm[r * p.splits + sp] = w;
+                den = fmaf(w, lsp[r * p.splits + sp], den);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+            if (lane == 0) {
+                lsm[r] = den;
+                if (p.lse) p.lse[row] = logf(den) + M;
+            }
         }
-        lsm[tid] = den;
-        if (p.lse) p.lse[row] = logf(den) + M;
     }
+    bool ok = true;
+    if (have) ok = mbar_wait(&staged_bar, 0);
+    if (have && !ok) record_device_error(p.err, DEV_ERR_WAIT_FULL);
     __syncthreads();
     for (int idx = tid; idx < R * (D / 4); idx += kThreads) {
         const int r = idx / (D / 4), d4 = idx % (D / 4);
         const int64_t row = ((int64_t)b * p.Hq + kvh * p.rep + r) * p.L;
-        const float4 *po = reinterpret_cast<const float4 *>(p.part_o + row * p.splits * D) + d4;
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (have) {
+            const float4 *po = reinterpret_cast<const float4 *>(pos_ + (size_t)r * p.splits * D) + d4;
 #pragma unroll 8
-        for (int sp = 0; sp < p.splits; ++sp) {
-            const float w = wsm[r * p.splits + sp];
-            const float4 o = __ldcg(po + (int64_t)sp * (D / 4));
-            acc.x = fmaf(w, o.x, acc.x);
-            acc.y = fmaf(w, o.y, acc.y);
-            acc.z = fmaf(w, o.z, acc.z);
-            acc.w = fmaf(w, o.w, acc.w);
+            for (int sp = 0; sp < p.splits; ++sp) {
+                const float w = wsm[r * p.splits + sp];
+                const float4 o = po[(int64_t)sp * (D / 4)];
+                acc.x = fmaf(w, o.x, acc.x);
+                acc.y = fmaf(w, o.y, acc.y);
+                acc.z = fmaf(w, o.z, acc.z);
+                acc.w = fmaf(w, o.w, acc.w);
+            }
+        } else {
+            const float4 *po = reinterpret_cast<const float4 *>(p.part_o + row * p.splits * D) + d4;
+#pragma unroll 8
+            for (int sp = 0; sp < p.splits; ++sp) {
+                const float w = wsm[r * p.splits + sp];
+                const float4 o = __ldcg(po + (int64_t)sp * (D / 4));
+                acc.x = fmaf(w, o.x, acc.x);
+                acc.y = fmaf(w, o.y, acc.y);
+                acc.z = fmaf(w, o.z, acc.z);
+                acc.w = fmaf(w, o.w, acc.w);
+            }
         }
         const float inv = 1.0f / lsm[r];
         const float v4[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
@@ -407,7 +449,10 @@ __global__ void __launch_bounds__(kThreads) sdpa_decode_kernel(const SdpaParams 
         }
     }
     if (!p.counters) return;
-    merge_if_last<T, D>(p, b, kvh, rg, R, tid, reinterpret_cast<float *>(ring));
+    {
+        const size_t ring_b = (size_t)NSTAGE * 2 * LY::TILE_BYTES, o_b = (size_t)LY::PV_GROUPS * RMAX * D * 4;
+        merge_if_last<T, D>(p, b, kvh, rg, R, tid, reinterpret_cast<float *>(ring), ring_b > o_b ? ring_b : o_b);
+    }
 }
 
 // Merge the splits of one output row: M = max m_s, w_s = exp(m_s - M),
@@ -527,7 +572,6 @@ __global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const S
     constexpr int KS = D / 16;                     // k-steps of QK^T
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *qb = smem;                                            // [16][D] T, swizzled
-    float *tabs = reinterpret_cast<float *>(smem + 16 * D * 2);    // RoPE cos/sin [D]
     uint8_t *rings = smem + 16 * D * 2 + D * 4;                    // MMA_WARPS x NST x (K, V)
     float *cmb = reinterpret_cast<float *>(rings);                 // after the rings drain: warp merge
 
@@ -540,38 +584,80 @@ __global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const S
     pdl_wait();
     const int S = p.S_dev ? min(*p.S_dev + p.S_add, p.S) : p.S;
     const int t0 = split * p.keys_per_split, t1 = min(S, t0 + p.keys_per_split);
-    const uint32_t qb_u = smem_u32(qb);
+    const int pos = S - 1;
+    // the one CTA per (b, kv head) whose keys include the appended slot writes it first
+    const bool appends = p.qkv && t0 <= pos && pos < t1 && rg == 0;
+
+    // ---- per-warp K/V tiles: w, w + 4, ... of the split's 16-key tiles. The
+    // first ones are requested before the query rows are prepared (their HBM
+    // latency overlaps that work), except in the CTA that appends the new key.
+    const int ntiles = t1 > t0 ? (t1 - t0 + TKM - 1) / TKM : 0;
+    const T *kbase = static_cast<const T *>(p.k) + b * p.ks[0] + kvh * p.ks[1];
+    const T *vbase = static_cast<const T *>(p.v) + b * p.vs[0] + kvh * p.vs[1];
+    const uint32_t ring_u = smem_u32(rings) + warp * NST * 2 * TILE;
+    auto issue = [&](int tile, int stage) {
+        const uint32_t kst = ring_u + stage * 2 * TILE, vst = kst + TILE;
+        for (int idx = lane; idx < TKM * CPR; idx += 32) {
+            const int j = idx / CPR, c = idx % CPR;
+            const int t = t0 + tile * TKM + j;
+            const bool ok = t < t1;
+            const int ts = ok ? t : t0;
+            cp_async16(kst + tile_off<D>(j, c), kbase + (int64_t)ts * p.ks[2] + c * 8, ok ? 16u : 0u);
+            cp_async16(vst + tile_off<D>(j, c), vbase + (int64_t)ts * p.vs[2] + c * 8, ok ? 16u : 0u);
+        }
+    };
+    auto prime = [&]() {
+#pragma unroll
+        for (int s2 = 0; s2 < NST - 1; ++s2) {
+            const int tile = warp + s2 * MMA_WARPS;
+            if (tile < ntiles) issue(tile, s2);
+            cp_async_commit();
+        }
+    };
+    if (!appends) prime();
 
     // ---- query rows -> qb (16-bit, rows >= R zero), with the fused RoPE/append
     if (p.qkv) {
-        const int pos = S - 1, half = D / 2, W = (p.Hq + 2 * p.Hkv) * D;
+        const int half = D / 2, W = (p.Hq + 2 * p.Hkv) * D;
         const __nv_bfloat16 *row = p.qkv + (int64_t)b * W;
-        for (int i = tid; i < half; i += MMA_WARPS * 32) {
-            const float f = p.inv_freq[i] * (float)pos;
-            tabs[i] = bfr16(cosf(f));
-            tabs[half + i] = bfr16(sinf(f));
-        }
-        __syncthreads();
-        for (int idx = tid; idx < 16 * D; idx += MMA_WARPS * 32) {
-            const int r = idx / D, d = idx % D;
-            float v = 0.0f;
+        constexpr int NTH = MMA_WARPS * 32, PER = (16 * (D / 2) + NTH - 1) / NTH;
+        // thread: rotation pairs (r, i) = (idx / half, idx % half), idx = tid + k * NTH;
+        // every load first, then the arithmetic
+        float x1[PER], x2[PER];
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            const int idx = tid + k * NTH, r = idx / half, i = idx % half;
+            x1[k] = x2[k] = 0.0f;
             if (r < R) {
-                const int hq = kvh * p.rep + r, i = d % half;
-                const float c = tabs[i], sn = tabs[half + i];
-                const float x1 = __bfloat162float(row[hq * D + i]), x2 = __bfloat162float(row[hq * D + i + half]);
-                v = d < half ? bfr16(bfr16(x1 * c) + bfr16(-x2 * sn)) : bfr16(bfr16(x2 * c) + bfr16(x1 * sn));
+                const int hq = kvh * p.rep + r;
+                x1[k] = __bfloat162float(row[hq * D + i]);
+                x2[k] = __bfloat162float(row[hq * D + i + half]);
             }
-            reinterpret_cast<T *>(qb + tile_off<D>(r, d / 8))[d % 8] = (T)v;
         }
-        if (t0 <= pos && pos < t1 && rg == 0) {
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            const int idx = tid + k * NTH, r = idx / half, i = idx % half;
+            if (r >= 16) break;
+            float lo = 0.0f, hi = 0.0f;
+            if (r < R) {
+                const float f = p.inv_freq[i] * (float)pos;
+                const float c = bfr16(cosf(f)), sn = bfr16(sinf(f));
+                lo = bfr16(bfr16(x1[k] * c) + bfr16(-x2[k] * sn));
+                hi = bfr16(bfr16(x2[k] * c) + bfr16(x1[k] * sn));
+            }
+            reinterpret_cast<T *>(qb + tile_off<D>(r, i / 8))[i % 8] = (T)lo;
+            reinterpret_cast<T *>(qb + tile_off<D>(r, (i + half) / 8))[(i + half) % 8] = (T)hi;
+        }
+        if (appends) {
             __nv_bfloat16 *kc = (__nv_bfloat16 *)p.k + b * p.ks[0] + kvh * p.ks[1] + (int64_t)pos * p.ks[2];
             __nv_bfloat16 *vc = (__nv_bfloat16 *)p.v + b * p.vs[0] + kvh * p.vs[1] + (int64_t)pos * p.vs[2];
             const __nv_bfloat16 *kr = row + (p.Hq + kvh) * D, *vr = row + (p.Hq + p.Hkv + kvh) * D;
-            for (int i = tid; i < half; i += MMA_WARPS * 32) {
-                const float c = tabs[i], sn = tabs[half + i];
-                const float x1 = __bfloat162float(kr[i]), x2 = __bfloat162float(kr[i + half]);
-                kc[i] = __float2bfloat16_rn(bfr16(x1 * c) + bfr16(-x2 * sn));
-                kc[i + half] = __float2bfloat16_rn(bfr16(x2 * c) + bfr16(x1 * sn));
+            for (int i = tid; i < half; i += NTH) {
+                const float f = p.inv_freq[i] * (float)pos;
+                const float c = bfr16(cosf(f)), sn = bfr16(sinf(f));
+                const float y1 = __bfloat162float(kr[i]), y2 = __bfloat162float(kr[i + half]);
+                kc[i] = __float2bfloat16_rn(bfr16(y1 * c) + bfr16(-y2 * sn));
+                kc[i + half] = __float2bfloat16_rn(bfr16(y2 * c) + bfr16(y1 * sn));
                 vc[i] = vr[i];
                 vc[i + half] = vr[i + half];
             }
@@ -588,29 +674,7 @@ __global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const S
         }
     }
     __syncthreads();  // qb complete; the appended slot is written before any tile copy reads it
-
-    // ---- per-warp tiles: w, w + 4, ... of the split's 16-key tiles
-    const int ntiles = t1 > t0 ? (t1 - t0 + TKM - 1) / TKM : 0;
-    const T *kbase = static_cast<const T *>(p.k) + b * p.ks[0] + kvh * p.ks[1];
-    const T *vbase = static_cast<const T *>(p.v) + b * p.vs[0] + kvh * p.vs[1];
-    const uint32_t ring_u = smem_u32(rings) + warp * NST * 2 * TILE;
-    auto issue = [&](int tile, int stage) {
-        const uint32_t kst = ring_u + stage * 2 * TILE, vst = kst + TILE;
-        for (int idx = lane; idx < TKM * CPR; idx += 32) {
-            const int j = idx / CPR, c = idx % CPR;
-            const int t = t0 + tile * TKM + j;
-            const bool ok = t < t1;
-            const int ts = ok ? t : t0;
-            cp_async16(kst + tile_off<D>(j, c), kbase + (int64_t)ts * p.ks[2] + c * 8, ok ? 16u : 0u);
-            cp_async16(vst + tile_off<D>(j, c), vbase + (int64_t)ts * p.vs[2] + c * 8, ok ? 16u : 0u);
-        }
-    };
-#pragma unroll
-    for (int s2 = 0; s2 < NST - 1; ++s2) {
-        const int tile = warp + s2 * MMA_WARPS;
-        if (tile < ntiles) issue(tile, s2);
-        cp_async_commit();
-    }
+    if (appends) prime();
 
     // Q fragments (A operand, rows g / g+8, all k-steps), loaded once
     uint32_t qa[KS][4];
@@ -763,7 +827,11 @@ __global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const S
         }
     }
     if (!p.counters) return;
-    merge_if_last<T, D>(p, b, kvh, rg, R, tid, cmb);
+    {
+        const size_t rings_b = (size_t)MMA_WARPS * NST * 2 * TKM * D * 2;
+        const size_t merge_b = (size_t)(2 * MMA_WARPS * 16 + MMA_WARPS * 16 * D) * 4;
+        merge_if_last<T, D>(p, b, kvh, rg, R, tid, cmb, rings_b > merge_b ? rings_b : merge_b);
+    }
 }
 
 template <int D>
@@ -826,15 +894,22 @@ int launch_typed(const SdpaParams &p, cudaStream_t stream) {
 
 }  // namespace
 
-int plan_sdpa_decode(SdpaParams &p, int sm_count) {
+int plan_sdpa_decode(SdpaParams &p, int sm_count, int dtype) {
     const int R = p.rep * p.L;
     p.rows = R < RMAX ? R : RMAX;
     p.row_groups = (R + p.rows - 1) / p.rows;
     const int64_t base = (int64_t)p.B * p.Hkv * p.row_groups;
-    // about one CTA per SM, and no split shorter than 4 tiles: fewer, longer
-    // splits keep the merge (one partial per split) short
-    int64_t want = (1LL * sm_count + base - 1) / base;
-    const int64_t max_splits = (p.S + 4 * TK - 1) / (4 * TK);
+    // About two CTAs per SM when few (b, kv head) pairs share the GPU, one
+    // otherwise, and no split shorter than one 16-key tile per warp (tensor-core
+    // kernel) or 4 tiles of 32 keys (SIMT kernel): the last CTA's merge grows
+    // with the split count (measured on B200: batch 1, 8 KV heads, 2049 keys:
+    // 37 splits 11.5 us, 19 splits 12.0 us; batch 4: 5 splits 18.5 us, 10
+    // splits 23.3 us).
+    const bool mma = dtype != TN_F32 && !p.mask;
+    const int min_keys = mma ? MMA_WARPS * TKM : 4 * TK;
+    const int64_t per_sm = base <= 8 ? 2 : 1;
+    int64_t want = (per_sm * sm_count + base - 1) / base;
+    const int64_t max_splits = (p.S + min_keys - 1) / min_keys;
     if (want > max_splits) want = max_splits;
     if (want < 1) want = 1;
     int kps = (int)((p.S + want - 1) / want);
