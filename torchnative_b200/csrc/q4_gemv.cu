@@ -218,20 +218,24 @@ __device__ __forceinline__ int sat_i8r(float v) {
     return __float2int_rz(v);
 }
 
-// One Q8_0 block (k_quants.rs:676-706) from 32 values held by one thread,
-// written into the staged planar tile (codes as two 16-byte chunks in the
-// pair-swizzled layout, then the widened scale and the offset constant).
-__device__ __forceinline__ void q8_block_to_smem(const float (&v)[32], int m, int b, const Smem &s,
-                                                 const GemvParams &p) {
+// One Q8_0 block (k_quants.rs:676-706) quantised by two adjacent lanes (lane
+// pair 2i, 2i + 1), each holding 16 of its values (`half` 0: elements 0-15,
+// 1: 16-31), written into the staged planar tile (codes as two 16-byte chunks
+// in the pair-swizzled layout, then the widened scale and the offset
+// constant). The block maximum and the code sum cross the pair by shuffles.
+__device__ __forceinline__ void q8_half_block_to_smem(const float (&v)[16], int m, int b, int half, const Smem &s,
+                                                      const GemvParams &p, int lane) {
+    const unsigned pm = 3u << (lane & ~1);
     float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    amax = fmaxf(amax, __shfl_xor_sync(pm, amax, 1));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
-    uint32_t w[8];
+    uint32_t w[4];
     int sum = 0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < 4; ++k) {
         uint32_t word = 0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -241,12 +245,14 @@ __device__ __forceinline__ void q8_block_to_smem(const float (&v)[32], int m, in
         }
         w[k] = word;
     }
-    const int pair = b >> 1, c = (b & 1) * 2;
+    sum += __shfl_xor_sync(pm, sum, 1);
+    const int pair = b >> 1, c = (b & 1) * 2 + half;
     const uint32_t row = s.xs + (uint32_t)m * p.nbp * 32;
     sts128(row + xchunk(pair, c), make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]));
-    sts128(row + xchunk(pair, c + 1), make_int4((int)w[4], (int)w[5], (int)w[6], (int)w[7]));
-    stsf(s.xds + (uint32_t)(m * p.nbp + b) * 4, __half2float(__float2half_rn(d)));
-    stsf(s.xcs + (uint32_t)(m * p.nbp + b) * 4, 12582912.0f + 8.0f * (float)sum);
+    if (half == 0) {
+        stsf(s.xds + (uint32_t)(m * p.nbp + b) * 4, __half2float(__float2half_rn(d)));
+        stsf(s.xcs + (uint32_t)(m * p.nbp + b) * 4, 12582912.0f + 8.0f * (float)sum);
+    }
 }
 
 // 8 consecutive bf16 values (one 16-byte load; rows are 16-byte aligned) as f32.
@@ -271,24 +277,25 @@ constexpr int kMaxFusedRows = 4;
 __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p, int tid, int warp, int lane,
                                               float *red) {
     const int K = p.nb * 32, nthr = kConsumerWarps * 32;
-    if (p.x_mode == X_NORM && p.M == 1 && p.nb <= nthr) {
-        // The decode case: one row, at most one block per thread. Every load is
-        // issued before the first use and the block stays in registers across
-        // the CTA-wide reduction, so the prologue costs one L2 round trip.
-        const int b = tid;
-        float h[32];
-        uint32_t wp[16];
+    if (p.x_mode == X_NORM && p.M == 1 && 2 * p.nb <= nthr) {
+        // The decode case: one row, half a block per thread (lanes 2i, 2i + 1
+        // share block i). Every load is issued before the first use and the
+        // values stay in registers across the CTA-wide reduction, so the
+        // prologue costs one L2 round trip.
+        const int b = tid >> 1, hf = tid & 1, e0 = b * 32 + 16 * hf;
+        float h[16];
+        uint32_t wp[8];
         float ss = 0.0f;
         if (b < p.nb) {
-            int4 xr[4], dr[4], wr[4];
+            int4 xr[2], dr[2], wr[2];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                xr[c] = __ldg(reinterpret_cast<const int4 *>(p.xb + b * 32) + c);
-                dr[c] = p.xdelta ? __ldg(reinterpret_cast<const int4 *>(p.xdelta + b * 32) + c) : make_int4(0, 0, 0, 0);
-                wr[c] = __ldg(reinterpret_cast<const int4 *>(p.xw + b * 32) + c);
+            for (int c = 0; c < 2; ++c) {
+                xr[c] = __ldg(reinterpret_cast<const int4 *>(p.xb + e0) + c);
+                dr[c] = p.xdelta ? __ldg(reinterpret_cast<const int4 *>(p.xdelta + e0) + c) : make_int4(0, 0, 0, 0);
+                wr[c] = __ldg(reinterpret_cast<const int4 *>(p.xw + e0) + c);
             }
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 const uint32_t xu[4] = {(uint32_t)xr[c].x, (uint32_t)xr[c].y, (uint32_t)xr[c].z, (uint32_t)xr[c].w};
                 const uint32_t du[4] = {(uint32_t)dr[c].x, (uint32_t)dr[c].y, (uint32_t)dr[c].z, (uint32_t)dr[c].w};
                 wp[4 * c + 0] = (uint32_t)wr[c].x;
@@ -307,7 +314,7 @@ __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 32; ++j) ss = fmaf(h[j], h[j], ss);
+            for (int j = 0; j < 16; ++j) ss = fmaf(h[j], h[j], ss);
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
@@ -319,26 +326,26 @@ __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p
         const float r = rsqrtf(t / (float)K + p.eps);
         if (b < p.nb) {
             if (p.xh_out && blockIdx.x == 0) {
-                uint32_t o[16];
+                uint32_t o[8];
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
+                for (int i = 0; i < 8; ++i)
                     o[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(h[2 * i])) |
                            ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(h[2 * i + 1])) << 16);
-                int4 *dst = reinterpret_cast<int4 *>(p.xh_out + b * 32);
+                int4 *dst = reinterpret_cast<int4 *>(p.xh_out + e0);
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 2; ++c)
                     dst[c] = make_int4((int)o[4 * c], (int)o[4 * c + 1], (int)o[4 * c + 2], (int)o[4 * c + 3]);
             }
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < 8; ++i) {
                 h[2 * i] = bfr(__uint_as_float(wp[i] << 16) * bfr(h[2 * i] * r));
                 h[2 * i + 1] = bfr(__uint_as_float(wp[i] & 0xffff0000u) * bfr(h[2 * i + 1] * r));
             }
-            q8_block_to_smem(h, 0, b, s, p);
+            q8_half_block_to_smem(h, 0, b, hf, s, p, lane);
         } else if (b < p.nbp) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) h[j] = 0.0f;
-            q8_block_to_smem(h, 0, b, s, p);
+            for (int j = 0; j < 16; ++j) h[j] = 0.0f;
+            q8_half_block_to_smem(h, 0, b, hf, s, p, lane);
         }
         return;
     }
@@ -377,40 +384,47 @@ __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p
             rinv[m] = rsqrtf(t / (float)K + p.eps);
         }
     }
+    // half a block per task: (b, hf) = (t / 2, t % 2); lane pairs hold one
+    // block. One loop per mode, every load of a task issued before its math.
 #pragma unroll
     for (int m = 0; m < kMaxFusedRows; ++m) {
         if (m >= p.M) continue;
-        for (int b = tid; b < p.nbp; b += nthr) {
-            float v[32];
+        const __nv_bfloat16 *xrow = p.xb + m * p.xb_row_stride;
+        for (int t = tid; t < 2 * p.nbp; t += nthr) {
+            const int b = t >> 1, hf = t & 1, e0 = b * 32 + 16 * hf;
+            float v[16];
             if (b >= p.nb) {  // padding block of an odd block count
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = 0.0f;
-            } else {
-                const __nv_bfloat16 *xr = p.xb + m * p.xb_row_stride + b * 32;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float *vc = v + 8 * c;
-                    load8_bf16(xr + 8 * c, vc);
-                    if (p.x_mode == X_NORM) {
-                        float dl[8], w[8];
-                        if (p.xdelta) load8_bf16(p.xdelta + m * p.xb_row_stride + b * 32 + 8 * c, dl);
-                        load8_bf16(p.xw + b * 32 + 8 * c, w);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const float h = p.xdelta ? bfr(vc[j] + dl[j]) : vc[j];
-                            if (p.xh_out && blockIdx.x == 0)
-                                p.xh_out[m * p.xb_row_stride + b * 32 + 8 * c + j] = __float2bfloat16_rn(h);
-                            vc[j] = bfr(w[j] * bfr(h * rinv[m]));
-                        }
-                    } else if (p.x_mode == X_SILU) {  // rows are [gate (K) | up (K)]
-                        float u[8];
-                        load8_bf16(xr + K + 8 * c, u);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) vc[j] = bfr(bfr(vc[j] / (1.0f + expf(-vc[j]))) * u[j]);
-                    }
+                for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+            } else if (p.x_mode == X_BF16) {
+                load8_bf16(xrow + e0, v);
+                load8_bf16(xrow + e0 + 8, v + 8);
+            } else if (p.x_mode == X_NORM) {
+                float dl[16], w[16];
+                load8_bf16(xrow + e0, v);
+                load8_bf16(xrow + e0 + 8, v + 8);
+                if (p.xdelta) {
+                    load8_bf16(p.xdelta + m * p.xb_row_stride + e0, dl);
+                    load8_bf16(p.xdelta + m * p.xb_row_stride + e0 + 8, dl + 8);
                 }
+                load8_bf16(p.xw + e0, w);
+                load8_bf16(p.xw + e0 + 8, w + 8);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float h = p.xdelta ? bfr(v[j] + dl[j]) : v[j];
+                    if (p.xh_out && blockIdx.x == 0) p.xh_out[m * p.xb_row_stride + e0 + j] = __float2bfloat16_rn(h);
+                    v[j] = bfr(w[j] * bfr(h * rinv[m]));
+                }
+            } else {  // X_SILU: rows are [gate (K) | up (K)]
+                float u[16];
+                load8_bf16(xrow + e0, v);
+                load8_bf16(xrow + e0 + 8, v + 8);
+                load8_bf16(xrow + K + e0, u);
+                load8_bf16(xrow + K + e0 + 8, u + 8);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = bfr(bfr(v[j] / (1.0f + expf(-v[j]))) * u[j]);
             }
-            q8_block_to_smem(v, m, b, s, p);
+            q8_half_block_to_smem(v, m, b, hf, s, p, lane);
         }
     }
 }
