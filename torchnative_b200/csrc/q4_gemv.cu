@@ -274,10 +274,11 @@ constexpr int kMaxFusedRows = 4;
 // rsqrt(mean(x^2) + eps)), x = bf16(h + delta)), or bf16(bf16(silu(g)) * u)
 // (X_SILU). Consumer threads only; `red` is kMaxFusedRows * kConsumerWarps
 // floats of shared scratch.
+template <int XM>
 __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p, int tid, int warp, int lane,
                                               float *red) {
     const int K = p.nb * 32, nthr = kConsumerWarps * 32;
-    if (p.x_mode == X_NORM && p.M == 1 && 2 * p.nb <= nthr) {
+    if (XM == X_NORM && p.M == 1 && 2 * p.nb <= nthr) {
         // The decode case: one row, half a block per thread (lanes 2i, 2i + 1
         // share block i). Every load is issued before the first use and the
         // values stay in registers across the CTA-wide reduction, so the
@@ -350,7 +351,7 @@ __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p
         return;
     }
     float rinv[kMaxFusedRows] = {1.0f, 1.0f, 1.0f, 1.0f};
-    if (p.x_mode == X_NORM) {
+    if constexpr (XM == X_NORM) {
         float ss[kMaxFusedRows] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int m = 0; m < kMaxFusedRows; ++m) {
@@ -396,10 +397,10 @@ __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p
             if (b >= p.nb) {  // padding block of an odd block count
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-            } else if (p.x_mode == X_BF16) {
+            } else if constexpr (XM == X_BF16) {
                 load8_bf16(xrow + e0, v);
                 load8_bf16(xrow + e0 + 8, v + 8);
-            } else if (p.x_mode == X_NORM) {
+            } else if constexpr (XM == X_NORM) {
                 float dl[16], w[16];
                 load8_bf16(xrow + e0, v);
                 load8_bf16(xrow + e0 + 8, v + 8);
@@ -541,7 +542,7 @@ __device__ __forceinline__ void global_rows(const Smem &s, const GemvParams &p, 
     }
 }
 
-template <int MT, bool STAGED>
+template <int MT, bool STAGED, int XM>
 __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, p);
@@ -607,11 +608,11 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
 
     // ---------------- consumers
     pdl_wait();  // the activations may come from the previous kernel in the stream
-    if (p.x_mode == X_PLANAR) {
+    if constexpr (XM == X_PLANAR) {
         stage_x(s, p, threadIdx.x, kConsumerWarps * 32);
     } else {
         __shared__ float red[kMaxFusedRows * kConsumerWarps];
-        stage_x_fused(s, p, threadIdx.x, warp, lane, red);
+        stage_x_fused<XM>(s, p, threadIdx.x, warp, lane, red);
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
@@ -648,13 +649,13 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
     }
 }
 
-template <int MT, bool STAGED>
+template <int MT, bool STAGED, int XM>
 int launch_variant(const GemvParams &p, int grid, size_t smem, cudaStream_t stream) {
     static int configured_for[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && configured_for[dev] < (int)smem) {
-        int st = check_cuda(cudaFuncSetAttribute(q4_gemv_q8_kernel<MT, STAGED>,
+        int st = check_cuda(cudaFuncSetAttribute(q4_gemv_q8_kernel<MT, STAGED, XM>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                             "torch._C._quantized_linear", "cudaFuncSetAttribute");
         if (st) return st;
@@ -670,7 +671,7 @@ int launch_variant(const GemvParams &p, int grid, size_t smem, cudaStream_t stre
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int st = check_cuda(cudaLaunchKernelEx(&cfg, q4_gemv_q8_kernel<MT, STAGED>, p), "torch._C._quantized_linear",
+    int st = check_cuda(cudaLaunchKernelEx(&cfg, q4_gemv_q8_kernel<MT, STAGED, XM>, p), "torch._C._quantized_linear",
                         "cudaLaunchKernelEx");
     if (st) return st;
     __atomic_fetch_add(STAGED ? &counters().q4_gemv_launches : &counters().q4_gemv_generic, 1ull, __ATOMIC_RELAXED);
@@ -763,16 +764,30 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
     int64_t grid = (int64_t)f.sm_count * ctas_per_sm;
     const int64_t by_rows = (N + 2 * plan.wpc - 1) / (2 * plan.wpc);
     if (by_rows < grid) grid = by_rows > 0 ? by_rows : 1;
-#define TN_GEMV_CASE(MT)                                                                   \
-    if (M <= MT)                                                                           \
-        return staged ? launch_variant<MT, true>(p, (int)grid, smem, stream)               \
-                      : launch_variant<MT, false>(p, (int)grid, smem, stream);
-    TN_GEMV_CASE(1)
-    TN_GEMV_CASE(2)
-    TN_GEMV_CASE(4)
-    TN_GEMV_CASE(8)
-    TN_GEMV_CASE(16)
-#undef TN_GEMV_CASE
+    // One kernel per (rows, staging, activation source): each holds only the
+    // prologue it runs (the prologue executes once per CTA, from a cold
+    // instruction cache, so its code size is latency).
+#define TN_GEMV_LAUNCH(MT, XM)                                                             \
+    return staged ? launch_variant<MT, true, XM>(p, (int)grid, smem, stream)               \
+                  : launch_variant<MT, false, XM>(p, (int)grid, smem, stream);
+#define TN_GEMV_CASE_FUSED(MT)                                                             \
+    if (M <= MT) {                                                                         \
+        switch (p.x_mode) {                                                                \
+        case X_BF16: TN_GEMV_LAUNCH(MT, X_BF16)                                            \
+        case X_NORM: TN_GEMV_LAUNCH(MT, X_NORM)                                            \
+        case X_SILU: TN_GEMV_LAUNCH(MT, X_SILU)                                            \
+        default: TN_GEMV_LAUNCH(MT, X_PLANAR)                                              \
+        }                                                                                  \
+    }
+    TN_GEMV_CASE_FUSED(1)
+    TN_GEMV_CASE_FUSED(2)
+    TN_GEMV_CASE_FUSED(4)
+    if (p.x_mode != X_PLANAR)
+        return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: fused prologue with M > 4");
+    if (M <= 8) TN_GEMV_LAUNCH(8, X_PLANAR)
+    if (M <= 16) TN_GEMV_LAUNCH(16, X_PLANAR)
+#undef TN_GEMV_CASE_FUSED
+#undef TN_GEMV_LAUNCH
     return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: GEMV called with M > 16");
 }
 
