@@ -163,15 +163,25 @@ __global__ void __launch_bounds__(256, 1) sdpa_prefill_kernel(const __grid_const
 #pragma unroll
             for (int i = 0; i < 32; ++i) sv[32 + i] = v[i];
         }
+        // Raw scores here; the scale is applied inside the exponent (c2 > 0, so
+        // the maximum of the raw scores scales to the maximum of the scaled).
+        // Only tiles that reach the diagonal or the key range end need masks.
         float mx = -INFINITY;
         const int kbase = j * BN + wg * 64;
+        const bool full = (j + 1) * BN <= a.S && (!a.causal || (j + 1) * BN - 1 <= q0);
+        if (full) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-            const int key = kbase + c;
-            const bool masked = key >= a.S || (a.causal && key > row);
-            sv[c] = masked ? -INFINITY : sv[c] * c2;
-            mx = fmaxf(mx, sv[c]);
+            for (int c = 0; c < 64; ++c) mx = fmaxf(mx, sv[c]);
+        } else {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                const int key = kbase + c;
+                const bool masked = key >= a.S || (a.causal && key > row);
+                sv[c] = masked ? -INFINITY : sv[c];
+                mx = fmaxf(mx, sv[c]);
+            }
         }
+        mx = mx * c2;
         xch[wg * 128 + r] = mx;
         tc05::fence_before();
         asm volatile("bar.sync 1, 256;" ::: "memory");
@@ -184,11 +194,16 @@ __global__ void __launch_bounds__(256, 1) sdpa_prefill_kernel(const __grid_const
         const float m_new = fmaxf(m2, mx);
         const float alpha = (m2 == -INFINITY) ? 0.0f : exp2f(m2 - m_new);
         float sum = 0.0f;
+        if (m_new == -INFINITY) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-            const float p = (m_new == -INFINITY) ? 0.0f : exp2f(sv[c] - m_new);
-            sv[c] = p;
-            sum += p;
+            for (int c = 0; c < 64; ++c) sv[c] = 0.0f;
+        } else {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                const float p = exp2f(fmaf(sv[c], c2, -m_new));
+                sv[c] = p;
+                sum += p;
+            }
         }
         l_part = l_part * alpha + sum;
         m2 = m_new;
