@@ -332,6 +332,32 @@ TN_API int tn_tp_allgather(void *const *bases, int rank, int world, const void *
                            void *stream);
 TN_API int tn_tp_step_end(void *local_base, void *stream);
 
+/* The all-gather fused into the Q4_0 GEMV itself. As producer (slot >= 0)
+ * the GEMV stores its output rows straight into every rank's region (row m,
+ * columns [rank*N_out, (rank+1)*N_out) of the [M][dst_row_stride] buffer at
+ * byte dst_offset of the data area, N_out its output columns) instead of y,
+ * and its last CTA signals every rank; as consumer (wait_slot >= 0) it waits,
+ * bounded, until every rank's producer of wait_slot has signalled this step
+ * before reading its activations. Slots share the numbering of
+ * tn_tp_allgather; a slot is fed either by tn_tp_allgather or by fused
+ * producers, never both. */
+typedef struct {
+    int world, rank;
+    void *bases[8];
+    int64_t dst_offset;
+    int64_t dst_row_stride;
+    int slot;
+    int wait_slot;
+} tn_tp_link;
+TN_API int tn_q4_0_linear_q8_tp(const int8_t *codes, int64_t codes_row_stride, const float *scales,
+                                const float *offsets, const void *w_blob, const float *bias, void *y,
+                                int y_dtype, int64_t M, int64_t N, int64_t K, int flags,
+                                const tn_tp_link *link, void *stream);
+TN_API int tn_q4_0_linear_fused_tp(int x_mode, const void *x, int64_t x_row_stride, const void *delta,
+                                   void *h_out, const void *norm_weight, float eps, const void *w_blob,
+                                   const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
+                                   int flags, const tn_tp_link *link, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

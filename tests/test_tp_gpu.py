@@ -59,7 +59,7 @@ def _gather_worker(rank, world, port, out):
                 r_i = torch.arange(rows, device=dev).view(rows, 1)
                 c_i = torch.arange(c, device=dev).view(1, c)
                 local = (1000 * (rank + 1) + 100 * k + 10 * step + r_i * c + c_i).to(torch.int16)
-                x.allgather(local, off, world * c, ctypes.c_void_p(s))
+                x.allgather(local, off, world * c, k, ctypes.c_void_p(s))
                 torch.cuda.synchronize()
                 want = torch.cat([(1000 * (g + 1) + 100 * k + 10 * step + r_i * c + c_i).to(torch.int16)
                                   for g in range(world)], dim=1)

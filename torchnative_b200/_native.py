@@ -29,6 +29,14 @@ TN_X_BF16, TN_X_RMSNORM, TN_X_SILU_MUL = 1, 2, 3
 
 # Every entry point declared in include/torchnative_b200.h, with its ctypes signature.
 _P, _I, _I64, _SZ, _D = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_double
+
+
+class TpLink(ctypes.Structure):
+    """tn_tp_link (include/torchnative_b200.h): a GEMV's place in a
+    tensor-parallel gather, as producer (slot) and/or consumer (wait_slot)."""
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("bases", ctypes.c_void_p * 8),
+                ("dst_offset", ctypes.c_int64), ("dst_row_stride", ctypes.c_int64), ("slot", ctypes.c_int),
+                ("wait_slot", ctypes.c_int)]
 _PI64 = ctypes.POINTER(ctypes.c_int64)
 
 
@@ -78,6 +86,9 @@ SIGNATURES = {
     "tn_tp_region_data_offset": (_I64, []),
     "tn_tp_allgather": (_I, [_P, _I, _I, _P, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     "tn_tp_step_end": (_I, [_P, _P]),
+    "tn_q4_0_linear_q8_tp": (_I, [_P, _I64, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P, _P]),
+    "tn_q4_0_linear_fused_tp": (_I, [_I, _P, _I64, _P, _P, _P, ctypes.c_float, _P, _P, _P, _I, _I64, _I64, _I64, _I,
+                                     _P, _P]),
 }
 
 _lib = None

@@ -65,6 +65,11 @@ struct GemvParams {
     const __nv_bfloat16 *xw;     // X_NORM: RMSNorm weight
     float eps;
     int64_t xb_row_stride;       // elements
+    // Tensor parallelism (tn_tp_link): scatter the output into every rank's
+    // exchange region (tp_slot >= 0) and/or wait for a gathered input.
+    int tp_world, tp_rank, tp_slot, tp_wait;
+    int64_t tp_dst_off, tp_dst_row, tp_cols;
+    uint8_t *tp_bases[kTpMaxRanks];
 };
 
 // Shared-memory layout (dynamic), as 32-bit shared-window addresses:
@@ -448,6 +453,19 @@ __device__ __forceinline__ void stage_x(const Smem &s, const GemvParams &p, int 
     }
 }
 
+// Output column n of row m: into y, or (tensor-parallel producer) into this
+// rank's columns of the gathered buffer in its exchange region.
+__device__ __forceinline__ void store_y(const GemvParams &p, int m, int64_t n, float v) {
+    if (p.tp_slot < 0) {
+        store_out(p.y, p.y_dtype, m * p.y_row_stride + n, v);
+        return;
+    }
+    // this rank's own region only; the launch's last CTA pushes the finished
+    // slice to the other ranks in 16-byte pieces
+    const int64_t idx = m * p.tp_dst_row + (int64_t)p.tp_rank * p.tp_cols + n;
+    store_out(p.tp_bases[p.tp_rank] + kTpDataOff + p.tp_dst_off, p.y_dtype, idx, v);
+}
+
 // Reduce-scatter across the warp: V = 2*MT values per lane (row r, column m at
 // index r*MT + m). After log2(V) butterfly levels each lane holds a partial of
 // one value, index lane >> (5 - log2 V); the remaining levels finish the sum.
@@ -485,14 +503,14 @@ __device__ __forceinline__ void finish_rows(float (&acc)[2][MT], const GemvParam
         const float u = __shfl_down_sync(0xffffffffu, t, 16);
         if ((lane & ((1 << (5 - LOGV)) - 1)) == 0 && r == 0 && m < p.M) {
             const float g = bfr(t), up = bfr(u);
-            store_out(p.y, p.y_dtype, m * p.y_row_stride + (n0 >> 1), bfr(bfr(g / (1.0f + expf(-g))) * up));
+            store_y(p, m, n0 >> 1, bfr(bfr(g / (1.0f + expf(-g))) * up));
         }
         return;
     }
     if ((lane & ((1 << (5 - LOGV)) - 1)) == 0 && m < p.M && (r == 0 || has_b)) {
         const int64_t n = n0 + r;
         if (p.bias) t = t + __ldg(p.bias + n);
-        store_out(p.y, p.y_dtype, m * p.y_row_stride + n, t);
+        store_y(p, m, n, t);
     }
 }
 
@@ -608,6 +626,14 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
 
     // ---------------- consumers
     pdl_wait();  // the activations may come from the previous kernel in the stream
+    if (p.tp_wait >= 0) {  // gathered activations: every rank's producer has signalled this step
+        if (threadIdx.x == 0) {
+            const uint8_t *lb = p.tp_bases[p.tp_rank];
+            const int epoch = ld_acquire_sys(reinterpret_cast<const int *>(lb + kTpEpochOff));
+            tp_wait_counts(lb, p.tp_wait, p.tp_world, epoch + 1, p.err);
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    }
     if constexpr (XM == X_PLANAR) {
         stage_x(s, p, threadIdx.x, kConsumerWarps * 32);
     } else {
@@ -617,7 +643,8 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
     const int group = warp / wpc, gw = warp % wpc;
-    for (int j = group; j < nchunks; j += groups) {
+    bool failed = false;
+    for (int j = group; j < nchunks && !failed; j += groups) {
         const int i = j * R + 2 * gw;  // my first row within the CTA's range
         const bool has_a = i < nrows, has_b = i + 1 < nrows;
         float acc[2][MT];
@@ -629,7 +656,8 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
             const int slot = j % p.nslots;
             if (!mbar_wait(&s.full[slot], (j / p.nslots) & 1)) {
                 record_device_error(p.err, DEV_ERR_WAIT_FULL);
-                return;
+                failed = true;
+                break;
             }
             const uint32_t ra = s.slots + (uint32_t)slot * p.slot_bytes + (uint32_t)(2 * gw) * p.rowbytes;
             if (has_b)
@@ -646,6 +674,57 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
                 global_rows<MT, false>(s, p, ra, ra, lane, acc);
         }
         if (has_a) finish_rows<MT>(acc, p, r0 + i, has_b, lane);
+    }
+    if (p.tp_slot >= 0) {
+        // Every consumer's rows are stored in this rank's region. The launch's
+        // last CTA (ticket) copies the whole slice to every other rank, fences
+        // system-wide and signals every rank -- also after a failed wait, so
+        // that peers do not stall.
+        __shared__ int tp_last;
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        if (threadIdx.x == 0) {
+            __threadfence();
+            int *ticket = reinterpret_cast<int *>(p.tp_bases[p.tp_rank] + kTpTicketOff) + p.tp_slot;
+            tp_last = atomicAdd(ticket, 1) == (int)gridDim.x - 1;
+            if (tp_last) {
+                *ticket = 0;
+                __threadfence();
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        if (tp_last) {
+            const int nthr = kConsumerWarps * 32;
+            const int64_t es = p.y_dtype == TN_F32 ? 4 : 2;
+            const int64_t row_b = p.tp_cols * es, col0 = (int64_t)p.tp_rank * row_b, stride_b = p.tp_dst_row * es;
+            const uint8_t *src = p.tp_bases[p.tp_rank] + kTpDataOff + p.tp_dst_off;
+            if (((row_b | col0 | stride_b | p.tp_dst_off) & 15) == 0) {
+                const int64_t per = row_b / 16, n = (int64_t)p.M * per;
+                for (int64_t i = threadIdx.x; i < n; i += nthr) {
+                    const int64_t off = (i / per) * stride_b + col0 + (i % per) * 16;
+                    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(src + off));
+                    for (int g = 0; g < p.tp_world; ++g)
+                        if (g != p.tp_rank)
+                            *reinterpret_cast<uint4 *>(p.tp_bases[g] + kTpDataOff + p.tp_dst_off + off) = v;
+                }
+            } else {
+                const int64_t per = row_b / 2, n = (int64_t)p.M * per;
+                for (int64_t i = threadIdx.x; i < n; i += nthr) {
+                    const int64_t off = (i / per) * stride_b + col0 + (i % per) * 2;
+                    const unsigned short v = __ldcg(reinterpret_cast<const unsigned short *>(src + off));
+                    for (int g = 0; g < p.tp_world; ++g)
+                        if (g != p.tp_rank)
+                            *reinterpret_cast<unsigned short *>(p.tp_bases[g] + kTpDataOff + p.tp_dst_off + off) = v;
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+            if (threadIdx.x == 0) {
+                __threadfence_system();
+                for (int g = 0; g < p.tp_world; ++g)
+                    atomicAdd_system(reinterpret_cast<int *>(p.tp_bases[g] + kTpCountOff) +
+                                         p.tp_slot * p.tp_world + p.tp_rank,
+                                     1);
+            }
+        }
     }
 }
 
@@ -793,10 +872,29 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
 
 }  // namespace
 
+namespace {
+
+void set_link(GemvParams &p, const tn_tp_link *link, int64_t out_cols) {
+    p.tp_slot = p.tp_wait = -1;
+    p.tp_world = 1;
+    if (!link) return;
+    p.tp_world = link->world;
+    p.tp_rank = link->rank;
+    p.tp_slot = link->slot;
+    p.tp_wait = link->wait_slot;
+    p.tp_dst_off = link->dst_offset;
+    p.tp_dst_row = link->dst_row_stride;
+    p.tp_cols = out_cols;
+    for (int g = 0; g < kTpMaxRanks; ++g) p.tp_bases[g] = g < link->world ? static_cast<uint8_t *>(link->bases[g]) : nullptr;
+}
+
+}  // namespace
+
 int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
                       const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
-                      int flags, cudaStream_t stream) {
+                      int flags, cudaStream_t stream, const tn_tp_link *link) {
     GemvParams p{};
+    set_link(p, link, (flags & TN_EPILOGUE_SILU_MUL_PAIRS) ? N / 2 : N);
     p.w = w;
     p.xq = xq;
     p.xd = xd;
@@ -812,8 +910,10 @@ int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const
 
 int launch_q4_gemv_fused(int x_mode, const void *xb, int64_t xb_row_stride, const void *xdelta, void *xh_out,
                          const void *norm_w, float eps, const uint8_t *w, const float *bias, void *y, int y_dtype,
-                         int64_t y_row_stride, int M, int64_t N, int64_t K, int flags, cudaStream_t stream) {
+                         int64_t y_row_stride, int M, int64_t N, int64_t K, int flags, cudaStream_t stream,
+                         const tn_tp_link *link) {
     GemvParams p{};
+    set_link(p, link, (flags & TN_EPILOGUE_SILU_MUL_PAIRS) ? N / 2 : N);
     p.w = w;
     p.bias = bias;
     p.y = y;

@@ -31,13 +31,14 @@ int q4_gemv_max_rows(int64_t K);
 // Decode GEMV over planar Q8_0 activations: y[m, n] for m < M (M <= 16).
 int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
                       const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
-                      int flags, cudaStream_t stream);
+                      int flags, cudaStream_t stream, const tn_tp_link *link = nullptr);
 
 // Decode GEMV whose planar Q8_0 activations are built in each CTA from bf16
 // rows (x_mode: 1 = x itself, 2 = RMSNorm(h + delta) with h + delta written to
 // xh_out by CTA 0, 3 = silu(gate) * up from [gate | up] rows); M <= 4.
 int launch_q4_gemv_fused(int x_mode, const void *xb, int64_t xb_row_stride, const void *xdelta, void *xh_out,
                          const void *norm_w, float eps, const uint8_t *w, const float *bias, void *y, int y_dtype,
-                         int64_t y_row_stride, int M, int64_t N, int64_t K, int flags, cudaStream_t stream);
+                         int64_t y_row_stride, int M, int64_t N, int64_t K, int flags, cudaStream_t stream,
+                         const tn_tp_link *link = nullptr);
 
 }  // namespace tn

@@ -5,6 +5,25 @@
 // activation rows.
 #include "q4_kernels.cuh"
 
+namespace tn {
+namespace {
+
+int check_link(const std::string &op, const tn_tp_link *l, int64_t out_cols) {
+    if (l->world < 1 || l->world > kTpMaxRanks || l->rank < 0 || l->rank >= l->world)
+        return set_error(TN_ERR_INVALID, op + ": tensor-parallel link: rank/world out of range (at most 8 ranks)");
+    for (int g = 0; g < l->world; ++g)
+        if (!l->bases[g]) return set_error(TN_ERR_INVALID, op + ": tensor-parallel link: null region base");
+    const int64_t max_slot = (kTpTicketOff - kTpCountOff) / 4 / l->world;
+    if (l->slot >= max_slot || l->wait_slot >= max_slot)
+        return set_error(TN_ERR_INVALID, op + ": tensor-parallel link: slot out of range");
+    if (l->slot >= 0 && (l->dst_offset < 0 || l->dst_row_stride < l->world * out_cols))
+        return set_error(TN_ERR_SHAPE, op + ": tensor-parallel link: destination row stride below world * columns");
+    return TN_OK;
+}
+
+}  // namespace
+}  // namespace tn
+
 extern "C" int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob, const float *bias,
                               void *y, int y_dtype, int64_t M, int64_t N, int64_t K, int act_mode, void *stream_) {
     const std::string op = "torch._C._quantized_linear";
@@ -95,9 +114,10 @@ extern "C" int tn_q8_0_quantize_planar(const void *x, int x_dtype, int64_t x_row
                                 static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, const float *scales,
-                                 const float *offsets, const void *w_blob, const float *bias, void *y, int y_dtype,
-                                 int64_t M, int64_t N, int64_t K, int flags, void *stream_) {
+extern "C" int tn_q4_0_linear_q8_tp(const int8_t *codes, int64_t codes_row_stride, const float *scales,
+                                    const float *offsets, const void *w_blob, const float *bias, void *y,
+                                    int y_dtype, int64_t M, int64_t N, int64_t K, int flags,
+                                    const tn_tp_link *link, void *stream_) {
     const std::string op = "torch._C._quantized_linear";
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
@@ -121,21 +141,35 @@ extern "C" int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, 
     if (pairs && (N % 2 != 0 || y_dtype != TN_BF16))
         return tn::set_error(TN_ERR_INVALID, op + ": the SiLU*up pair epilogue needs an even N and a bf16 output");
     const int64_t ycols = pairs ? N / 2 : N;
+    if (link) {
+        int st = tn::check_link(op, link, ycols);
+        if (st) return st;
+        if (M > chunk) return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": a tensor-parallel link needs one launch (M <= " +
+                                                                        std::to_string(chunk) + ")");
+    }
     const size_t ysz = tn_dtype_size(y_dtype);
     for (int64_t m0 = 0; m0 < M; m0 += chunk) {
         const int mc = (int)((M - m0) < chunk ? (M - m0) : chunk);
         int st = tn::launch_q4_gemv_q8(static_cast<const uint8_t *>(w_blob), codes + m0 * codes_row_stride,
                                        scales + m0 * nb, offsets + m0 * nb, codes_row_stride, bias,
                                        static_cast<uint8_t *>(y) + (size_t)m0 * ycols * ysz, y_dtype, ycols, mc, N,
-                                       K, flags, stream);
+                                       K, flags, stream, link);
         if (st) return st;
     }
     return TN_OK;
 }
 
-extern "C" int tn_q4_0_linear_fused(int x_mode, const void *x, int64_t x_row_stride, const void *delta, void *h_out,
-                                    const void *norm_weight, float eps, const void *w_blob, const float *bias,
-                                    void *y, int y_dtype, int64_t M, int64_t N, int64_t K, int flags, void *stream) {
+extern "C" int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, const float *scales,
+                                 const float *offsets, const void *w_blob, const float *bias, void *y, int y_dtype,
+                                 int64_t M, int64_t N, int64_t K, int flags, void *stream) {
+    return tn_q4_0_linear_q8_tp(codes, codes_row_stride, scales, offsets, w_blob, bias, y, y_dtype, M, N, K, flags,
+                                nullptr, stream);
+}
+
+extern "C" int tn_q4_0_linear_fused_tp(int x_mode, const void *x, int64_t x_row_stride, const void *delta,
+                                       void *h_out, const void *norm_weight, float eps, const void *w_blob,
+                                       const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
+                                       int flags, const tn_tp_link *link, void *stream) {
     const std::string op = "tn_q4_0_linear_fused";
     __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
     if (x_mode != TN_X_BF16 && x_mode != TN_X_RMSNORM && x_mode != TN_X_SILU_MUL)
@@ -163,7 +197,18 @@ extern "C" int tn_q4_0_linear_fused(int x_mode, const void *x, int64_t x_row_str
     const bool pairs = (flags & TN_EPILOGUE_SILU_MUL_PAIRS) != 0;
     if (pairs && (N % 2 != 0 || y_dtype != TN_BF16))
         return tn::set_error(TN_ERR_INVALID, op + ": the SiLU*up pair epilogue needs an even N and a bf16 output");
+    if (link) {
+        int st = tn::check_link(op, link, pairs ? N / 2 : N);
+        if (st) return st;
+    }
     return tn::launch_q4_gemv_fused(x_mode, x, x_row_stride, delta, h_out, norm_weight, eps,
                                     static_cast<const uint8_t *>(w_blob), bias, y, y_dtype, pairs ? N / 2 : N, (int)M,
-                                    N, K, flags, static_cast<cudaStream_t>(stream));
+                                    N, K, flags, static_cast<cudaStream_t>(stream), link);
+}
+
+extern "C" int tn_q4_0_linear_fused(int x_mode, const void *x, int64_t x_row_stride, const void *delta, void *h_out,
+                                    const void *norm_weight, float eps, const void *w_blob, const float *bias,
+                                    void *y, int y_dtype, int64_t M, int64_t N, int64_t K, int flags, void *stream) {
+    return tn_q4_0_linear_fused_tp(x_mode, x, x_row_stride, delta, h_out, norm_weight, eps, w_blob, bias, y, y_dtype,
+                                   M, N, K, flags, nullptr, stream);
 }

@@ -137,6 +137,40 @@ __device__ __forceinline__ void record_device_error(int *word, int code) {
     if (word) atomicCAS(word, 0, code);
 }
 
+// ---- tensor-parallel exchange regions (tp_comm.cu, and the GEMV epilogue
+// that scatters its output rows straight into every rank's region) --------
+//   [0, 4)                  epoch: steps this rank has completed
+//   [64, 32768)             counters[slot][src]
+//   [32768, 65536)          tickets[slot]: CTAs of this rank's producer kernel done
+//   [65536, ...)            gathered activation rows
+constexpr int64_t kTpEpochOff = 0, kTpCountOff = 64, kTpTicketOff = 32768, kTpDataOff = 65536;
+constexpr int kTpMaxRanks = 8;
+
+__device__ __forceinline__ int ld_acquire_sys(const int *p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait until counters[slot][g] >= target for every source rank g of
+// this rank's region (one thread). False if it gave up (error recorded) or an
+// earlier wait already had.
+__device__ __forceinline__ bool tp_wait_counts(const uint8_t *local_base, int slot, int world, int target, int *err) {
+    const int *cnt = reinterpret_cast<const int *>(local_base + kTpCountOff) + slot * world;
+    for (int g = 0; g < world; ++g) {
+        if (ld_acquire_sys(cnt + g) >= target) continue;
+        if (err && *reinterpret_cast<volatile int *>(err) != 0) return false;
+        const long long start = clock64();
+        while (ld_acquire_sys(cnt + g) < target) {
+            if (clock64() - start > kWaitBudgetCycles) {
+                record_device_error(err, DEV_ERR_WAIT_FULL);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
 // Programmatic dependent launch: wait for the producer grid's memory, and let
 // the next grid start its prologue.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

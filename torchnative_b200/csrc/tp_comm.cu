@@ -5,8 +5,11 @@
 // Every rank owns one exchange region (cudaMalloc'd, shared with the other
 // ranks through CUDA IPC handles, plain peer mappings -- no multicast):
 //   [0, 4)             epoch: steps this rank has completed (tn_tp_step_end)
-//   [64, 64 + 4 S G)   counters[slot][src]: CTAs of rank src that finished
-//                      writing this rank's copy of gather `slot`
+//   [64, 32768)        counters[slot][src]: for this kernel's gathers, CTAs of
+//                      rank src that finished writing this rank's copy of
+//                      gather `slot`; for gathers fused into a GEMV's epilogue
+//                      (q4_gemv.cu), launches of rank src that finished
+//   [32768, 65536)     tickets[slot]: the fused producer's finished CTAs
 //   [65536, ...)       the gathered activation rows, at caller-chosen offsets
 // One gather: every rank stores its [rows][cols] slice straight into every
 // rank's region (row r, columns [rank * cols, (rank + 1) * cols) of a
@@ -24,18 +27,12 @@
 namespace tn {
 namespace {
 
-constexpr int64_t kEpochOff = 0, kCountOff = 64, kDataOff = 65536;
-constexpr int kMaxRanks = 8;
+constexpr int64_t kEpochOff = kTpEpochOff, kCountOff = kTpCountOff, kDataOff = kTpDataOff;
+constexpr int kMaxRanks = kTpMaxRanks;
 
 struct Bases {
     uint8_t *p[kMaxRanks];
 };
-
-__device__ __forceinline__ int ld_acquire_sys(const int *p) {
-    int v;
-    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 __global__ void __launch_bounds__(256) tp_allgather_kernel(Bases bases, int rank, int world, const uint8_t *local,
                                                            int64_t local_row_bytes, int rows, int64_t row_bytes,
@@ -142,7 +139,7 @@ int tn_tp_allgather(void *const *bases, int rank, int world, const void *local, 
     if (world < 1 || world > tn::kMaxRanks || rank < 0 || rank >= world)
         return tn::set_error(TN_ERR_INVALID, std::string(op) + ": rank/world out of range (at most 8 ranks)");
     if (rows < 0 || cols < 0 || local_row_stride < cols || dst_row_stride < world * cols || slot < 0 ||
-        (int64_t)(slot + 1) * world * 4 > tn::kDataOff - tn::kCountOff)
+        (int64_t)(slot + 1) * world * 4 > tn::kTpTicketOff - tn::kCountOff)
         return tn::set_error(TN_ERR_SHAPE, std::string(op) + ": bad shape, stride or slot");
     if (!bases || !local) return tn::set_error(TN_ERR_INVALID, std::string(op) + ": null pointer");
     tn::Bases b{};

@@ -174,20 +174,39 @@ class Q4LlamaDecoder:
         # split-merge inside the SDPA launch: 6 kernels a layer. Larger batches
         # use the separate kernels.
         self.fused = batch <= 4
+        # With the peer-memory exchange, the o_proj and down_proj gathers run
+        # inside those GEMVs (rows scattered to every rank, the next RMSNorm GEMV
+        # waits); the attention, SiLU*up and logits gathers stay separate launches.
+        self.fused_gather = self.fused and self.xchg is not None
+        self._links = self._build_links()
 
-    def _gather(self, local: torch.Tensor, full: torch.Tensor, stream) -> None:
-        """The all-gather after a sharded output (nothing on one GPU)."""
+    def _off(self, full: torch.Tensor) -> int:
+        return {self.attn.data_ptr(): self._off_attn, self.delta.data_ptr(): self._off_delta,
+                self.act.data_ptr(): self._off_act, self.logits.data_ptr(): self._off_logits}[full.data_ptr()]
+
+    def _gather(self, local: torch.Tensor, full: torch.Tensor, slot: int, stream) -> None:
+        """The all-gather after a sharded output (nothing on one GPU). Slots
+        number the gathers of a step: 4 per layer (attention, o_proj, SiLU*up,
+        down_proj), then the logits."""
         if self.tp is None:
             return
         local2d, full2d = local.reshape(self.B, -1), full.view(self.B, -1)
         if self.xchg is not None:
-            off = {self.attn.data_ptr(): self._off_attn, self.delta.data_ptr(): self._off_delta,
-                   self.act.data_ptr(): self._off_act, self.logits.data_ptr(): self._off_logits}[full.data_ptr()]
-            self.xchg.allgather(local2d, off, full2d.shape[1], stream)
+            self.xchg.allgather(local2d, self._off(full), full2d.shape[1], slot, stream)
             return
         from . import tp as tpm
 
         tpm.gather_rows(self.tp, local2d, full2d, self.gather_scratch, stream)
+
+    def _link(self, slot: int = -1, full: torch.Tensor | None = None, wait_slot: int = -1):
+        """tn_tp_link for a GEMV whose output feeds gather `slot` (written into
+        `full` on every rank) and/or that reads gather `wait_slot`; None when
+        the gathers are not fused (one GPU, or NCCL)."""
+        if self.xchg is None or not self.fused_gather:
+            return None
+        if slot >= 0:
+            return self.xchg.link(slot, self._off(full), full.view(self.B, -1).shape[1], wait_slot)
+        return self.xchg.link(wait_slot=wait_slot)
 
     def _step_end(self, stream) -> None:
         if self.xchg is not None:
@@ -221,7 +240,7 @@ class Q4LlamaDecoder:
         """Our kernels per layer: the peer-memory all-gathers are ours, NCCL's
         are not (they add the layout step at batch > 1)."""
         if self.xchg is not None:
-            extra = 4
+            extra = 2 if self.fused_gather else 4
         else:
             extra = 4 if (self.tp is not None and self.B > 1) else 0
         return (6 if self.fused else 11) + extra
@@ -260,10 +279,11 @@ class Q4LlamaDecoder:
     def _stream():
         return P(torch.cuda.current_stream().cuda_stream)
 
-    def _linear(self, w, y, n, k, stream, flags=0):
-        N.check(N.lib().tn_q4_0_linear_q8(P(self.codes.data_ptr()), k, P(self.scales.data_ptr()),
-                                          P(self.offsets.data_ptr()), P(w.data_ptr()), None, P(y.data_ptr()),
-                                          N.TN_BF16, self.B, n, k, N.TN_WEIGHTS_STATIC | flags, stream))
+    def _linear(self, w, y, n, k, stream, flags=0, link=None):
+        N.check(N.lib().tn_q4_0_linear_q8_tp(P(self.codes.data_ptr()), k, P(self.scales.data_ptr()),
+                                             P(self.offsets.data_ptr()), P(w.data_ptr()), None, P(y.data_ptr()),
+                                             N.TN_BF16, self.B, n, k, N.TN_WEIGHTS_STATIC | flags,
+                                             None if link is None else ctypes.addressof(link), stream))
 
     def _norm(self, delta, weight, stream):
         N.check(N.lib().tn_llama_add_rmsnorm_q8(P(self.h.data_ptr()), None if delta is None else P(delta.data_ptr()),
@@ -291,72 +311,95 @@ class Q4LlamaDecoder:
                                            P(self.attn_l.data_ptr()), None, N.TN_BF16, B, Hq, Hkv, D, self.cap,
                                            self._qstr, self._kstr, self._kstr, P(self.pos.data_ptr()), 1,
                                            1.0 / math.sqrt(D), stream))
-            self._gather(self.attn_l, self.attn, stream)
+            self._gather(self.attn_l, self.attn, 4 * li, stream)
             HD = s.heads * D
             N.check(L.tn_q8_0_quantize_planar(P(self.attn.data_ptr()), N.TN_BF16, HD, P(self.codes.data_ptr()),
                                               HD, P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, HD,
                                               stream))
             self._linear(lw["o"], self.delta_l, self.h_l, HD, stream)
-            self._gather(self.delta_l, self.delta, stream)
+            self._gather(self.delta_l, self.delta, 4 * li + 1, stream)
             self._norm(self.delta, lw["mlp_norm"], stream)
             self._linear(lw["gate_up"], self.act_l, 2 * self.i_l, s.hidden, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS)
-            self._gather(self.act_l, self.act, stream)
+            self._gather(self.act_l, self.act, 4 * li + 2, stream)
             N.check(L.tn_q8_0_quantize_planar(P(self.act.data_ptr()), N.TN_BF16, s.inter, P(self.codes.data_ptr()),
                                               s.inter, P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B,
                                               s.inter, stream))
             self._linear(lw["down"], self.delta_l, self.h_l, s.inter, stream)
-            self._gather(self.delta_l, self.delta, stream)
+            self._gather(self.delta_l, self.delta, 4 * li + 3, stream)
         self._norm(self.delta, self.final_norm, stream)
         self._linear(self.lm_head, self.logits_l, self.v_l, s.hidden, stream)
-        self._gather(self.logits_l, self.logits, stream)
+        self._gather(self.logits_l, self.logits, 4 * self.n_layers, stream)
         N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
                                         P(self.embed.data_ptr()), s.hidden, P(self.h.data_ptr()),
                                         P(self.pos.data_ptr()), stream))
         self._step_end(stream)
 
-    def _fused_linear(self, mode, x, x_stride, delta, h_out, norm_w, w, y, n, k, stream, flags=0):
-        N.check(N.lib().tn_q4_0_linear_fused(mode, P(x.data_ptr()), x_stride,
-                                             None if delta is None else P(delta.data_ptr()),
-                                             None if h_out is None else P(h_out.data_ptr()),
-                                             None if norm_w is None else P(norm_w.data_ptr()), self.s.eps,
-                                             P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, self.B, n, k,
-                                             N.TN_WEIGHTS_STATIC | flags, stream))
+    def _fused_linear(self, mode, x, x_stride, delta, h_out, norm_w, w, y, n, k, stream, flags=0, link=None):
+        N.check(N.lib().tn_q4_0_linear_fused_tp(mode, P(x.data_ptr()), x_stride,
+                                                None if delta is None else P(delta.data_ptr()),
+                                                None if h_out is None else P(h_out.data_ptr()),
+                                                None if norm_w is None else P(norm_w.data_ptr()), self.s.eps,
+                                                P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, self.B, n, k,
+                                                N.TN_WEIGHTS_STATIC | flags,
+                                                None if link is None else ctypes.addressof(link), stream))
 
     def _step_fused(self, stream) -> None:
         L, s, B = N.lib(), self.s, self.B
         D, Hq, Hkv, H, I = s.head_dim, self.hq, self.hkv, s.hidden, s.inter  # local heads
         HD = s.heads * D
         ha, hb = self.h, self.h2
+        fg = self.xchg is not None and self.fused_gather
+        links = self._links  # built once per (decoder); ctypes structs must outlive the launches
         for li, lw in enumerate(self.layers):
             # residual: hb = ha + (previous layer's down_proj); qkv = Q4(RMSNorm(hb))
             self._fused_linear(N.TN_X_RMSNORM, ha, H, None if li == 0 else self.delta, hb, lw["attn_norm"],
-                               lw["qkv"], self.qkv_out, self.qkv_l, H, stream)
+                               lw["qkv"], self.qkv_out, self.qkv_l, H, stream,
+                               link=links[("qkv", li)] if fg and li > 0 else None)
             kc, vc = self.k_cache[li], self.v_cache[li]
             N.check(L.tn_sdpa_decode_step(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()), P(kc.data_ptr()),
                                           P(vc.data_ptr()), P(self.attn_l.data_ptr()), None, B, Hq, Hkv, D, self.cap,
                                           self._kstr, self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D),
                                           stream))
-            self._gather(self.attn_l, self.attn, stream)
+            self._gather(self.attn_l, self.attn, 4 * li, stream)
             self._fused_linear(N.TN_X_BF16, self.attn, HD, None, None, None, lw["o"], self.delta_l, self.h_l, HD,
-                               stream)
-            self._gather(self.delta_l, self.delta, stream)
+                               stream, link=links[("o", li)] if fg else None)
+            if not fg:
+                self._gather(self.delta_l, self.delta, 4 * li + 1, stream)
             # residual: ha = hb + o_proj; act = SiLU(gate) * up of Q4(RMSNorm(ha))
             self._fused_linear(N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act_l,
-                               2 * self.i_l, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS)
-            self._gather(self.act_l, self.act, stream)
+                               2 * self.i_l, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS,
+                               link=links[("gate_up", li)] if fg else None)
+            self._gather(self.act_l, self.act, 4 * li + 2, stream)
             # the activation quantiser once (not in each of the down GEMV's CTAs:
             # 448 blocks per CTA cost more than a launch), then the planar GEMV
             N.check(L.tn_q8_0_quantize_planar(P(self.act.data_ptr()), N.TN_BF16, I, P(self.codes.data_ptr()), I,
                                               P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, I, stream))
-            self._linear(lw["down"], self.delta_l, self.h_l, I, stream)
-            self._gather(self.delta_l, self.delta, stream)
+            self._linear(lw["down"], self.delta_l, self.h_l, I, stream, link=links[("down", li)] if fg else None)
+            if not fg:
+                self._gather(self.delta_l, self.delta, 4 * li + 3, stream)
         self._fused_linear(N.TN_X_RMSNORM, ha, H, self.delta, hb, self.final_norm, self.lm_head, self.logits_l,
-                           self.v_l, H, stream)
-        self._gather(self.logits_l, self.logits, stream)
+                           self.v_l, H, stream, link=links[("lm_head", 0)] if fg else None)
+        self._gather(self.logits_l, self.logits, 4 * self.n_layers, stream)
         N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
                                         P(self.embed.data_ptr()), s.hidden, P(ha.data_ptr()),
                                         P(self.pos.data_ptr()), stream))
         self._step_end(stream)
+
+    def _build_links(self) -> dict:
+        """The fused gathers' links: o_proj and down_proj scatter their rows
+        into every rank's `delta` (slots 4l + 1, 4l + 3); the next RMSNorm GEMV
+        (gate/up, the next layer's q/k/v, lm_head) waits for them."""
+        if self.xchg is None or not self.fused_gather:
+            return {}
+        links = {}
+        for li in range(self.n_layers):
+            links[("o", li)] = self._link(slot=4 * li + 1, full=self.delta)
+            links[("gate_up", li)] = self._link(wait_slot=4 * li + 1)
+            links[("down", li)] = self._link(slot=4 * li + 3, full=self.delta)
+            if li > 0:
+                links[("qkv", li)] = self._link(wait_slot=4 * (li - 1) + 3)
+        links[("lm_head", 0)] = self._link(wait_slot=4 * (self.n_layers - 1) + 3)
+        return links
 
     def kernel_graphs(self) -> dict:
         """For timing the step's parts: one CUDA graph per kind of launch in

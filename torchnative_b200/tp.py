@@ -157,7 +157,6 @@ class PeerExchange:
             self.bases[g] = peer.value
             self._opened.append(peer.value)
         self._next = 0
-        self.slot = 0
 
     def buffer(self, rows: int, cols: int, dtype=torch.bfloat16) -> tuple[torch.Tensor, int]:
         """A [rows, cols] 16-bit gather destination in this rank's region and
@@ -170,16 +169,24 @@ class PeerExchange:
         t = torch.as_tensor(_DevicePointer(self.base + self.data_off + off, rows * cols), device=self.dev)
         return t.view(dtype).view(rows, cols), off
 
-    def allgather(self, local: torch.Tensor, dst_off: int, full_cols: int, stream) -> None:
-        """One gather of this step: local [rows, c] -> every rank's [rows, full_cols] at dst_off."""
+    def allgather(self, local: torch.Tensor, dst_off: int, full_cols: int, slot: int, stream) -> None:
+        """Gather `slot` of this step: local [rows, c] -> every rank's [rows, full_cols] at dst_off."""
         rows, c = local.shape
         N.check(N.lib().tn_tp_allgather(self.bases, self.tp.rank, self.tp.world, P(local.data_ptr()),
-                                        local.stride(0), rows, c, dst_off, full_cols, self.slot, stream))
-        self.slot += 1
+                                        local.stride(0), rows, c, dst_off, full_cols, slot, stream))
+
+    def link(self, slot: int = -1, dst_off: int = 0, full_cols: int = 0, wait_slot: int = -1) -> "N.TpLink":
+        """A tn_tp_link for a GEMV that feeds gather `slot` (its output scattered
+        into every rank's buffer at dst_off) and/or reads gather `wait_slot`."""
+        ln = N.TpLink()
+        ln.world, ln.rank = self.tp.world, self.tp.rank
+        for g in range(self.tp.world):
+            ln.bases[g] = self.bases[g]
+        ln.dst_offset, ln.dst_row_stride, ln.slot, ln.wait_slot = dst_off, full_cols, slot, wait_slot
+        return ln
 
     def step_end(self, stream) -> None:
         N.check(N.lib().tn_tp_step_end(P(self.base), stream))
-        self.slot = 0
 
     def close(self) -> None:
         """After a barrier that no rank passes with a gather in flight."""
