@@ -266,6 +266,15 @@ TN_API int tn_sdpa_decode_step(const void *qkv, const float *inv_freq, void *k_c
                                void *out, float *lse, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
                                int64_t capacity, const int64_t *k_strides, const int64_t *v_strides,
                                const int *pos_dev, double scale, void *stream);
+/* The same, and out also as the next Q4_0 linear's planar Q8_0 activation
+ * (codes [B][Hq D], scales / offsets [B][Hq D / 32]; the bytes
+ * tn_q8_0_quantize_planar writes for out), each KV head's merging CTA
+ * quantising its own rows. */
+TN_API int tn_sdpa_decode_step_q8(const void *qkv, const float *inv_freq, void *k_cache, void *v_cache,
+                                  void *out, float *lse, int8_t *codes, float *scales, float *offsets,
+                                  int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t capacity,
+                                  const int64_t *k_strides, const int64_t *v_strides, const int *pos_dev,
+                                  double scale, void *stream);
 
 /* ------------------------------------------------ decode-step glue (bf16) --
  * The work between the hot operators in one greedy token of transformers'

@@ -237,3 +237,47 @@ def test_decode_step_replays_as_one_graph(N, cuda_device, fused):
         replay.append(int(dec.tokens[0]))
     assert replay == eager
     assert int(dec.pos.item()) == 34
+
+
+def test_decode_attention_writes_the_planar_q8_of_its_output(N, cuda_device):
+    """tn_sdpa_decode_step_q8: the same bf16 output as tn_sdpa_decode_step,
+    and codes / scales / offsets byte-identical to tn_q8_0_quantize_planar
+    of that output (the o_proj GEMV then stages them directly)."""
+    from torchnative_b200.llama_decode import rope_inv_freq
+
+    g = torch.Generator().manual_seed(21)
+    B, Hq, Hkv, D, cap = 2, 32, 8, 128, 300
+    pos0 = 217
+    dev = cuda_device
+    qkv = torch.randn((B, (Hq + 2 * Hkv) * D), generator=g).to(torch.bfloat16).to(dev)
+    kc = torch.randn((B, Hkv, cap, D), generator=g).to(torch.bfloat16).to(dev)
+    vc = torch.randn((B, Hkv, cap, D), generator=g).to(torch.bfloat16).to(dev)
+    inv = rope_inv_freq(D, 500000.0).to(dev)
+    st = (ctypes.c_int64 * 4)(*kc.stride())
+    outs = []
+    for q8 in (False, True):
+        k2, v2 = kc.clone(), vc.clone()
+        pos = torch.tensor([pos0], dtype=torch.int32, device=dev)
+        out = torch.empty((B, Hq, D), device=dev, dtype=torch.bfloat16)
+        if q8:
+            codes = torch.zeros((B, Hq * D), device=dev, dtype=torch.int8)
+            scales = torch.zeros((B, Hq * D // 32), device=dev)
+            offs = torch.zeros((B, Hq * D // 32), device=dev)
+            N.check(N.lib().tn_sdpa_decode_step_q8(P(qkv.data_ptr()), P(inv.data_ptr()), P(k2.data_ptr()),
+                                                   P(v2.data_ptr()), P(out.data_ptr()), None, P(codes.data_ptr()),
+                                                   P(scales.data_ptr()), P(offs.data_ptr()), B, Hq, Hkv, D, cap, st, st,
+                                                   P(pos.data_ptr()), 1.0 / math.sqrt(D), _stream()))
+        else:
+            N.check(N.lib().tn_sdpa_decode_step(P(qkv.data_ptr()), P(inv.data_ptr()), P(k2.data_ptr()),
+                                                P(v2.data_ptr()), P(out.data_ptr()), None, B, Hq, Hkv, D, cap, st, st,
+                                                P(pos.data_ptr()), 1.0 / math.sqrt(D), _stream()))
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+    rc = torch.zeros_like(codes)
+    rs, ro = torch.zeros_like(scales), torch.zeros_like(offs)
+    K = Hq * D
+    N.check(N.lib().tn_q8_0_quantize_planar(P(outs[1].data_ptr()), N.TN_BF16, K, P(rc.data_ptr()), K,
+                                            P(rs.data_ptr()), P(ro.data_ptr()), B, K, _stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(codes, rc) and torch.equal(scales, rs) and torch.equal(offs, ro)
+    N.device_status(reset=True)

@@ -73,6 +73,8 @@ SIGNATURES = {
     "tn_sdpa_decode_cache": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _PI64, _P,
                                   _I64, _D, _P]),
     "tn_sdpa_decode_step": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _P, _D, _P]),
+    "tn_sdpa_decode_step_q8": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _P,
+                                    _D, _P]),
     "tn_llama_add_rmsnorm_q8": (_I, [_P, _P, _P, _P, ctypes.c_float, _I64, _I64, _P, _P, _P, _P]),
     "tn_llama_silu_mul_q8": (_I, [_P, _I64, _I64, _P, _P, _P, _P]),
     "tn_llama_rope_append": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64, _P]),

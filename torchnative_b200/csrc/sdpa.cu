@@ -161,7 +161,20 @@ extern "C" int tn_sdpa_decode_step(const void *qkv, const float *inv_freq, void 
                                    float *lse, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t capacity,
                                    const int64_t *k_strides, const int64_t *v_strides, const int *pos_dev,
                                    double scale, void *stream_) {
+    return tn_sdpa_decode_step_q8(qkv, inv_freq, k_cache, v_cache, out, lse, nullptr, nullptr, nullptr, B, Hq, Hkv,
+                                  D, capacity, k_strides, v_strides, pos_dev, scale, stream_);
+}
+
+extern "C" int tn_sdpa_decode_step_q8(const void *qkv, const float *inv_freq, void *k_cache, void *v_cache,
+                                      void *out, float *lse, int8_t *codes, float *scales, float *offsets,
+                                      int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t capacity,
+                                      const int64_t *k_strides, const int64_t *v_strides, const int *pos_dev,
+                                      double scale, void *stream_) {
     const std::string op = "tn_sdpa_decode_step";
+    if ((codes || scales || offsets) &&
+        (!codes || !scales || !offsets || (reinterpret_cast<uintptr_t>(codes) & 3) != 0))
+        return tn::set_error(TN_ERR_INVALID, op + ": planar Q8_0 output needs codes (4-byte aligned), scales and "
+                                                  "offsets");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     __atomic_fetch_add(&tn::counters().sdpa_calls, 1ull, __ATOMIC_RELAXED);
     if (D != 64 && D != 128)
@@ -213,5 +226,8 @@ extern "C" int tn_sdpa_decode_step(const void *qkv, const float *inv_freq, void 
     st = tn::workspace_zeroed(&cnt, (size_t)p.B * p.Hkv * sizeof(int) + 256, stream, /*slot=*/3);
     if (st) return st;
     p.counters = static_cast<int *>(cnt);
+    p.q8_codes = codes;
+    p.q8_scales = scales;
+    p.q8_offs = offsets;
     return tn::launch_sdpa_decode(p, TN_BF16, stream);
 }

@@ -35,6 +35,11 @@ struct SdpaParams {
     // If set, the last CTA of each (b, kv head) merges the splits itself
     // (counters start at zero and are left at zero).
     int *counters;
+    // If set (decode step, L = 1): the merge also writes out as planar Q8_0
+    // (codes [B][Hq D] int8, scales / offsets [B][Hq D / 32] f32), the bytes
+    // tn_q8_0_quantize_planar writes for the bf16 output.
+    int8_t *q8_codes;
+    float *q8_scales, *q8_offs;
     int *err;
 };
 

@@ -216,6 +216,43 @@ __device__ __forceinline__ void merge_if_last(const SdpaParams &p, int b, int kv
             else
                 static_cast<__half *>(p.out)[oi] = __float2half_rn(v4[e]);
         }
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+            if (p.q8_codes) {
+                // Planar Q8_0 of the bf16 output (k_quants.rs:676-706): the 8 lanes
+                // holding one 32-element block (consecutive d4) share its maximum
+                // and code sum.
+                const int lane = tid & 31;
+                const unsigned gm = 0xffu << (lane & ~7);
+                float q[4], amax = 0.0f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    q[e] = __bfloat162float(__float2bfloat16_rn(v4[e]));
+                    amax = fmaxf(amax, fabsf(q[e]));
+                }
+#pragma unroll
+                for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(gm, amax, off));
+                const float dq = __fdiv_rn(amax, 127.0f);
+                const float id = (dq != 0.0f) ? __fdiv_rn(1.0f, dq) : 0.0f;
+                uint32_t word = 0;
+                int sum = 0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float t = roundf(__fmul_rn(q[e], id));
+                    const int c = !(t == t) ? 0 : (t <= -128.0f ? -128 : (t >= 127.0f ? 127 : __float2int_rz(t)));
+                    sum += c;
+                    word |= (uint32_t)(c & 0xff) << (8 * e);
+                }
+#pragma unroll
+                for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(gm, sum, off);
+                const int hq = kvh * p.rep + r, K = p.Hq * D;
+                const int64_t e0 = (int64_t)b * K + hq * D + d4 * 4;
+                *reinterpret_cast<uint32_t *>(p.q8_codes + e0) = word;
+                if ((lane & 7) == 0) {
+                    p.q8_scales[e0 / 32] = __half2float(__float2half_rn(dq));
+                    p.q8_offs[e0 / 32] = 12582912.0f + 8.0f * (float)sum;
+                }
+            }
+        }
     }
     if (tid == 0) *counter = 0;
 }

@@ -356,13 +356,23 @@ class Q4LlamaDecoder:
                                lw["qkv"], self.qkv_out, self.qkv_l, H, stream,
                                link=links[("qkv", li)] if fg and li > 0 else None)
             kc, vc = self.k_cache[li], self.v_cache[li]
-            N.check(L.tn_sdpa_decode_step(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()), P(kc.data_ptr()),
-                                          P(vc.data_ptr()), P(self.attn_l.data_ptr()), None, B, Hq, Hkv, D, self.cap,
-                                          self._kstr, self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D),
-                                          stream))
-            self._gather(self.attn_l, self.attn, 4 * li, stream)
-            self._fused_linear(N.TN_X_BF16, self.attn, HD, None, None, None, lw["o"], self.delta_l, self.h_l, HD,
-                               stream, link=links[("o", li)] if fg else None)
+            if self.tp is None:
+                # one GPU: the attention's merging CTAs also write its planar Q8_0,
+                # and o_proj stages those codes (no per-CTA bf16 -> Q8 prologue)
+                N.check(L.tn_sdpa_decode_step_q8(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()),
+                                                 P(kc.data_ptr()), P(vc.data_ptr()), P(self.attn.data_ptr()), None,
+                                                 P(self.codes.data_ptr()), P(self.scales.data_ptr()),
+                                                 P(self.offsets.data_ptr()), B, Hq, Hkv, D, self.cap, self._kstr,
+                                                 self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D), stream))
+                self._linear(lw["o"], self.delta, H, HD, stream)
+            else:
+                N.check(L.tn_sdpa_decode_step(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()),
+                                              P(kc.data_ptr()), P(vc.data_ptr()), P(self.attn_l.data_ptr()), None, B,
+                                              Hq, Hkv, D, self.cap, self._kstr, self._kstr, P(self.pos.data_ptr()),
+                                              1.0 / math.sqrt(D), stream))
+                self._gather(self.attn_l, self.attn, 4 * li, stream)
+                self._fused_linear(N.TN_X_BF16, self.attn, HD, None, None, None, lw["o"], self.delta_l, self.h_l, HD,
+                                   stream, link=links[("o", li)] if fg else None)
             if not fg:
                 self._gather(self.delta_l, self.delta, 4 * li + 1, stream)
             # residual: ha = hb + o_proj; act = SiLU(gate) * up of Q4(RMSNorm(ha))
@@ -416,12 +426,12 @@ class Q4LlamaDecoder:
         parts = {
             "qkv_rmsnorm_gemv": lambda lw, li, st: self._fused_linear(
                 N.TN_X_RMSNORM, ha, H, self.delta, hb, lw["attn_norm"], lw["qkv"], self.qkv_out, s.qkv, H, st),
-            "sdpa_decode_step": lambda lw, li, st: N.check(L.tn_sdpa_decode_step(
+            "sdpa_decode_step_q8": lambda lw, li, st: N.check(L.tn_sdpa_decode_step_q8(
                 P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()), P(self.k_cache[li].data_ptr()),
-                P(self.v_cache[li].data_ptr()), P(self.attn.data_ptr()), None, B, Hq, Hkv, D, self.cap, self._kstr,
+                P(self.v_cache[li].data_ptr()), P(self.attn.data_ptr()), None, P(self.codes.data_ptr()),
+                P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, Hq, Hkv, D, self.cap, self._kstr,
                 self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D), st)),
-            "o_gemv": lambda lw, li, st: self._fused_linear(
-                N.TN_X_BF16, self.attn, Hq * D, None, None, None, lw["o"], self.delta, H, Hq * D, st),
+            "o_gemv": lambda lw, li, st: self._linear(lw["o"], self.delta, H, Hq * D, st),
             "gate_up_rmsnorm_gemv_silu": lambda lw, li, st: self._fused_linear(
                 N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act, 2 * I, H, st,
                 N.TN_EPILOGUE_SILU_MUL_PAIRS),
