@@ -90,7 +90,7 @@ extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void 
     const bool tma_ok = aligned16(q) && (q_strides[0] * 2) % 16 == 0 && (q_strides[1] * 2) % 16 == 0 &&
                         (q_strides[2] * 2) % 16 == 0;
     if (dtype != TN_F32 && D == 128 && !attn_mask && p.rep * L > 16 && tma_ok && aligned16(out))
-        return tn::launch_sdpa_prefill(p, dtype, stream);
+        return L > 128 ? tn::launch_sdpa_prefill2(p, dtype, stream) : tn::launch_sdpa_prefill(p, dtype, stream);
     // Other calls with many query rows per head: the FP32-pipe flash kernel
     // (one pass over K/V per 64 query rows, where the split-KV kernel would
     // re-read K/V for every 8 rows).

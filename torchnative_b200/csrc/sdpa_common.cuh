@@ -47,6 +47,8 @@ int launch_sdpa_decode(const SdpaParams &p, int dtype, cudaStream_t stream);
 // Prefill on tcgen05 tensor cores: bf16/f16, D = 128, no additive mask, TMA-
 // compatible q/k/v (16-byte aligned base and strides).
 int launch_sdpa_prefill(const SdpaParams &p, int dtype, cudaStream_t stream);
+// The same with two query tiles (256 rows) per CTA, for longer sequences.
+int launch_sdpa_prefill2(const SdpaParams &p, int dtype, cudaStream_t stream);
 // Prefill on the FP32 pipes: every dtype, D = 64 or 128, masks, any q strides;
 // grid (ceil(L / 64), Hq, B).
 int launch_sdpa_prefill_simt(const SdpaParams &p, int dtype, cudaStream_t stream);
