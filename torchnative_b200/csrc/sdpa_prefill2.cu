@@ -98,7 +98,12 @@ __global__ void __launch_bounds__(THREADS, 1) sdpa_prefill2_kernel(const __grid_
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int qt = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
+    // One linear grid, query-tile major. Under a causal mask the work of a
+    // tile grows with its index, so the last tiles go out first (longest
+    // job first) and the short ones fill the tail of the last wave.
+    const int heads = a.Hq * a.B, slot = (int)blockIdx.x / heads, rest = (int)blockIdx.x % heads;
+    const int nqt = (int)gridDim.x / heads;
+    const int qt = a.causal ? nqt - 1 - slot : slot, hq = rest % a.Hq, b = rest / a.Hq;
     const int hkv = hq / a.rep, q0 = qt * (NQT * BM);
     const int nt0 = tiles_of(a, q0, 0), nt1 = tiles_of(a, q0, 1);
     const int ntm = nt0 > nt1 ? nt0 : nt1;
@@ -396,7 +401,10 @@ int launch_sdpa_prefill2(const SdpaParams &p, int dtype, cudaStream_t stream) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((p.L + NQT * BM - 1) / (NQT * BM)), (unsigned)p.Hq, (unsigned)p.B);
+    const long long nqt = (p.L + NQT * BM - 1) / (NQT * BM);
+    const long long ctas = nqt * p.Hq * p.B;
+    if (ctas > 0x7fffffffLL) return set_error(TN_ERR_SHAPE, std::string(op) + ": too many query tiles for one grid");
+    cfg.gridDim = dim3((unsigned)ctas);
     cfg.blockDim = dim3(THREADS);
     cfg.dynamicSmemBytes = PREFILL2_SMEM;
     cfg.stream = stream;
