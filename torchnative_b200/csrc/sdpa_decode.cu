@@ -113,13 +113,19 @@ __device__ __forceinline__ void merge_if_last(const SdpaParams &p, int b, int kv
                                               float *scratch, size_t scratch_bytes) {
     __shared__ int last;
     __shared__ __align__(8) uint64_t staged_bar;
-    __threadfence();
+    // One thread publishes the CTA's partial: the barrier orders every
+    // thread's stores before its release fence and ticket; the last CTA's
+    // acquire fence (same thread) orders the other splits' partials before the
+    // barrier that releases its readers.
     __syncthreads();
     int *counter = p.counters + ((int64_t)b * p.Hkv + kvh) * p.row_groups + rg;
-    if (tid == 0) last = (atomicAdd(counter, 1) == p.splits - 1);
+    if (tid == 0) {
+        __threadfence();
+        last = (atomicAdd(counter, 1) == p.splits - 1);
+        if (last) __threadfence();
+    }
     __syncthreads();
     if (!last) return;
-    __threadfence();
     float *wsm = scratch;                 // [R][splits] m_s, then weights e^(m_s - M)
     float *lsp = wsm + RMAX * p.splits;   // [R][splits] l_s
     float *lsm = lsp + RMAX * p.splits;   // [R] sum of weighted l_s
@@ -651,19 +657,24 @@ __global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const S
             cp_async_commit();
         }
     };
-    if (!appends) prime();
-
     // ---- query rows -> qb (16-bit, rows >= R zero), with the fused RoPE/append
     if (p.qkv) {
-        const int half = D / 2, W = (p.Hq + 2 * p.Hkv) * D;
+        constexpr int half = D / 2, NTH = MMA_WARPS * 32;
+        static_assert(NTH % half == 0, "a thread keeps one rotation frequency");
+        constexpr int RPP = NTH / half, PER = 16 / RPP;  // rows per pass, passes over the 16 MMA rows
+        const int W = (p.Hq + 2 * p.Hkv) * D;
         const __nv_bfloat16 *row = p.qkv + (int64_t)b * W;
-        constexpr int NTH = MMA_WARPS * 32, PER = (16 * (D / 2) + NTH - 1) / NTH;
-        // thread: rotation pairs (r, i) = (idx / half, idx % half), idx = tid + k * NTH;
-        // every load first, then the arithmetic
+        // thread: frequency i = tid % half of rows r0, r0 + RPP, ... Every load
+        // is issued first -- the query rows (and, in the appending CTA, the new
+        // key and value) ahead of the K/V ring, so that they do not queue behind
+        // it -- then the ring, then the arithmetic.
+        const int i = tid % half, r0 = tid / half;
+        const bool kv_lane = appends && tid < half;
+        const float fq = r0 < R ? p.inv_freq[i] : 0.0f;
         float x1[PER], x2[PER];
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
-            const int idx = tid + k * NTH, r = idx / half, i = idx % half;
+            const int r = r0 + k * RPP;
             x1[k] = x2[k] = 0.0f;
             if (r < R) {
                 const int hq = kvh * p.rep + r;
@@ -671,35 +682,43 @@ __global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const S
                 x2[k] = __bfloat162float(row[hq * D + i + half]);
             }
         }
+        const __nv_bfloat16 *kr = row + (p.Hq + kvh) * D, *vr = row + (p.Hq + p.Hkv + kvh) * D;
+        float y1 = 0.0f, y2 = 0.0f;
+        __nv_bfloat16 v1 = __float2bfloat16_rn(0.0f), v2 = v1;
+        if (kv_lane) {
+            y1 = __bfloat162float(kr[i]);
+            y2 = __bfloat162float(kr[i + half]);
+            v1 = vr[i];
+            v2 = vr[i + half];
+        }
+        if (!appends) prime();
+        float c = 0.0f, sn = 0.0f;
+        if (r0 < R) {
+            const float f = fq * (float)pos;
+            c = bfr16(cosf(f));
+            sn = bfr16(sinf(f));
+        }
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
-            const int idx = tid + k * NTH, r = idx / half, i = idx % half;
-            if (r >= 16) break;
+            const int r = r0 + k * RPP;
             float lo = 0.0f, hi = 0.0f;
             if (r < R) {
-                const float f = p.inv_freq[i] * (float)pos;
-                const float c = bfr16(cosf(f)), sn = bfr16(sinf(f));
                 lo = bfr16(bfr16(x1[k] * c) + bfr16(-x2[k] * sn));
                 hi = bfr16(bfr16(x2[k] * c) + bfr16(x1[k] * sn));
             }
             reinterpret_cast<T *>(qb + tile_off<D>(r, i / 8))[i % 8] = (T)lo;
             reinterpret_cast<T *>(qb + tile_off<D>(r, (i + half) / 8))[(i + half) % 8] = (T)hi;
         }
-        if (appends) {
+        if (kv_lane) {
             __nv_bfloat16 *kc = (__nv_bfloat16 *)p.k + b * p.ks[0] + kvh * p.ks[1] + (int64_t)pos * p.ks[2];
             __nv_bfloat16 *vc = (__nv_bfloat16 *)p.v + b * p.vs[0] + kvh * p.vs[1] + (int64_t)pos * p.vs[2];
-            const __nv_bfloat16 *kr = row + (p.Hq + kvh) * D, *vr = row + (p.Hq + p.Hkv + kvh) * D;
-            for (int i = tid; i < half; i += NTH) {
-                const float f = p.inv_freq[i] * (float)pos;
-                const float c = bfr16(cosf(f)), sn = bfr16(sinf(f));
-                const float y1 = __bfloat162float(kr[i]), y2 = __bfloat162float(kr[i + half]);
-                kc[i] = __float2bfloat16_rn(bfr16(y1 * c) + bfr16(-y2 * sn));
-                kc[i + half] = __float2bfloat16_rn(bfr16(y2 * c) + bfr16(y1 * sn));
-                vc[i] = vr[i];
-                vc[i + half] = vr[i + half];
-            }
+            kc[i] = __float2bfloat16_rn(bfr16(y1 * c) + bfr16(-y2 * sn));
+            kc[i + half] = __float2bfloat16_rn(bfr16(y2 * c) + bfr16(y1 * sn));
+            vc[i] = v1;
+            vc[i + half] = v2;
         }
     } else {
+        if (!appends) prime();
         for (int idx = tid; idx < 16 * D; idx += MMA_WARPS * 32) {
             const int r = idx / D, d = idx % D;
             T v = (T)0.0f;
@@ -825,7 +844,10 @@ __global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const S
     }
     __syncthreads();  // every warp's ring is drained: reuse it for the warp merge
 
-    // ---- merge the 4 warps: cmb = [warp][16] m, [warp][16] l, [warp][16][D] o
+    // ---- merge the 4 warps: cmb = [warp][16] m, [warp][16] l, [warp][16][WOS] o
+    // (rows padded by 4 floats: the 8 row groups g of a fragment store land in
+    // 8 different bank quads)
+    constexpr int WOS = D + 4;
     float *wm = cmb, *wl = cmb + MMA_WARPS * 16, *wo = cmb + 2 * MMA_WARPS * 16;
     if (t4 == 0) {
         wm[warp * 16 + g] = m_run[0];
@@ -835,38 +857,52 @@ __global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const S
     }
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
-        float *r0p = wo + (warp * 16 + g) * D + 8 * n + 2 * t4, *r1p = wo + (warp * 16 + g + 8) * D + 8 * n + 2 * t4;
-        r0p[0] = o[n][0];
-        r0p[1] = o[n][1];
-        r1p[0] = o[n][2];
-        r1p[1] = o[n][3];
+        float *r0p = wo + (warp * 16 + g) * WOS + 8 * n + 2 * t4, *r1p = r0p + 8 * WOS;
+        *reinterpret_cast<float2 *>(r0p) = make_float2(o[n][0], o[n][1]);
+        *reinterpret_cast<float2 *>(r1p) = make_float2(o[n][2], o[n][3]);
     }
     __syncthreads();
-    for (int idx = tid; idx < R * D; idx += MMA_WARPS * 32) {
-        const int r = idx / D, d = idx % D;
+    // the warps' weights e^(m_w - M) once per (warp, row), then one float4 of a
+    // row per thread
+    __shared__ float wa[MMA_WARPS * 16], wml[16][2];
+    if (tid < R) {
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < MMA_WARPS; ++w) M = fmaxf(M, wm[w * 16 + r]);
-        float acc = 0.0f, l = 0.0f;
+        for (int w = 0; w < MMA_WARPS; ++w) M = fmaxf(M, wm[w * 16 + tid]);
+        float l = 0.0f;
 #pragma unroll
         for (int w = 0; w < MMA_WARPS; ++w) {
-            const float mw = wm[w * 16 + r];
+            const float mw = wm[w * 16 + tid];
             const float a = (mw == -INFINITY) ? 0.0f : expf(mw - M);
-            acc = fmaf(a, wo[(w * 16 + r) * D + d], acc);
-            l = fmaf(a, wl[w * 16 + r], l);
+            wa[w * 16 + tid] = a;
+            l = fmaf(a, wl[w * 16 + tid], l);
+        }
+        wml[tid][0] = M;
+        wml[tid][1] = l;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < R * (D / 4); idx += MMA_WARPS * 32) {
+        const int r = idx / (D / 4), d4 = idx % (D / 4);
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int w = 0; w < MMA_WARPS; ++w) {
+            const float a = wa[w * 16 + r];
+            const float4 o4 = *reinterpret_cast<const float4 *>(wo + (w * 16 + r) * WOS + 4 * d4);
+            acc.x = fmaf(a, o4.x, acc.x);
+            acc.y = fmaf(a, o4.y, acc.y);
+            acc.z = fmaf(a, o4.z, acc.z);
+            acc.w = fmaf(a, o4.w, acc.w);
         }
         const int gr = rg * p.rows + r, lq = gr / p.rep, hq = kvh * p.rep + gr % p.rep;
         const int64_t row = ((int64_t)b * p.Hq + hq) * p.L + lq;
-        p.part_o[(row * p.splits + split) * D + d] = acc;
-        if (d == 0) {
-            p.part_ml[(row * p.splits + split) * 2 + 0] = M;
-            p.part_ml[(row * p.splits + split) * 2 + 1] = l;
-        }
+        *reinterpret_cast<float4 *>(p.part_o + (row * p.splits + split) * D + 4 * d4) = acc;
+        if (d4 == 0)
+            *reinterpret_cast<float2 *>(p.part_ml + (row * p.splits + split) * 2) = make_float2(wml[r][0], wml[r][1]);
     }
     if (!p.counters) return;
     {
         const size_t rings_b = (size_t)MMA_WARPS * NST * 2 * TKM * D * 2;
-        const size_t merge_b = (size_t)(2 * MMA_WARPS * 16 + MMA_WARPS * 16 * D) * 4;
+        const size_t merge_b = (size_t)(2 * MMA_WARPS * 16 + MMA_WARPS * 16 * WOS) * 4;
         merge_if_last<T, D>(p, b, kvh, rg, R, tid, cmb, rings_b > merge_b ? rings_b : merge_b);
     }
 }
@@ -874,7 +910,7 @@ __global__ void __launch_bounds__(MMA_WARPS * 32) sdpa_decode_mma_kernel(const S
 template <int D>
 size_t decode_mma_smem() {
     const size_t rings = (size_t)MMA_WARPS * NST * 2 * TKM * D * 2;
-    const size_t merge = (size_t)(2 * MMA_WARPS * 16 + MMA_WARPS * 16 * D) * 4;
+    const size_t merge = (size_t)(2 * MMA_WARPS * 16 + MMA_WARPS * 16 * (D + 4)) * 4;
     return 16 * D * 2 + D * 4 + (rings > merge ? rings : merge) + 128;
 }
 
