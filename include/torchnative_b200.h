@@ -194,6 +194,20 @@ TN_API int tn_q4_0_linear_fused(int x_mode, const void *x, int64_t x_row_stride,
                                 const float *bias, void *y, int y_dtype, int64_t M, int64_t N,
                                 int64_t K, int flags, void *stream);
 
+/* tn_q4_0_linear_fused whose launch also writes the planar Q8_0 of its own
+ * bf16 output y (the layout of tn_q8_0_quantize_planar, with K = y's column
+ * count: N, or N/2 under TN_EPILOGUE_SILU_MUL_PAIRS) -- the next linear's
+ * activations, byte for byte what tn_q8_0_quantize_planar(y) writes, without
+ * its launch. y bf16, y's columns a multiple of 32. The decode step uses it for
+ * LlamaMLP's act = SiLU(gate) * up ahead of down_proj. No reference counterpart
+ * as one call: the reference quantises the activation inside the next
+ * _quantized_linear (k_quants.rs:676-706). */
+TN_API int tn_q4_0_linear_fused_q8out(int x_mode, const void *x, int64_t x_row_stride, const void *delta,
+                                      void *h_out, const void *norm_weight, float eps, const void *w_blob,
+                                      const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
+                                      int flags, int8_t *codes, int64_t codes_row_stride, float *scales,
+                                      float *offsets, void *stream);
+
 /* tn_q4_0_linear without any device allocation. No counterpart in the
  * reference: it exists for hosts that cannot let a library call cudaMalloc
  * while they run -- an engine that owns a preplanned arena of HBM, work being

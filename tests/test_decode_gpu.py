@@ -281,3 +281,68 @@ def test_decode_attention_writes_the_planar_q8_of_its_output(N, cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(codes, rc) and torch.equal(scales, rs) and torch.equal(offs, ro)
     N.device_status(reset=True)
+
+
+@pytest.mark.parametrize("mode,pairs,M,Nout,K", [
+    ("rmsnorm", True, 1, 2 * 2048, 4096),   # LlamaMLP's gate/up, decode batch 1
+    ("rmsnorm", True, 3, 2 * 1024, 512),
+    ("rmsnorm", True, 2, 2 * 32 * 5, 256),  # 5 blocks: CTAs with and without a block
+    ("bf16", False, 2, 4096, 1024),
+    ("bf16", False, 4, 96, 256),
+])
+def test_gemv_writes_the_planar_q8_of_its_output(N, cuda_device, mode, pairs, M, Nout, K):
+    """tn_q4_0_linear_fused_q8out: the same bf16 y as tn_q4_0_linear_fused, and
+    codes / scales / offsets byte-identical to tn_q8_0_quantize_planar of that
+    y (the down_proj GEMV stages them; the quantiser launch disappears)."""
+    rng = np.random.default_rng(M * 131 + Nout + K)
+    dev = cuda_device
+    blob = q4_exact.random_q4_0_blob(rng, Nout, K)
+    w = torch.frombuffer(bytearray(blob), dtype=torch.uint8).to(dev)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(torch.bfloat16).to(dev)
+    delta = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32) * 0.5).to(torch.bfloat16).to(dev)
+    nw = torch.from_numpy(1.0 + 0.1 * rng.standard_normal(K).astype(np.float32)).to(torch.bfloat16).to(dev)
+    xm = N.TN_X_RMSNORM if mode == "rmsnorm" else N.TN_X_BF16
+    flags = N.TN_WEIGHTS_STATIC | (N.TN_EPILOGUE_SILU_MUL_PAIRS if pairs else 0)
+    cols = Nout // 2 if pairs else Nout
+    ys = [torch.full((M, cols), float("nan"), device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    hs = [torch.zeros((M, K), device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    codes = torch.full((M, cols), 99, device=dev, dtype=torch.int8)
+    scales = torch.full((M, cols // 32), -1.0, device=dev)
+    offs = torch.full((M, cols // 32), -1.0, device=dev)
+    common = lambda h, y: [xm, P(x.data_ptr()), K, P(delta.data_ptr()) if xm == N.TN_X_RMSNORM else None,  # noqa: E731
+                           P(h.data_ptr()) if xm == N.TN_X_RMSNORM else None,
+                           P(nw.data_ptr()) if xm == N.TN_X_RMSNORM else None, 1e-5, P(w.data_ptr()), None,
+                           P(y.data_ptr()), N.TN_BF16, M, Nout, K, flags]
+    N.check(N.lib().tn_q4_0_linear_fused(*common(hs[0], ys[0]), _stream()))
+    N.check(N.lib().tn_q4_0_linear_fused_q8out(*common(hs[1], ys[1]), P(codes.data_ptr()), cols,
+                                               P(scales.data_ptr()), P(offs.data_ptr()), _stream()))
+    rc = torch.zeros_like(codes)
+    rs, ro = torch.zeros_like(scales), torch.zeros_like(offs)
+    N.check(N.lib().tn_q8_0_quantize_planar(P(ys[1].data_ptr()), N.TN_BF16, cols, P(rc.data_ptr()), cols,
+                                            P(rs.data_ptr()), P(ro.data_ptr()), M, cols, _stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(ys[0], ys[1]) and torch.equal(hs[0], hs[1])
+    assert torch.equal(codes, rc) and torch.equal(scales, rs) and torch.equal(offs, ro)
+    N.device_status(reset=True)
+
+
+def test_gemv_planar_q8_output_refuses_what_it_cannot_quantise(N, cuda_device):
+    """A float32 y, or y columns that are not whole 32-element blocks, are
+    refused by name before anything is launched."""
+    dev = cuda_device
+    w = torch.zeros(64 * 8 * 18, device=dev, dtype=torch.uint8)
+    x = torch.zeros((1, 256), device=dev, dtype=torch.bfloat16)
+    y = torch.zeros((1, 64), device=dev)
+    q = torch.zeros(64, device=dev, dtype=torch.int8)
+    sc = torch.zeros(2, device=dev)
+
+    def call(y_dtype, nout, flags):
+        return N.lib().tn_q4_0_linear_fused_q8out(N.TN_X_BF16, P(x.data_ptr()), 256, None, None, None, 1e-5,
+                                                  P(w.data_ptr()), None, P(y.data_ptr()), y_dtype, 1, nout, 256,
+                                                  flags, P(q.data_ptr()), 64, P(sc.data_ptr()), P(sc.data_ptr()),
+                                                  _stream())
+
+    assert call(N.TN_F32, 64, 0) == N.TN_ERR_NOT_IMPLEMENTED
+    assert "bf16" in N.last_error()
+    assert call(N.TN_BF16, 48, 0) == N.TN_ERR_SHAPE
+    assert call(N.TN_BF16, 32, N.TN_EPILOGUE_SILU_MUL_PAIRS) == N.TN_ERR_SHAPE  # 16 columns of act

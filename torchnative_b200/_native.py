@@ -67,6 +67,8 @@ SIGNATURES = {
     "tn_q4_0_linear_q8": (_I, [_P, _I64, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
     "tn_q4_0_linear_fused": (_I, [_I, _P, _I64, _P, _P, _P, ctypes.c_float, _P, _P, _P, _I, _I64, _I64, _I64, _I,
                                   _P]),
+    "tn_q4_0_linear_fused_q8out": (_I, [_I, _P, _I64, _P, _P, _P, ctypes.c_float, _P, _P, _P, _I, _I64, _I64, _I64,
+                                        _I, _P, _I64, _P, _P, _P]),
     "tn_q4_0_linear_noalloc": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
     "tn_sdpa_flash_attention": (_I, [_P, _P, _P, _P, _I, _PI64, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64,
                                      _PI64, _PI64, _PI64, _I, _D, _P]),

@@ -34,6 +34,9 @@ constexpr uint32_t kMagic = 0x4B400000u;           // 12582912.0f
 // Shared memory per CTA when two CTAs share an SM (228 KB per SM, 1 KB of it
 // reserved per CTA).
 constexpr size_t kTwoCtaBudget = 112 * 1024;
+// Output columns a CTA may hold for the planar Q8_0 epilogue (whole 32-column
+// blocks), per activation row.
+constexpr int kYCap = 128;
 
 struct GemvParams {
     const uint8_t *w;
@@ -70,6 +73,12 @@ struct GemvParams {
     int tp_world, tp_rank, tp_slot, tp_wait;
     int64_t tp_dst_off, tp_dst_row, tp_cols;
     uint8_t *tp_bases[kTpMaxRanks];
+    // Planar Q8_0 of y (oq != null): every CTA owns whole 32-column blocks of
+    // y, keeps its bf16 outputs in shared memory and quantises them after its
+    // last row.
+    int8_t *oq;
+    float *od, *oc;
+    int64_t oq_row_stride;
 };
 
 // Shared-memory layout (dynamic), as 32-bit shared-window addresses:
@@ -77,10 +86,11 @@ struct GemvParams {
 //   xs    M * nbp * 32 bytes      activation codes, pair-swizzled (xchunk)
 //   xds   M * nbp floats          widened activation scales
 //   xcs   M * nbp floats          offset constants
+//   ys    M * kYCap floats        this CTA's outputs (planar Q8_0 epilogue only)
 //   slots nslots * slot_bytes     chunks of 2*wpc weight rows (16-byte aligned)
 struct Smem {
     uint64_t *full, *empty;
-    uint32_t xs, xds, xcs, slots;
+    uint32_t xs, xds, xcs, ys, slots;
 };
 
 __device__ __forceinline__ Smem carve(uint8_t *base, const GemvParams &p) {
@@ -95,6 +105,8 @@ __device__ __forceinline__ Smem carve(uint8_t *base, const GemvParams &p) {
     off += (uint32_t)p.M * p.nbp * 4;
     s.xcs = b + off;
     off += (uint32_t)p.M * p.nbp * 4;
+    s.ys = b + off;
+    if (p.oq) off += (uint32_t)p.M * kYCap * 4;
     off = (off + 127) & ~127u;
     s.slots = b + off;
     return s;
@@ -471,7 +483,7 @@ __device__ __forceinline__ void store_y(const GemvParams &p, int m, int64_t n, f
 // one value, index lane >> (5 - log2 V); the remaining levels finish the sum.
 template <int MT>
 __device__ __forceinline__ void finish_rows(float (&acc)[2][MT], const GemvParams &p, int64_t n0, bool has_b,
-                                            int lane) {
+                                            int lane, const Smem &s, int64_t ycol0) {
     constexpr int V = 2 * MT;
     constexpr int LOGV = (V == 2) ? 1 : (V == 4) ? 2 : (V == 8) ? 3 : (V == 16) ? 4 : 5;
     float v[V];
@@ -503,7 +515,9 @@ __device__ __forceinline__ void finish_rows(float (&acc)[2][MT], const GemvParam
         const float u = __shfl_down_sync(0xffffffffu, t, 16);
         if ((lane & ((1 << (5 - LOGV)) - 1)) == 0 && r == 0 && m < p.M) {
             const float g = bfr(t), up = bfr(u);
-            store_y(p, m, n0 >> 1, bfr(bfr(g / (1.0f + expf(-g))) * up));
+            const float a = bfr(bfr(g / (1.0f + expf(-g))) * up);
+            store_y(p, m, n0 >> 1, a);
+            if (p.oq) stsf(s.ys + (uint32_t)(m * kYCap + ((n0 >> 1) - ycol0)) * 4, a);
         }
         return;
     }
@@ -511,6 +525,7 @@ __device__ __forceinline__ void finish_rows(float (&acc)[2][MT], const GemvParam
         const int64_t n = n0 + r;
         if (p.bias) t = t + __ldg(p.bias + n);
         store_y(p, m, n, t);
+        if (p.oq) stsf(s.ys + (uint32_t)(m * kYCap + (n - ycol0)) * 4, bfr(t));
     }
 }
 
@@ -566,10 +581,13 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
     const Smem s = carve(smem_raw, p);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t G = gridDim.x, c = blockIdx.x;
-    // (gate, up) row pairs never straddle two CTAs: partition in pairs then
-    const int64_t gran = (p.flags & TN_EPILOGUE_SILU_MUL_PAIRS) ? 2 : 1;
+    // (gate, up) row pairs never straddle two CTAs: partition in pairs then;
+    // with the planar Q8_0 epilogue, in whole 32-column blocks of y
+    const bool pairs = (p.flags & TN_EPILOGUE_SILU_MUL_PAIRS) != 0;
+    const int64_t gran = (pairs ? 2 : 1) * (p.oq ? 32 : 1);
     const int64_t r0 = c * (p.N / gran) / G * gran, r1 = (c + 1) * (p.N / gran) / G * gran;
     const int nrows = (int)(r1 - r0);
+    const int64_t ycol0 = pairs ? r0 >> 1 : r0;
     // Chunks of R = 2 * wpc consecutive rows; chunk j lives in slot j % nslots
     // and is consumed by warp group j % groups (wpc warps, two rows each).
     const int wpc = p.wpc, R = 2 * p.wpc, groups = kConsumerWarps / p.wpc;
@@ -673,7 +691,33 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
             else
                 global_rows<MT, false>(s, p, ra, ra, lane, acc);
         }
-        if (has_a) finish_rows<MT>(acc, p, r0 + i, has_b, lane);
+        if (has_a) finish_rows<MT>(acc, p, r0 + i, has_b, lane, s, ycol0);
+    }
+    if (p.oq) {
+        // Planar Q8_0 of this CTA's blocks of y, from the bf16 values it
+        // stored (q8_0_quantize_planar's arithmetic: k_quants.rs:676-706), one
+        // warp per (row, block), one element per lane.
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+        const int nblk = (pairs ? nrows >> 1 : nrows) / 32;
+        const int64_t nbo = (pairs ? p.N >> 1 : p.N) / 32, blk0 = ycol0 / 32;
+        for (int t = warp; t < p.M * nblk; t += kConsumerWarps) {
+            const int m = t / nblk, bl = t % nblk;
+            float v;
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(s.ys + (uint32_t)(m * kYCap + bl * 32 + lane) * 4));
+            // the largest |v| (NaN counts as 0, as fmaxf skips it): non-negative
+            // floats order like their bit patterns
+            const float av = fabsf(v);
+            const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(av == av ? av : 0.0f)));
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+            const int q = sat_i8r(roundf(__fmul_rn(v, id)));
+            const int sum = __reduce_add_sync(0xffffffffu, q);
+            p.oq[m * p.oq_row_stride + (blk0 + bl) * 32 + lane] = (int8_t)q;
+            if (lane == 0) {
+                p.od[m * nbo + blk0 + bl] = __half2float(__float2half_rn(d));
+                p.oc[m * nbo + blk0 + bl] = 12582912.0f + 8.0f * (float)sum;
+            }
+        }
     }
     if (p.tp_slot >= 0) {
         // Every consumer's rows are stored in this rank's region. The launch's
@@ -757,8 +801,8 @@ int launch_variant(const GemvParams &p, int grid, size_t smem, cudaStream_t stre
     return TN_OK;
 }
 
-size_t smem_bytes(int M, int nbp, int nslots, int slot_bytes) {
-    size_t off = 16 * kMaxSlots + (size_t)M * nbp * 40;
+size_t smem_bytes(int M, int nbp, int nslots, int slot_bytes, int ycols) {
+    size_t off = 16 * kMaxSlots + (size_t)M * nbp * 40 + (size_t)M * ycols * 4;
     off = (off + 127) & ~size_t(127);
     return off + (size_t)nslots * slot_bytes;
 }
@@ -774,9 +818,9 @@ struct Plan {
 // per SM. nslots is a multiple of the number of warp groups, so chunk j and
 // chunk j - nslots belong to the same group and no warp ever waits on a slot's
 // barrier more than one phase ahead (parity waits cannot tell phases two apart).
-Plan plan_slots(int M, int nbp, int rowbytes, bool staged, size_t budget, size_t in_flight) {
+Plan plan_slots(int M, int nbp, int rowbytes, bool staged, size_t budget, size_t in_flight, int ycols = 0) {
     Plan pl{false, 1, 0, 0};
-    const size_t base = smem_bytes(M, nbp, 0, 0);
+    const size_t base = smem_bytes(M, nbp, 0, 0, ycols);
     if (!staged) {
         pl.ok = base <= budget;
         pl.wpc = kConsumerWarps / 2;
@@ -823,15 +867,16 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
     p.rowbytes = 18 * p.nb;
     p.err = device_error_word();
     const bool staged = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(p.w) & 15) == 0);
+    const int ycols = p.oq ? kYCap : 0;
     // Two CTAs per SM for M <= 2 (each with ~64 KB in flight): the next
     // kernel's CTAs can then start streaming while this one's last CTAs drain.
     Plan plan{false, 1, 0, 0};
     int ctas_per_sm = 1;
     if (M <= 2) {
-        plan = plan_slots(M, p.nbp, p.rowbytes, staged, kTwoCtaBudget, 64 * 1024);
+        plan = plan_slots(M, p.nbp, p.rowbytes, staged, kTwoCtaBudget, 64 * 1024, ycols);
         if (plan.ok) ctas_per_sm = 2;
     }
-    if (!plan.ok) plan = plan_slots(M, p.nbp, p.rowbytes, staged, (size_t)f.smem_optin - 1024, 128 * 1024);
+    if (!plan.ok) plan = plan_slots(M, p.nbp, p.rowbytes, staged, (size_t)f.smem_optin - 1024, 128 * 1024, ycols);
     if (!plan.ok)
         return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: activation tile too large for "
                                                                    "shared memory");
@@ -839,10 +884,18 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
     p.slot_bytes = plan.slot_bytes;
     p.nslots = plan.nslots;
     p.flags = flags;
-    const size_t smem = smem_bytes(M, p.nbp, plan.nslots, plan.slot_bytes);
+    const size_t smem = smem_bytes(M, p.nbp, plan.nslots, plan.slot_bytes, ycols);
     int64_t grid = (int64_t)f.sm_count * ctas_per_sm;
     const int64_t by_rows = (N + 2 * plan.wpc - 1) / (2 * plan.wpc);
     if (by_rows < grid) grid = by_rows > 0 ? by_rows : 1;
+    if (p.oq) {
+        // whole blocks per CTA, at most kYCap columns of them
+        const int64_t blocks = ((flags & TN_EPILOGUE_SILU_MUL_PAIRS) ? N / 2 : N) / 32;
+        if (blocks < grid) grid = blocks;
+        if ((blocks + grid - 1) / grid * 32 > kYCap)
+            return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": too many output blocks per CTA for the "
+                                                                       "planar Q8_0 epilogue");
+    }
     // One kernel per (rows, staging, activation source): each holds only the
     // prologue it runs (the prologue executes once per CTA, from a cold
     // instruction cache, so its code size is latency).
@@ -911,9 +964,15 @@ int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const
 int launch_q4_gemv_fused(int x_mode, const void *xb, int64_t xb_row_stride, const void *xdelta, void *xh_out,
                          const void *norm_w, float eps, const uint8_t *w, const float *bias, void *y, int y_dtype,
                          int64_t y_row_stride, int M, int64_t N, int64_t K, int flags, cudaStream_t stream,
-                         const tn_tp_link *link) {
+                         const tn_tp_link *link, const Q8Out *q8) {
     GemvParams p{};
     set_link(p, link, (flags & TN_EPILOGUE_SILU_MUL_PAIRS) ? N / 2 : N);
+    if (q8) {
+        p.oq = q8->codes;
+        p.od = q8->scales;
+        p.oc = q8->offsets;
+        p.oq_row_stride = q8->codes_row_stride;
+    }
     p.w = w;
     p.bias = bias;
     p.y = y;

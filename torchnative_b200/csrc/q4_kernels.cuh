@@ -33,12 +33,23 @@ int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const
                       const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
                       int flags, cudaStream_t stream, const tn_tp_link *link = nullptr);
 
+// Planar Q8_0 of a GEMV's own bf16 output (the next linear's activations):
+// codes [M][codes_row_stride], scales and offsets [M][out_cols / 32].
+struct Q8Out {
+    int8_t *codes;
+    int64_t codes_row_stride;
+    float *scales;
+    float *offsets;
+};
+
 // Decode GEMV whose planar Q8_0 activations are built in each CTA from bf16
 // rows (x_mode: 1 = x itself, 2 = RMSNorm(h + delta) with h + delta written to
-// xh_out by CTA 0, 3 = silu(gate) * up from [gate | up] rows); M <= 4.
+// xh_out by CTA 0, 3 = silu(gate) * up from [gate | up] rows); M <= 4. With
+// `q8` (bf16 y, out_cols % 32 == 0, no link), each CTA also quantises its
+// whole 32-column blocks of y.
 int launch_q4_gemv_fused(int x_mode, const void *xb, int64_t xb_row_stride, const void *xdelta, void *xh_out,
                          const void *norm_w, float eps, const uint8_t *w, const float *bias, void *y, int y_dtype,
                          int64_t y_row_stride, int M, int64_t N, int64_t K, int flags, cudaStream_t stream,
-                         const tn_tp_link *link = nullptr);
+                         const tn_tp_link *link = nullptr, const Q8Out *q8 = nullptr);
 
 }  // namespace tn

@@ -166,11 +166,12 @@ extern "C" int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, 
                                 nullptr, stream);
 }
 
-extern "C" int tn_q4_0_linear_fused_tp(int x_mode, const void *x, int64_t x_row_stride, const void *delta,
-                                       void *h_out, const void *norm_weight, float eps, const void *w_blob,
-                                       const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
-                                       int flags, const tn_tp_link *link, void *stream) {
-    const std::string op = "tn_q4_0_linear_fused";
+namespace {
+
+int linear_fused(const std::string &op, int x_mode, const void *x, int64_t x_row_stride, const void *delta,
+                 void *h_out, const void *norm_weight, float eps, const void *w_blob, const float *bias, void *y,
+                 int y_dtype, int64_t M, int64_t N, int64_t K, int flags, const tn_tp_link *link,
+                 const tn::Q8Out *q8, void *stream) {
     __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
     if (x_mode != TN_X_BF16 && x_mode != TN_X_RMSNORM && x_mode != TN_X_SILU_MUL)
         return tn::set_error(TN_ERR_INVALID, op + ": unknown x_mode " + std::to_string(x_mode));
@@ -203,7 +204,40 @@ extern "C" int tn_q4_0_linear_fused_tp(int x_mode, const void *x, int64_t x_row_
     }
     return tn::launch_q4_gemv_fused(x_mode, x, x_row_stride, delta, h_out, norm_weight, eps,
                                     static_cast<const uint8_t *>(w_blob), bias, y, y_dtype, pairs ? N / 2 : N, (int)M,
-                                    N, K, flags, static_cast<cudaStream_t>(stream), link);
+                                    N, K, flags, static_cast<cudaStream_t>(stream), link, q8);
+}
+
+}  // namespace
+
+extern "C" int tn_q4_0_linear_fused_tp(int x_mode, const void *x, int64_t x_row_stride, const void *delta,
+                                       void *h_out, const void *norm_weight, float eps, const void *w_blob,
+                                       const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
+                                       int flags, const tn_tp_link *link, void *stream) {
+    return linear_fused("tn_q4_0_linear_fused", x_mode, x, x_row_stride, delta, h_out, norm_weight, eps, w_blob, bias,
+                        y, y_dtype, M, N, K, flags, link, nullptr, stream);
+}
+
+extern "C" int tn_q4_0_linear_fused_q8out(int x_mode, const void *x, int64_t x_row_stride, const void *delta,
+                                          void *h_out, const void *norm_weight, float eps, const void *w_blob,
+                                          const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
+                                          int flags, int8_t *codes, int64_t codes_row_stride, float *scales,
+                                          float *offsets, void *stream) {
+    const std::string op = "tn_q4_0_linear_fused_q8out";
+    const int64_t cols = (flags & TN_EPILOGUE_SILU_MUL_PAIRS) ? N / 2 : N;
+    if (y_dtype != TN_BF16)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": the planar Q8_0 output is quantised from a bf16 y");
+    if (N < 0 || cols % 32 != 0)
+        return tn::set_error(TN_ERR_SHAPE, op + ": the output's columns must be whole 32-element blocks");
+    if (M > 0 && N > 0) {
+        if (!codes || !scales || !offsets) return tn::set_error(TN_ERR_INVALID, op + ": null planar Q8_0 output");
+        if (codes_row_stride < cols)
+            return tn::set_error(TN_ERR_INVALID, op + ": codes row stride smaller than the output's columns");
+        if (((reinterpret_cast<uintptr_t>(scales) | reinterpret_cast<uintptr_t>(offsets)) & 3) != 0)
+            return tn::set_error(TN_ERR_INVALID, op + ": scales and offsets must be 4-byte aligned");
+    }
+    const tn::Q8Out q8{codes, codes_row_stride, scales, offsets};
+    return linear_fused(op, x_mode, x, x_row_stride, delta, h_out, norm_weight, eps, w_blob, bias, y, y_dtype, M, N,
+                        K, flags, nullptr, &q8, stream);
 }
 
 extern "C" int tn_q4_0_linear_fused(int x_mode, const void *x, int64_t x_row_stride, const void *delta, void *h_out,

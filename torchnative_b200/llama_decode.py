@@ -243,7 +243,10 @@ class Q4LlamaDecoder:
             extra = 2 if self.fused_gather else 4
         else:
             extra = 4 if (self.tp is not None and self.B > 1) else 0
-        return (6 if self.fused else 11) + extra
+        if self.fused:
+            # one GPU: gate/up also writes the planar Q8_0 of act (no quantiser launch)
+            return (5 if self.tp is None else 6) + extra
+        return 11 + extra
 
     @property
     def kernels_per_step(self) -> int:
@@ -334,7 +337,18 @@ class Q4LlamaDecoder:
                                         P(self.pos.data_ptr()), stream))
         self._step_end(stream)
 
-    def _fused_linear(self, mode, x, x_stride, delta, h_out, norm_w, w, y, n, k, stream, flags=0, link=None):
+    def _fused_linear(self, mode, x, x_stride, delta, h_out, norm_w, w, y, n, k, stream, flags=0, link=None,
+                      q8=False):
+        if q8:
+            # also the planar Q8_0 of y (the next linear's activations) from the same launch
+            cols = n // 2 if flags & N.TN_EPILOGUE_SILU_MUL_PAIRS else n
+            N.check(N.lib().tn_q4_0_linear_fused_q8out(
+                mode, P(x.data_ptr()), x_stride, None if delta is None else P(delta.data_ptr()),
+                None if h_out is None else P(h_out.data_ptr()), None if norm_w is None else P(norm_w.data_ptr()),
+                self.s.eps, P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, self.B, n, k,
+                N.TN_WEIGHTS_STATIC | flags, P(self.codes.data_ptr()), cols, P(self.scales.data_ptr()),
+                P(self.offsets.data_ptr()), stream))
+            return
         N.check(N.lib().tn_q4_0_linear_fused_tp(mode, P(x.data_ptr()), x_stride,
                                                 None if delta is None else P(delta.data_ptr()),
                                                 None if h_out is None else P(h_out.data_ptr()),
@@ -376,14 +390,21 @@ class Q4LlamaDecoder:
             if not fg:
                 self._gather(self.delta_l, self.delta, 4 * li + 1, stream)
             # residual: ha = hb + o_proj; act = SiLU(gate) * up of Q4(RMSNorm(ha))
-            self._fused_linear(N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act_l,
-                               2 * self.i_l, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS,
-                               link=links[("gate_up", li)] if fg else None)
-            self._gather(self.act_l, self.act, 4 * li + 2, stream)
-            # the activation quantiser once (not in each of the down GEMV's CTAs:
-            # 448 blocks per CTA cost more than a launch), then the planar GEMV
-            N.check(L.tn_q8_0_quantize_planar(P(self.act.data_ptr()), N.TN_BF16, I, P(self.codes.data_ptr()), I,
-                                              P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, I, stream))
+            if self.tp is None:
+                # one GPU: the same launch writes act's planar Q8_0 block by block
+                # (each CTA owns whole 32-column blocks), which down_proj stages
+                self._fused_linear(N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act,
+                                   2 * I, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS, q8=True)
+            else:
+                self._fused_linear(N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act_l,
+                                   2 * self.i_l, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS,
+                                   link=links[("gate_up", li)] if fg else None)
+                self._gather(self.act_l, self.act, 4 * li + 2, stream)
+                # the activation quantiser once (not in each of the down GEMV's
+                # CTAs: 448 blocks per CTA cost more than a launch)
+                N.check(L.tn_q8_0_quantize_planar(P(self.act.data_ptr()), N.TN_BF16, I, P(self.codes.data_ptr()), I,
+                                                  P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, I,
+                                                  stream))
             self._linear(lw["down"], self.delta_l, self.h_l, I, stream, link=links[("down", li)] if fg else None)
             if not fg:
                 self._gather(self.delta_l, self.delta, 4 * li + 3, stream)
@@ -432,12 +453,9 @@ class Q4LlamaDecoder:
                 P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, Hq, Hkv, D, self.cap, self._kstr,
                 self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D), st)),
             "o_gemv": lambda lw, li, st: self._linear(lw["o"], self.delta, H, Hq * D, st),
-            "gate_up_rmsnorm_gemv_silu": lambda lw, li, st: self._fused_linear(
+            "gate_up_rmsnorm_gemv_silu_q8": lambda lw, li, st: self._fused_linear(
                 N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act, 2 * I, H, st,
-                N.TN_EPILOGUE_SILU_MUL_PAIRS),
-            "act_q8": lambda lw, li, st: N.check(L.tn_q8_0_quantize_planar(
-                P(self.act.data_ptr()), N.TN_BF16, I, P(self.codes.data_ptr()), I, P(self.scales.data_ptr()),
-                P(self.offsets.data_ptr()), B, I, st)),
+                N.TN_EPILOGUE_SILU_MUL_PAIRS, q8=True),
             "down_gemv": lambda lw, li, st: self._linear(lw["down"], self.delta, H, I, st),
         }
         graphs = {}
