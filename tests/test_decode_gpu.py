@@ -119,11 +119,15 @@ def test_rope_append_matches_apply_rotary_pos_emb(N, cuda_device):
     assert kc[:, :, :pos].abs().sum() == 0 and kc[:, :, pos + 1:].abs().sum() == 0
 
 
-def test_argmax_embed_picks_the_first_maximum(N, cuda_device):
-    B, V, H = 3, 1000, 64
+@pytest.mark.parametrize("V", [1000, 1003, 128256])
+def test_argmax_embed_picks_the_first_maximum(N, cuda_device, V):
+    B, H = 3, 64
     logits = torch.randn((B, V), device=cuda_device).to(torch.bfloat16)
     logits[1, 10] = 50.0
     logits[1, 700] = 50.0  # tie: the first index wins, as torch.argmax
+    logits[2, V - 2] = 60.0
+    logits[2, 17] = 60.0  # tie across the row: 17 (inside a 16-byte load with 16) wins
+    logits[2, 16] = 59.0
     embed = torch.randn((V, H), device=cuda_device).to(torch.bfloat16)
     tokens = torch.zeros(B, dtype=torch.int32, device=cuda_device)
     h = torch.empty((B, H), device=cuda_device, dtype=torch.bfloat16)

@@ -151,7 +151,32 @@ __global__ void __launch_bounds__(1024) argmax_embed_kernel(const __nv_bfloat16 
     const __nv_bfloat16 *lr = logits + (int64_t)row * V;
     float best = -INFINITY;
     int idx = 0x7fffffff;
-    for (int i = tid; i < V; i += blockDim.x) {
+    // 16-byte loads, kU of them in flight per thread before any compare (a
+    // row is ~250 KB read by one CTA: latency, not bandwidth, bounds it)
+    constexpr int kU = 8;
+    const int nvec = ((reinterpret_cast<uintptr_t>(lr) & 15) == 0) ? V / 8 : 0;
+    const uint4 *lv = reinterpret_cast<const uint4 *>(lr);
+    for (int base = 0; base < nvec; base += kU * (int)blockDim.x) {
+        uint4 r[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int j = base + u * (int)blockDim.x + tid;
+            r[u] = j < nvec ? __ldcs(lv + j) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int j = base + u * (int)blockDim.x + tid;
+            if (j >= nvec) break;
+            const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float v = __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));
+                const int i = j * 8 + e;
+                if (v > best || (v == best && i < idx)) best = v, idx = i;
+            }
+        }
+    }
+    for (int i = nvec * 8 + tid; i < V; i += blockDim.x) {
         const float v = __bfloat162float(lr[i]);
         if (v > best || (v == best && i < idx)) best = v, idx = i;
     }
