@@ -58,6 +58,8 @@ def parse():
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
     ap.add_argument("--rows", type=int, default=1, help="activation rows M for --case gemv")
     ap.add_argument("--shape", default=None, help="one N,K for --case gemv (default: BASELINE's four shapes)")
+    ap.add_argument("--format", default="q4_0", choices=["q4_0", "q8_0"],
+                    help="weight format for --case gemv (q8_0 times tn_q8_0_linear: quantiser + GEMV)")
     ap.add_argument("--batch", type=int, default=1, help="sequences decoded together (BASELINE: 1 and 16)")
     ap.add_argument("--seqs", default="512,4096,16384", help="sequence lengths for --case sdpa_prefill")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
@@ -126,6 +128,18 @@ def random_q4_blob(n: int, k: int, gen, dev):
     from torchnative_b200.llama_decode import random_q4_blob as r
 
     return r(n, k, gen, dev)
+
+
+def random_q8_blob(n: int, k: int, gen, dev):
+    """A synthetic Q8_0 weight on the device: random code bytes, scales
+    f16(|N(0,1)| * 0.001), in BlockQ8_0's 34-byte layout."""
+    import torch
+
+    nb = n * (k // 32)
+    blob = torch.randint(0, 256, (nb * 34,), device=dev, dtype=torch.uint8, generator=gen)
+    d = (torch.randn(nb, device=dev, generator=gen).abs() * 0.001).to(torch.float16)
+    blob.view(nb, 34)[:, 0:2] = d.view(torch.uint8).view(nb, 2)
+    return blob
 
 
 PROMPT = 2048
@@ -602,10 +616,11 @@ def run_case_gemv(args):
     shapes = ((14336, 4096), (4096, 14336), (6144, 4096), (28672, 4096))
     if args.shape:
         shapes = (tuple(int(x) for x in args.shape.split(",")),)
+    q8w = args.format == "q8_0"
     for n, k in shapes:
-        wbytes = q4_bytes(n, k)
+        wbytes = n * (k // 32) * 34 if q8w else q4_bytes(n, k)
         copies = max(2, -(-300_000_000 // wbytes))
-        ws = [random_q4_blob(n, k, gen, dev) for _ in range(copies)]
+        ws = [random_q8_blob(n, k, gen, dev) if q8w else random_q4_blob(n, k, gen, dev) for _ in range(copies)]
         x = torch.randn((M, k), device=dev, generator=gen).to(torch.bfloat16)
         codes = torch.empty((M, k), device=dev, dtype=torch.int8)
         scales = torch.empty((M, k // 32), device=dev)
@@ -616,16 +631,26 @@ def run_case_gemv(args):
                                           P(scales.data_ptr()), P(offs.data_ptr()), M, k, s()))
 
         def launch(w):
+            if q8w:  # the bf16 activation's quantiser launch, then the Q8_0-weight GEMV
+                N.check(L.tn_q8_0_linear(P(x.data_ptr()), N.TN_BF16, k, P(w.data_ptr()), None, P(y.data_ptr()),
+                                         N.TN_BF16, M, n, k, N.TN_ACT_Q8_0, s()))
+                return
             N.check(L.tn_q4_0_linear_q8(P(codes.data_ptr()), k, P(scales.data_ptr()), P(offs.data_ptr()),
                                         P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, M, n, k,
                                         N.TN_WEIGHTS_STATIC, s()))
 
-        launch(ws[0])
-        torch.cuda.synchronize()
+        # warm on the capture stream: the workspace is per stream and must
+        # exist before the capture (nothing may allocate while capturing)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            launch(ws[0])
+        side.synchronize()
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        with torch.cuda.graph(g, stream=side):
             for w in ws:
                 launch(w)
+        torch.cuda.current_stream().wait_stream(side)
         for _ in range(args.warmup):
             g.replay()
         torch.cuda.synchronize()
@@ -637,7 +662,7 @@ def run_case_gemv(args):
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / (args.steps * copies)
         algo = wbytes + M * (k + k // 32 * 8) + M * n * 2
-        print(json.dumps({"case": "gemv", "M": M, "N": n, "K": k, "us_per_launch": us,
+        print(json.dumps({"case": "gemv", "format": args.format, "M": M, "N": n, "K": k, "us_per_launch": us,
                           "GBps": algo / us / 1e3, "frac": algo / us / 1e3 / peak, "peak": peak,
                           "peak_kind": peak_kind, "copies": copies}), flush=True)
         del ws

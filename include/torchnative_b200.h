@@ -123,6 +123,13 @@ TN_API int tn_q4_0_dequantize(const void *blob, float *out, int64_t rows, int64_
 TN_API int tn_q8_0_quantize(const void *x, int x_dtype, int64_t x_row_stride, void *blob, int64_t rows,
                      int64_t cols, void *stream);
 
+/* Q8_0 reader: blob -> float32 [rows, cols], bit-identical to
+ * BlockQ8_0::to_float (k_quants.rs:658-674), behind torch._C._dequantize for a
+ * q8_0 weight (quant.rs:180-189); replaces candle's dequantize_block_q8_0_f32
+ * (vendor/candle-core/src/quantized/cuda.rs:105-160). Writer: tn_q8_0_quantize (the
+ * same BlockQ8_0::from_float serves weights and activations). */
+TN_API int tn_q8_0_dequantize(const void *blob, float *out, int64_t rows, int64_t cols, void *stream);
+
 /* torch._C._quantized_linear(input, weight, bias) (torch_c/src/quant.rs:286-369):
  * y[M, N] = x[M, K] @ W[N, K]^T (+ bias[N]).
  *   x: device [M, K], dtype x_dtype in {F32, BF16, F16}, row stride
@@ -142,6 +149,19 @@ TN_API int tn_q8_0_quantize(const void *x, int x_dtype, int64_t x_row_stride, vo
 TN_API int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob,
                    const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
                    int act_mode, void *stream);
+
+/* The same torch._C._quantized_linear for a Q8_0 weight (quant.rs:286-369 with
+ * format "q8_0"): w_blob is N rows of K/32 GGML BlockQ8_0 blocks of 34 bytes
+ * (f16 d, then 32 int8 codes; k_quants.rs:652-756). The activations are
+ * quantised to Q8_0 as for Q4_0 and every output element is
+ * sum over blocks of (i32 sum q8_w * q8_x) * d_w * d_x in f32, the arithmetic
+ * of BlockQ8_0::vec_dot_unopt (k_quants.rs:737-756). Replaces candle's CUDA
+ * arm for GgmlDType::Q8_0 (quantized/cuda.rs:846-877). Every M runs on the
+ * decode GEMV (chunks of at most 16 rows). Same arguments, refusals and
+ * workspace rules as tn_q4_0_linear. */
+TN_API int tn_q8_0_linear(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob,
+                          const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
+                          int act_mode, void *stream);
 
 /* The same linear split in two, for callers that fuse the activation
  * quantisation into the kernel that produces the activations (an RMSNorm or a

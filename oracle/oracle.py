@@ -57,6 +57,10 @@ def lib():
         L.tno_q4_0_q8_0_dot.restype = ctypes.c_float
         L.tno_q4_0_linear.argtypes = [p, p, p, f32p, i64, i64, i64, ctypes.c_int]
         L.tno_q4_0_linear.restype = None
+        L.tno_q8_0_q8_0_dot.argtypes = [p, p, i64]
+        L.tno_q8_0_q8_0_dot.restype = ctypes.c_float
+        L.tno_q8_0_linear.argtypes = [p, p, p, f32p, i64, i64, i64, ctypes.c_int]
+        L.tno_q8_0_linear.restype = None
         L.tno_sdpa.argtypes = [p, p, p, p, ctypes.c_int, p, p, p, ctypes.c_int, i64, i64, i64, i64,
                                i64, i64, p, p, p, ctypes.c_int, ctypes.c_double, ctypes.c_int]
         L.tno_sdpa.restype = None
@@ -117,6 +121,22 @@ def q4_0_linear(x: np.ndarray, w_blob: bytes | np.ndarray, n_out: int, bias: np.
     y = np.empty((m, n_out), dtype=np.float32)
     b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
     lib().tno_q4_0_linear(_ptr(x), _ptr(w), _ptr(b), _ptr(y), m, n_out, k, int(threads))
+    return y.reshape(*lead, n_out)
+
+
+def q8_0_linear(x: np.ndarray, w_blob: bytes | np.ndarray, n_out: int, bias: np.ndarray | None = None,
+                threads: int = 1) -> np.ndarray:
+    """torch._C._quantized_linear for a Q8_0 weight on the CPU (quant.rs:286-369 ->
+    k_quants.rs:2430-2580 with BlockQ8_0::vec_dot_unopt, :737-756)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    lead, k = x.shape[:-1], x.shape[-1]
+    m = int(np.prod(lead)) if lead else 1
+    w = np.frombuffer(w_blob, dtype=np.uint8) if isinstance(w_blob, (bytes, bytearray)) else w_blob
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    assert w.size == n_out * (k // 32) * Q8_0_BLOCK_BYTES
+    y = np.empty((m, n_out), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    lib().tno_q8_0_linear(_ptr(x), _ptr(w), _ptr(b), _ptr(y), m, n_out, k, int(threads))
     return y.reshape(*lead, n_out)
 
 

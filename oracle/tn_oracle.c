@@ -201,7 +201,26 @@ float tno_q4_0_q8_0_dot(const uint8_t *w, const uint8_t *xq, int64_t nblocks) {
     return sumf;
 }
 
+float tno_q8_0_q8_0_dot(const uint8_t *w, const uint8_t *xq, int64_t nblocks) {
+    /* BlockQ8_0::vec_dot_unopt, k_quants.rs:737-756: the same order as the
+     * Q4_0 dot above -- integer block sum of signed codes, then
+     * sumf += (sum_i as f32 * d_w) * d_x, block after block. */
+    float sumf = 0.0f;
+    for (int64_t b = 0; b < nblocks; ++b) {
+        const uint8_t *wb = w + b * 34;
+        const uint8_t *xb = xq + b * 34;
+        int32_t sum_i = 0;
+        for (int j = 0; j < 32; ++j) sum_i += (int32_t)(int8_t)wb[2 + j] * (int32_t)(int8_t)xb[2 + j];
+        float dw = tno_f16_to_f32(get_u16(wb));
+        float dx = tno_f16_to_f32(get_u16(xb));
+        sumf += (float)sum_i * dw * dx;
+    }
+    return sumf;
+}
+
 /* ---- the matmul: quads of output columns split across workers ----------- */
+
+typedef float (*dot_fn)(const uint8_t *, const uint8_t *, int64_t);
 
 typedef struct {
     const uint8_t *xq;
@@ -209,6 +228,8 @@ typedef struct {
     float *y;
     int64_t M, N, nb;
     int64_t quad_begin, quad_end;
+    dot_fn dot;
+    int64_t wblock; /* bytes per weight block: 18 (Q4_0) or 34 (Q8_0) */
 } lin_job;
 
 static void *lin_worker(void *arg) {
@@ -221,7 +242,7 @@ static void *lin_worker(void *arg) {
                 const uint8_t *xr = j->xq + r * j->nb * 34;
                 for (int c = 0; c < 4; ++c) {
                     int64_t col = q * 4 + c;
-                    j->y[r * j->N + col] = tno_q4_0_q8_0_dot(j->w + col * j->nb * 18, xr, j->nb);
+                    j->y[r * j->N + col] = j->dot(j->w + col * j->nb * j->wblock, xr, j->nb);
                 }
             }
         }
@@ -229,8 +250,8 @@ static void *lin_worker(void *arg) {
     return NULL;
 }
 
-void tno_q4_0_linear(const float *x, const uint8_t *w_blob, const float *bias, float *y,
-                     int64_t M, int64_t N, int64_t K, int threads) {
+static void q_linear(const float *x, const uint8_t *w_blob, const float *bias, float *y, int64_t M, int64_t N,
+                     int64_t K, int threads, dot_fn dot, int64_t wblock) {
     int64_t nb = K / 32;
     uint8_t *xq = (uint8_t *)malloc((size_t)(M * nb * 34 + 1));
     for (int64_t r = 0; r < M; ++r) tno_q8_0_quantize(x + r * K, xq + r * nb * 34, K);
@@ -245,7 +266,7 @@ void tno_q4_0_linear(const float *x, const uint8_t *w_blob, const float *bias, f
         int64_t qb = t * per, qe = qb + per < quads ? qb + per : quads;
         created[t] = 0;
         if (qb >= qe) continue;
-        jobs[t] = (lin_job){xq, w_blob, y, M, N, nb, qb, qe};
+        jobs[t] = (lin_job){xq, w_blob, y, M, N, nb, qb, qe, dot, wblock};
         if (t + 1 < threads && pthread_create(&tid[t], NULL, lin_worker, &jobs[t]) == 0)
             created[t] = 1;
         else
@@ -256,11 +277,21 @@ void tno_q4_0_linear(const float *x, const uint8_t *w_blob, const float *bias, f
     /* the column tail (k_quants.rs:2555-2575): the same dot, one column at a time */
     for (int64_t r = 0; r < M; ++r)
         for (int64_t col = quads * 4; col < N; ++col)
-            y[r * N + col] = tno_q4_0_q8_0_dot(w_blob + col * nb * 18, xq + r * nb * 34, nb);
+            y[r * N + col] = dot(w_blob + col * nb * wblock, xq + r * nb * 34, nb);
     free(xq);
     if (bias)
         for (int64_t r = 0; r < M; ++r)
             for (int64_t col = 0; col < N; ++col) y[r * N + col] = y[r * N + col] + bias[col];
+}
+
+void tno_q4_0_linear(const float *x, const uint8_t *w_blob, const float *bias, float *y,
+                     int64_t M, int64_t N, int64_t K, int threads) {
+    q_linear(x, w_blob, bias, y, M, N, K, threads, tno_q4_0_q8_0_dot, 18);
+}
+
+void tno_q8_0_linear(const float *x, const uint8_t *w_blob, const float *bias, float *y,
+                     int64_t M, int64_t N, int64_t K, int threads) {
+    q_linear(x, w_blob, bias, y, M, N, K, threads, tno_q8_0_q8_0_dot, 34);
 }
 
 /* ------------------------------------------------------------------------ */

@@ -61,6 +61,16 @@ float tno_q4_0_q8_0_dot(const uint8_t *w_row, const uint8_t *xq_row, int64_t nbl
 void tno_q4_0_linear(const float *x, const uint8_t *w_blob, const float *bias, float *y,
                      int64_t M, int64_t N, int64_t K, int threads);
 
+/* One output element for a Q8_0 weight: BlockQ8_0::vec_dot_unopt,
+ * k_quants.rs:737-756 (integer block sum, then (sum * d_w) * d_x added in
+ * order). */
+float tno_q8_0_q8_0_dot(const uint8_t *w_row, const uint8_t *xq_row, int64_t nblocks);
+
+/* torch._C._quantized_linear for a Q8_0 weight (N rows of 34-byte blocks):
+ * the same steps as tno_q4_0_linear with tno_q8_0_q8_0_dot per element. */
+void tno_q8_0_linear(const float *x, const uint8_t *w_blob, const float *bias, float *y,
+                     int64_t M, int64_t N, int64_t K, int threads);
+
 /* ---- scaled_dot_product_attention ----------------------------------------
  * sdpa_flash_cpu's default branch, torchnative/rust/torch_c/src/aten.rs:
  * 10092-10460 (arithmetic 10327-10420), GQA through repeat_kv_heads

@@ -117,3 +117,34 @@ def random_q4_0_blob(rng: np.random.Generator, n: int, k: int) -> bytes:
     codes = rng.integers(-8, 8, size=(n, k), dtype=np.int64)
     d = (np.abs(rng.standard_normal((n, k // 32))) * 0.01).astype(np.float16)
     return q4_0_blob_from_codes(codes, d)
+
+
+def exact_linear_q8_0(xq_blob: bytes, w_blob: bytes, rows: int, out_features: int, in_features: int):
+    """The same for a Q8_0 weight (BlockQ8_0::vec_dot_unopt, k_quants.rs:737-756):
+    every term d_x * d_w * sum(q_x * q_w) is exact in float64 (11 + 11 + 20 bits)."""
+    dw, qw = q8_0_parts(w_blob, out_features, in_features)
+    dx, qx = q8_0_parts(xq_blob, rows, in_features)
+    ints = np.einsum("rbk,obk->rob", qx, qw)
+    absints = np.einsum("rbk,obk->rob", np.abs(qx), np.abs(qw))
+    scale = dx[:, None, :] * dw[None, :, :]
+    value, rel = _sum_terms(ints.astype(np.float64) * scale)
+    abs_sum = (absints.astype(np.float64) * np.abs(scale)).sum(axis=2)
+    return value, abs_sum, rel * abs_sum
+
+
+def q8_0_blob_from_codes(codes: np.ndarray, d: np.ndarray) -> bytes:
+    """A Q8_0 blob from signed codes in [-127, 127] ([N, K]) and f16 scales
+    ([N, K/32]), in BlockQ8_0's layout (k_quants.rs:652-674)."""
+    n, k = codes.shape
+    out = np.empty((n, k // 32, 34), dtype=np.uint8)
+    out[:, :, 0:2] = np.asarray(d, dtype=np.float16).reshape(n, k // 32, 1).view(np.uint8)
+    out[:, :, 2:] = codes.astype(np.int8).reshape(n, k // 32, 32).view(np.uint8)
+    return out.tobytes()
+
+
+def random_q8_0_blob(rng: np.random.Generator, n: int, k: int) -> bytes:
+    """Synthetic Q8_0 weight: codes uniform in [-127, 127], scales
+    f16(|N(0,1)| * 0.001)."""
+    codes = rng.integers(-127, 128, size=(n, k), dtype=np.int64)
+    d = (np.abs(rng.standard_normal((n, k // 32))) * 0.001).astype(np.float16)
+    return q8_0_blob_from_codes(codes, d)

@@ -141,3 +141,42 @@ def test_lossless_integer_operands_give_the_exact_integer_matmul():
     x[:, ::32] = 127.0  # every block's absmax is 127 -> d = 1, codes = x
     y = oracle.q4_0_linear(x, blob, N)
     assert (y.astype(np.float64) == x.astype(np.float64) @ codes.T.astype(np.float64)).all()
+
+
+# ---- Q8_0 weights (BlockQ8_0::vec_dot_unopt, k_quants.rs:737-756) ----------
+
+
+@pytest.mark.parametrize("rows,out_f,in_f,seed", [(1, 8, 64, 21), (3, 12, 512, 22), (4, 37, 4096, 23)])
+def test_q8_0_weight_linear_within_counted_bound_of_exact_value(rows, out_f, in_f, seed):
+    """The Q8_0-weight linear: the weight written by BlockQ8_0::from_float
+    (pinned to gguf-py above), the activations quantised the same way, and the
+    result within the reference's counted bound of the exact value; the bound
+    refuses the unquantised-activation answer."""
+    w = (np.random.default_rng(seed + 1).standard_normal((out_f, in_f)) * 0.05).astype(np.float32)
+    x = q4_exact.tie_free_gauss(rows, in_f, seed)
+    blob = oracle.q8_0_quantize(w)
+    got = oracle.q8_0_linear(x, blob, out_f, threads=3)
+    xq = oracle.q8_0_quantize(x)
+    exact, abs_sum, ref_err = q4_exact.exact_linear_q8_0(xq, blob, rows, out_f, in_f)
+    bound = q4_exact.linear_bound(in_f, abs_sum, ref_err)
+    assert float(np.max(np.abs(got - exact) / bound)) <= 1.0
+    wdq = oracle.q8_0_dequantize(blob, out_f * in_f).astype(np.float64).reshape(out_f, in_f)
+    assert float(np.max(np.abs(x.astype(np.float64) @ wdq.T - exact) / bound)) > 1.0
+
+
+def test_q8_0_weight_linear_is_the_row_dot_and_lossless_operands_are_exact():
+    rng = np.random.default_rng(25)
+    M, N, K = 3, 10, 256
+    codes = rng.integers(-127, 128, size=(N, K))
+    blob = q4_exact.q8_0_blob_from_codes(codes, np.ones((N, K // 32), dtype=np.float16))
+    x = rng.integers(-127, 128, size=(M, K)).astype(np.float32)
+    x[:, ::32] = 127.0  # every block's absmax is 127 -> d = 1, codes = x
+    y = oracle.q8_0_linear(x, blob, N, threads=2)
+    assert (y.astype(np.float64) == x.astype(np.float64) @ codes.T.astype(np.float64)).all()
+    xq = oracle.q8_0_quantize(x)
+    nb = K // 32
+    for r in range(M):
+        for c in range(N):
+            one = oracle.lib().tno_q8_0_q8_0_dot(np.frombuffer(blob, np.uint8)[c * nb * 34:].ctypes.data,
+                                                 np.frombuffer(xq, np.uint8)[r * nb * 34:].ctypes.data, nb)
+            assert np.float32(one) == y[r, c]

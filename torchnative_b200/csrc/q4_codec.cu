@@ -83,6 +83,18 @@ __global__ void q4_0_dequantize_kernel(const uint8_t *__restrict__ blob, float *
     }
 }
 
+// BlockQ8_0::to_float, k_quants.rs:658-674: code * f32(d), exact in f32
+// (an 8-bit integer times an 11-bit significand).
+__global__ void q8_0_dequantize_kernel(const uint8_t *__restrict__ blob, float *__restrict__ out, int64_t nblocks) {
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    const uint8_t *b = blob + i * 34;
+    const float d = half_bits_to_f32((uint32_t)b[0] | ((uint32_t)b[1] << 8));
+    float *o = out + i * 32;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) o[j] = __fmul_rn(static_cast<float>(static_cast<int8_t>(b[2 + j])), d);
+}
+
 // BlockQ8_0::from_float, k_quants.rs:676-706, for one 32-element block of row
 // `r`, block `b`. Returns the f16 scale bits and writes the 32 codes.
 template <typename T>
@@ -292,6 +304,22 @@ int tn_q4_0_dequantize(const void *blob, float *out, int64_t rows, int64_t cols,
     if (!blob || !out) return tn::set_error(TN_ERR_INVALID, std::string(op) + ": null pointer");
     int threads = 128;
     tn::q4_0_dequantize_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
+        static_cast<const uint8_t *>(blob), out, nb);
+    __atomic_fetch_add(&tn::counters().q4_codec_launches, 1ull, __ATOMIC_RELAXED);
+    return tn::check_launch(op);
+}
+
+int tn_q8_0_dequantize(const void *blob, float *out, int64_t rows, int64_t cols, void *stream) {
+    const char *op = "torch._C._dequantize";
+    if (rows < 0 || cols < 0) return tn::set_error(TN_ERR_SHAPE, std::string(op) + ": negative size");
+    if (cols % 32 != 0)
+        return tn::set_error(TN_ERR_SHAPE, std::string(op) + ": q8_0 rows are whole 32-element blocks, got " +
+                                               std::to_string(cols) + " columns");
+    int64_t nb = rows * (cols / 32);
+    if (nb == 0) return TN_OK;
+    if (!blob || !out) return tn::set_error(TN_ERR_INVALID, std::string(op) + ": null pointer");
+    int threads = 128;
+    tn::q8_0_dequantize_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
         static_cast<const uint8_t *>(blob), out, nb);
     __atomic_fetch_add(&tn::counters().q4_codec_launches, 1ull, __ATOMIC_RELAXED);
     return tn::check_launch(op);

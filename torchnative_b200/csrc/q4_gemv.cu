@@ -52,8 +52,9 @@ struct GemvParams {
     int M;
     int nb;       // blocks per weight row
     int nbp;      // nb rounded up to even (x staging granularity)
-    int rowbytes; // 18 * nb
-    int wpc;      // consumer warps per chunk (a chunk is 2 * wpc rows)
+    int rowbytes; // 18 * nb (Q4_0 weights) or 34 * nb (Q8_0 weights)
+    int wpc;      // consumer warps per chunk (a chunk is rpw * wpc rows)
+    int rpw;      // weight rows per consumer warp in a chunk: 2, or 1 for rows too long to stage two per warp
     int slot_bytes;
     int nslots;
     int flags;
@@ -79,6 +80,7 @@ struct GemvParams {
     int8_t *oq;
     float *od, *oc;
     int64_t oq_row_stride;
+    int wfmt;  // weight format: 0 = Q4_0 (18-byte blocks), 1 = Q8_0 (34-byte blocks)
 };
 
 // Shared-memory layout (dynamic), as 32-bit shared-window addresses:
@@ -222,6 +224,68 @@ __device__ __forceinline__ void single_dot(const Blk &a, const Blk &bb, int b, c
             const float xd = ldsf(s.xds + so), xc = ldsf(s.xcs + so);
             acc[0][m] = fmaf(magic_dot(a, xl, xh) - xc, a.d * xd, acc[0][m]);
             if (TWO) acc[1][m] = fmaf(magic_dot(bb, xl, xh) - xc, bb.d * xd, acc[1][m]);
+        }
+    }
+}
+
+// Q8_0 weights (BlockQ8_0, k_quants.rs:652-756): 32 signed codes and an f16
+// scale per block. The block dot is the same exact integer as for Q4_0 (signed
+// dp4a, |sum| <= 32 * 127 * 127 < 2^22, so the magic-number sum is exact) and
+// needs no code-sum offset: subtract the magic constant itself.
+struct Blk8 {
+    uint32_t c[8];  // codes 0-15 in c[0..3], codes 16-31 in c[4..7]
+    float d;
+};
+constexpr float kMagicF = 12582912.0f;
+
+__device__ __forceinline__ float magic_dot8(const Blk8 &w, int4 xl, int4 xh) {
+    int I = (int)kMagic;
+    I = __dp4a((int)w.c[0], xl.x, I);
+    I = __dp4a((int)w.c[1], xl.y, I);
+    I = __dp4a((int)w.c[2], xl.z, I);
+    I = __dp4a((int)w.c[3], xl.w, I);
+    I = __dp4a((int)w.c[4], xh.x, I);
+    I = __dp4a((int)w.c[5], xh.y, I);
+    I = __dp4a((int)w.c[6], xh.z, I);
+    I = __dp4a((int)w.c[7], xh.w, I);
+    return __int_as_float(I);
+}
+
+template <int MT, bool TWO>
+__device__ __forceinline__ void pair_dot8(const Blk8 &a0, const Blk8 &a1, const Blk8 &b0, const Blk8 &b1, int pair,
+                                          const Smem &s, const GemvParams &p, float (&acc)[2][MT]) {
+    const uint32_t xrow = (uint32_t)p.nbp * 32;
+    const uint32_t c0 = xchunk(pair, 0), c1 = xchunk(pair, 1), c2 = xchunk(pair, 2), c3 = xchunk(pair, 3);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        if (m < p.M) {
+            const uint32_t xb = s.xs + m * xrow;
+            const int4 x0 = lds128(xb + c0), x1 = lds128(xb + c1), x2 = lds128(xb + c2), x3 = lds128(xb + c3);
+            const float2 xd = lds64f(s.xds + (uint32_t)(m * p.nbp + 2 * pair) * 4);
+            acc[0][m] = fmaf(magic_dot8(a0, x0, x1) - kMagicF, a0.d * xd.x, acc[0][m]);
+            acc[0][m] = fmaf(magic_dot8(a1, x2, x3) - kMagicF, a1.d * xd.y, acc[0][m]);
+            if (TWO) {
+                acc[1][m] = fmaf(magic_dot8(b0, x0, x1) - kMagicF, b0.d * xd.x, acc[1][m]);
+                acc[1][m] = fmaf(magic_dot8(b1, x2, x3) - kMagicF, b1.d * xd.y, acc[1][m]);
+            }
+        }
+    }
+}
+
+template <int MT, bool TWO>
+__device__ __forceinline__ void single_dot8(const Blk8 &a, const Blk8 &bb, int b, const Smem &s, const GemvParams &p,
+                                            float (&acc)[2][MT]) {
+    const uint32_t xrow = (uint32_t)p.nbp * 32;
+    const int pair = b >> 1, cb = (b & 1) * 2;
+    const uint32_t cl = xchunk(pair, cb), ch = xchunk(pair, cb + 1);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        if (m < p.M) {
+            const uint32_t xb = s.xs + m * xrow;
+            const int4 xl = lds128(xb + cl), xh = lds128(xb + ch);
+            const float xd = ldsf(s.xds + (uint32_t)(m * p.nbp + b) * 4);
+            acc[0][m] = fmaf(magic_dot8(a, xl, xh) - kMagicF, a.d * xd, acc[0][m]);
+            if (TWO) acc[1][m] = fmaf(magic_dot8(bb, xl, xh) - kMagicF, bb.d * xd, acc[1][m]);
         }
     }
 }
@@ -539,6 +603,68 @@ __device__ __forceinline__ Blk load_block_global(const uint8_t *blk) {
     return unpack(u[1] | (u[2] << 16), u[3] | (u[4] << 16), u[5] | (u[6] << 16), u[7] | (u[8] << 16), u[0]);
 }
 
+// One 34-byte Q8_0 block from global memory, as 17 little-endian halves.
+__device__ __forceinline__ Blk8 load_block8_global(const uint8_t *blk) {
+    const unsigned short *h = reinterpret_cast<const unsigned short *>(blk);
+    uint32_t u[17];
+#pragma unroll
+    for (int i = 0; i < 17; ++i) u[i] = __ldg(h + i);
+    Blk8 b;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b.c[i] = u[1 + 2 * i] | (u[2 + 2 * i] << 16);
+    b.d = half_bits_to_f32(u[0]);
+    return b;
+}
+
+// Staged Q8_0 rows: a pair of blocks is 68 bytes = 17 aligned words. Block
+// 2*pair: scale in the low half of word 0, codes straddling words 0..8 (funnel
+// shifts); block 2*pair+1: scale in the high half of word 8, codes in words
+// 9..16.
+__device__ __forceinline__ void unpack8_pair(const uint32_t (&w)[17], Blk8 &b0, Blk8 &b1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        b0.c[i] = __funnelshift_r(w[i], w[i + 1], 16);
+        b1.c[i] = w[9 + i];
+    }
+    b0.d = half_bits_to_f32(w[0] & 0xffffu);
+    b1.d = half_bits_to_f32(w[8] >> 16);
+}
+
+template <int MT, bool TWO>
+__device__ __forceinline__ void staged_rows8(const Smem &s, const GemvParams &p, uint32_t rowA, uint32_t rowB,
+                                             int lane, float (&acc)[2][MT]) {
+    const int npairs = p.nb >> 1;
+    for (int pp = lane; pp < npairs; pp += 32) {
+        const uint32_t a = rowA + pp * 68, b = rowB + pp * 68;
+        uint32_t wa[17], wb[17];
+#pragma unroll
+        for (int i = 0; i < 17; ++i) wa[i] = lds32(a + 4 * i);
+        if (TWO) {
+#pragma unroll
+            for (int i = 0; i < 17; ++i) wb[i] = lds32(b + 4 * i);
+        }
+        Blk8 a0, a1, b0, b1;
+        unpack8_pair(wa, a0, a1);
+        if (TWO) {
+            unpack8_pair(wb, b0, b1);
+        } else {
+            b0 = a0;
+            b1 = a1;
+        }
+        pair_dot8<MT, TWO>(a0, a1, b0, b1, pp, s, p, acc);
+    }
+}
+
+template <int MT, bool TWO>
+__device__ __forceinline__ void global_rows8(const Smem &s, const GemvParams &p, const uint8_t *rowA,
+                                             const uint8_t *rowB, int lane, float (&acc)[2][MT]) {
+    for (int b = lane; b < p.nb; b += 32) {
+        const Blk8 a = load_block8_global(rowA + b * 34);
+        const Blk8 bb = TWO ? load_block8_global(rowB + b * 34) : a;
+        single_dot8<MT, TWO>(a, bb, b, s, p, acc);
+    }
+}
+
 template <int MT, bool TWO>
 __device__ __forceinline__ void staged_rows(const Smem &s, const GemvParams &p, uint32_t rowA, uint32_t rowB,
                                             int lane, float (&acc)[2][MT]) {
@@ -575,7 +701,8 @@ __device__ __forceinline__ void global_rows(const Smem &s, const GemvParams &p, 
     }
 }
 
-template <int MT, bool STAGED, int XM>
+// WF: weight format, 0 = Q4_0, 1 = Q8_0.
+template <int MT, bool STAGED, int XM, int WF>
 __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, p);
@@ -588,9 +715,9 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
     const int64_t r0 = c * (p.N / gran) / G * gran, r1 = (c + 1) * (p.N / gran) / G * gran;
     const int nrows = (int)(r1 - r0);
     const int64_t ycol0 = pairs ? r0 >> 1 : r0;
-    // Chunks of R = 2 * wpc consecutive rows; chunk j lives in slot j % nslots
+    // Chunks of R = rpw * wpc consecutive rows; chunk j lives in slot j % nslots
     // and is consumed by warp group j % groups (wpc warps, two rows each).
-    const int wpc = p.wpc, R = 2 * p.wpc, groups = kConsumerWarps / p.wpc;
+    const int wpc = p.wpc, R = p.rpw * p.wpc, groups = kConsumerWarps / p.wpc;
     const int nchunks = (nrows + R - 1) / R;
 
     if (STAGED && threadIdx.x == 0) {
@@ -663,8 +790,8 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
     const int group = warp / wpc, gw = warp % wpc;
     bool failed = false;
     for (int j = group; j < nchunks && !failed; j += groups) {
-        const int i = j * R + 2 * gw;  // my first row within the CTA's range
-        const bool has_a = i < nrows, has_b = i + 1 < nrows;
+        const int i = j * R + p.rpw * gw;  // my first row within the CTA's range
+        const bool has_a = i < nrows, has_b = p.rpw == 2 && i + 1 < nrows;
         float acc[2][MT];
 #pragma unroll
         for (int r = 0; r < 2; ++r)
@@ -677,19 +804,33 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
                 failed = true;
                 break;
             }
-            const uint32_t ra = s.slots + (uint32_t)slot * p.slot_bytes + (uint32_t)(2 * gw) * p.rowbytes;
-            if (has_b)
-                staged_rows<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
-            else if (has_a)
-                staged_rows<MT, false>(s, p, ra, ra, lane, acc);
+            const uint32_t ra = s.slots + (uint32_t)slot * p.slot_bytes + (uint32_t)(p.rpw * gw) * p.rowbytes;
+            if constexpr (WF == 1) {
+                if (has_b)
+                    staged_rows8<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
+                else if (has_a)
+                    staged_rows8<MT, false>(s, p, ra, ra, lane, acc);
+            } else {
+                if (has_b)
+                    staged_rows<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
+                else if (has_a)
+                    staged_rows<MT, false>(s, p, ra, ra, lane, acc);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.empty[slot]);
         } else if (has_a) {
             const uint8_t *ra = p.w + (r0 + i) * (int64_t)p.rowbytes;
-            if (has_b)
-                global_rows<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
-            else
-                global_rows<MT, false>(s, p, ra, ra, lane, acc);
+            if constexpr (WF == 1) {
+                if (has_b)
+                    global_rows8<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
+                else
+                    global_rows8<MT, false>(s, p, ra, ra, lane, acc);
+            } else {
+                if (has_b)
+                    global_rows<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
+                else
+                    global_rows<MT, false>(s, p, ra, ra, lane, acc);
+            }
         }
         if (has_a) finish_rows<MT>(acc, p, r0 + i, has_b, lane, s, ycol0);
     }
@@ -772,13 +913,13 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
     }
 }
 
-template <int MT, bool STAGED, int XM>
+template <int MT, bool STAGED, int XM, int WF = 0>
 int launch_variant(const GemvParams &p, int grid, size_t smem, cudaStream_t stream) {
     static int configured_for[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && configured_for[dev] < (int)smem) {
-        int st = check_cuda(cudaFuncSetAttribute(q4_gemv_q8_kernel<MT, STAGED, XM>,
+        int st = check_cuda(cudaFuncSetAttribute(q4_gemv_q8_kernel<MT, STAGED, XM, WF>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                             "torch._C._quantized_linear", "cudaFuncSetAttribute");
         if (st) return st;
@@ -794,7 +935,7 @@ int launch_variant(const GemvParams &p, int grid, size_t smem, cudaStream_t stre
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int st = check_cuda(cudaLaunchKernelEx(&cfg, q4_gemv_q8_kernel<MT, STAGED, XM>, p), "torch._C._quantized_linear",
+    int st = check_cuda(cudaLaunchKernelEx(&cfg, q4_gemv_q8_kernel<MT, STAGED, XM, WF>, p), "torch._C._quantized_linear",
                         "cudaLaunchKernelEx");
     if (st) return st;
     __atomic_fetch_add(STAGED ? &counters().q4_gemv_launches : &counters().q4_gemv_generic, 1ull, __ATOMIC_RELAXED);
@@ -809,17 +950,18 @@ size_t smem_bytes(int M, int nbp, int nslots, int slot_bytes, int ycols) {
 
 struct Plan {
     bool ok;
-    int wpc, slot_bytes, nslots;
+    int wpc, slot_bytes, nslots, rpw;
 };
 
-// Chunk size and ring depth. A chunk is 2 * wpc rows copied by one bulk copy:
+// Chunk size and ring depth. A chunk is rpw * wpc rows copied by one bulk copy:
 // the largest wpc whose chunk stays within ~24 KB (many small copies in flight
 // were measured to cap the fetch rate), and enough slots for ~128 KB in flight
 // per SM. nslots is a multiple of the number of warp groups, so chunk j and
 // chunk j - nslots belong to the same group and no warp ever waits on a slot's
 // barrier more than one phase ahead (parity waits cannot tell phases two apart).
-Plan plan_slots(int M, int nbp, int rowbytes, bool staged, size_t budget, size_t in_flight, int ycols = 0) {
-    Plan pl{false, 1, 0, 0};
+Plan plan_slots(int M, int nbp, int rowbytes, bool staged, size_t budget, size_t in_flight, int ycols = 0,
+                int rpw = 2) {
+    Plan pl{false, 1, 0, 0, 2};
     const size_t base = smem_bytes(M, nbp, 0, 0, ycols);
     if (!staged) {
         pl.ok = base <= budget;
@@ -827,9 +969,9 @@ Plan plan_slots(int M, int nbp, int rowbytes, bool staged, size_t budget, size_t
         return pl;
     }
     int wpc = kConsumerWarps;
-    while (wpc > 1 && 2 * wpc * rowbytes > 24 * 1024) wpc >>= 1;
+    while (wpc > 1 && rpw * wpc * rowbytes > 24 * 1024) wpc >>= 1;
     const int groups = kConsumerWarps / wpc;
-    const int slot_bytes = 2 * wpc * rowbytes;
+    const int slot_bytes = rpw * wpc * rowbytes;
     if (base + (size_t)groups * slot_bytes > budget) return pl;
     int nslots = (int)((budget - base) / slot_bytes);
     const int want = (int)((in_flight + slot_bytes - 1) / slot_bytes);
@@ -837,19 +979,24 @@ Plan plan_slots(int M, int nbp, int rowbytes, bool staged, size_t budget, size_t
     nslots = nslots < kMaxSlots ? nslots : kMaxSlots;
     nslots = (nslots / groups) * groups;
     if (nslots < groups) return pl;
-    pl = Plan{true, wpc, slot_bytes, nslots};
+    pl = Plan{true, wpc, slot_bytes, nslots, rpw};
     return pl;
 }
 
 }  // namespace
 
-int q4_gemv_max_rows(int64_t K) {
+int q4_gemv_max_rows(int64_t K, int wfmt) {
     DeviceFacts f{};
     if (device_facts(&f)) return 0;
-    const int nb = (int)(K / 32), nbp = (nb + 1) & ~1, rowbytes = 18 * nb;
+    const int nb = (int)(K / 32), nbp = (nb + 1) & ~1, rowbytes = (wfmt ? 34 : 18) * nb;
     const bool staged = (K % 256 == 0);
-    for (int mt = 16; mt >= 1; mt >>= 1)
-        if (plan_slots(mt, nbp, rowbytes, staged, (size_t)f.smem_optin - 1024, 128 * 1024).ok) return mt;
+    for (int mt = 16; mt >= 1; mt >>= 1) {
+        if (staged && plan_slots(mt, nbp, rowbytes, true, (size_t)f.smem_optin - 1024, 128 * 1024).ok) return mt;
+        if (staged && plan_slots(mt, nbp, rowbytes, true, (size_t)f.smem_optin - 1024, 128 * 1024, 0, 1).ok)
+            return mt;
+        // rows too long for the staged ring: the unstaged path
+        if (plan_slots(mt, nbp, rowbytes, false, (size_t)f.smem_optin - 1024, 128 * 1024).ok) return mt;
+    }
     return 0;
 }
 
@@ -864,29 +1011,39 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
     p.M = M;
     p.nb = (int)(K / 32);
     p.nbp = (p.nb + 1) & ~1;
-    p.rowbytes = 18 * p.nb;
+    p.rowbytes = (p.wfmt ? 34 : 18) * p.nb;
     p.err = device_error_word();
-    const bool staged = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(p.w) & 15) == 0);
+    bool staged = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(p.w) & 15) == 0);
     const int ycols = p.oq ? kYCap : 0;
     // Two CTAs per SM for M <= 2 (each with ~64 KB in flight): the next
     // kernel's CTAs can then start streaming while this one's last CTAs drain.
-    Plan plan{false, 1, 0, 0};
+    Plan plan{false, 1, 0, 0, 2};
     int ctas_per_sm = 1;
     if (M <= 2) {
         plan = plan_slots(M, p.nbp, p.rowbytes, staged, kTwoCtaBudget, 64 * 1024, ycols);
         if (plan.ok) ctas_per_sm = 2;
     }
     if (!plan.ok) plan = plan_slots(M, p.nbp, p.rowbytes, staged, (size_t)f.smem_optin - 1024, 128 * 1024, ycols);
+    if (!plan.ok && staged && !(flags & TN_EPILOGUE_SILU_MUL_PAIRS))
+        // Rows too long for a ring of 2 rows per consumer warp (Q8_0 weights at
+        // K = 14336: 16 rows of 15 KB): one row per warp (8 rows in the ring).
+        plan = plan_slots(M, p.nbp, p.rowbytes, true, (size_t)f.smem_optin - 1024, 128 * 1024, ycols, 1);
+    if (!plan.ok && staged) {
+        // Still too long: stream them from global memory instead.
+        staged = false;
+        plan = plan_slots(M, p.nbp, p.rowbytes, false, (size_t)f.smem_optin - 1024, 128 * 1024, ycols);
+    }
     if (!plan.ok)
         return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: activation tile too large for "
                                                                    "shared memory");
     p.wpc = plan.wpc;
+    p.rpw = plan.rpw;
     p.slot_bytes = plan.slot_bytes;
     p.nslots = plan.nslots;
     p.flags = flags;
     const size_t smem = smem_bytes(M, p.nbp, plan.nslots, plan.slot_bytes, ycols);
     int64_t grid = (int64_t)f.sm_count * ctas_per_sm;
-    const int64_t by_rows = (N + 2 * plan.wpc - 1) / (2 * plan.wpc);
+    const int64_t by_rows = (N + plan.rpw * plan.wpc - 1) / (plan.rpw * plan.wpc);
     if (by_rows < grid) grid = by_rows > 0 ? by_rows : 1;
     if (p.oq) {
         // whole blocks per CTA, at most kYCap columns of them
@@ -910,6 +1067,21 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
         case X_SILU: TN_GEMV_LAUNCH(MT, X_SILU)                                            \
         default: TN_GEMV_LAUNCH(MT, X_PLANAR)                                              \
         }                                                                                  \
+    }
+    if (p.wfmt == 1) {  // Q8_0 weights: planar activations only
+        if (p.x_mode != X_PLANAR || p.oq)
+            return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: Q8_0 weights take planar "
+                                                                       "activations");
+#define TN_GEMV_LAUNCH8(MT)                                                                \
+    return staged ? launch_variant<MT, true, X_PLANAR, 1>(p, (int)grid, smem, stream)      \
+                  : launch_variant<MT, false, X_PLANAR, 1>(p, (int)grid, smem, stream);
+        if (M <= 1) TN_GEMV_LAUNCH8(1)
+        if (M <= 2) TN_GEMV_LAUNCH8(2)
+        if (M <= 4) TN_GEMV_LAUNCH8(4)
+        if (M <= 8) TN_GEMV_LAUNCH8(8)
+        if (M <= 16) TN_GEMV_LAUNCH8(16)
+#undef TN_GEMV_LAUNCH8
+        return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: GEMV called with M > 16");
     }
     TN_GEMV_CASE_FUSED(1)
     TN_GEMV_CASE_FUSED(2)
@@ -959,6 +1131,25 @@ int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const
     p.y_dtype = y_dtype;
     p.x_mode = X_PLANAR;
     return launch_gemv(p, M, N, K, flags, stream);
+}
+
+int launch_q8w_gemv(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
+                    const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
+                    int flags, cudaStream_t stream) {
+    GemvParams p{};
+    set_link(p, nullptr, N);
+    p.w = w;
+    p.xq = xq;
+    p.xd = xd;
+    p.xc = xc;
+    p.bias = bias;
+    p.y = y;
+    p.xq_row_stride = xq_row_stride;
+    p.y_row_stride = y_row_stride;
+    p.y_dtype = y_dtype;
+    p.x_mode = X_PLANAR;
+    p.wfmt = 1;
+    return launch_gemv(p, M, N, K, flags & ~TN_EPILOGUE_SILU_MUL_PAIRS, stream);
 }
 
 int launch_q4_gemv_fused(int x_mode, const void *xb, int64_t xb_row_stride, const void *xdelta, void *xh_out,

@@ -25,8 +25,15 @@ int launch_q4_gemm(const __half *xq, int64_t xq_row_stride, const float *xd, con
                    void *y, int y_dtype, int64_t y_row_stride, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
 
 // Largest activation-row count (<= 16) one GEMV launch holds in shared memory
-// for this K; 0 if even one row does not fit.
-int q4_gemv_max_rows(int64_t K);
+// for this K (wfmt 0: Q4_0 weights, 1: Q8_0 weights); 0 if even one row does
+// not fit.
+int q4_gemv_max_rows(int64_t K, int wfmt = 0);
+
+// Decode GEMV of Q8_0 weights (34-byte GGML blocks) over planar Q8_0
+// activations (offsets unused): y[m, n] for m < M (M <= 16).
+int launch_q8w_gemv(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
+                    const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
+                    int flags, cudaStream_t stream);
 
 // Decode GEMV over planar Q8_0 activations: y[m, n] for m < M (M <= 16).
 int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,

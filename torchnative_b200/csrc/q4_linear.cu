@@ -94,6 +94,59 @@ extern "C" int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, 
     return TN_OK;
 }
 
+extern "C" int tn_q8_0_linear(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob, const float *bias,
+                              void *y, int y_dtype, int64_t M, int64_t N, int64_t K, int act_mode, void *stream_) {
+    const std::string op = "torch._C._quantized_linear";
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
+    if (x_dtype != TN_F32 && x_dtype != TN_BF16 && x_dtype != TN_F16)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": the activation must be torch.float32, torch.bfloat16 or "
+                                                          "torch.float16 on CUDA, got " +
+                                                          tn_dtype_name(x_dtype));
+    if (y_dtype != TN_F32 && y_dtype != TN_BF16 && y_dtype != TN_F16)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": unsupported output dtype " + tn_dtype_name(y_dtype));
+    if (act_mode != TN_ACT_Q8_0 && act_mode != TN_ACT_FLOAT)
+        return tn::set_error(TN_ERR_INVALID, op + ": unknown activation mode " + std::to_string(act_mode));
+    if (M < 0 || N < 0 || K < 0) return tn::set_error(TN_ERR_SHAPE, op + ": negative size");
+    if (K % 32 != 0)
+        return tn::set_error(TN_ERR_SHAPE, op + ": mat1 and mat2 shapes cannot be multiplied ([" + std::to_string(M) +
+                                               ", " + std::to_string(K) + "] and " + std::to_string(K) + "x" +
+                                               std::to_string(N) + "): a q8_0 row is whole 32-element blocks");
+    if (M == 0 || N == 0) return TN_OK;
+    if (K == 0) return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": in_features == 0 is not implemented");
+    if (!x || !w_blob || !y) return tn::set_error(TN_ERR_INVALID, op + ": null device pointer");
+    if (x_row_stride < K) return tn::set_error(TN_ERR_INVALID, op + ": activation row stride smaller than in_features");
+    if ((reinterpret_cast<uintptr_t>(w_blob) & 1) != 0)
+        return tn::set_error(TN_ERR_INVALID, op + ": the q8_0 blob must be at least 2-byte aligned");
+    if (act_mode == TN_ACT_FLOAT)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED,
+                             op + ": the float-activation mode is not implemented on CUDA yet; use the Q8_0 mode "
+                                  "(the reference's arithmetic)");
+    const int chunk = tn::q4_gemv_max_rows(K, 1);
+    if (chunk <= 0)
+        return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": in_features " + std::to_string(K) +
+                                                         " is too large for the decode kernel's shared memory");
+    const int64_t nb = K / 32;
+    void *ws = nullptr;
+    const size_t codes = (size_t)M * K, scal = (size_t)M * nb * 4;
+    int st = tn::workspace(&ws, codes + 2 * scal + 256, stream, /*slot=*/0);
+    if (st) return st;
+    int8_t *xq = static_cast<int8_t *>(ws);
+    float *xd = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + ((codes + 15) & ~size_t(15)));
+    float *xc = xd + (size_t)M * nb;
+    st = tn::launch_q8_planar(x, x_dtype, x_row_stride, xq, xd, xc, M, nb, K, stream);
+    if (st) return st;
+    const size_t ysz = tn_dtype_size(y_dtype);
+    for (int64_t m0 = 0; m0 < M; m0 += chunk) {
+        const int mc = (int)((M - m0) < chunk ? (M - m0) : chunk);
+        st = tn::launch_q8w_gemv(static_cast<const uint8_t *>(w_blob), xq + m0 * K, xd + m0 * nb, xc + m0 * nb, K,
+                                 bias, static_cast<uint8_t *>(y) + (size_t)m0 * N * ysz, y_dtype, N, mc, N, K, 0,
+                                 stream);
+        if (st) return st;
+    }
+    return TN_OK;
+}
+
 extern "C" int tn_q8_0_quantize_planar(const void *x, int x_dtype, int64_t x_row_stride, int8_t *codes,
                                        int64_t codes_row_stride, float *scales, float *offsets, int64_t rows,
                                        int64_t cols, void *stream) {

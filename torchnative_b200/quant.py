@@ -17,7 +17,10 @@ from . import _native as N
 
 Q4_0_BLOCK_ELEMS = 32
 Q4_0_BLOCK_BYTES = 18
-_FORMATS = {"q4_0": (Q4_0_BLOCK_ELEMS, Q4_0_BLOCK_BYTES)}
+Q8_0_BLOCK_BYTES = 34
+# format -> (elements per block, bytes per block); the formats that have B200
+# kernels (quant.rs format_name spellings)
+_FORMATS = {"q4_0": (Q4_0_BLOCK_ELEMS, Q4_0_BLOCK_BYTES), "q8_0": (Q4_0_BLOCK_ELEMS, Q8_0_BLOCK_BYTES)}
 
 _DTYPE_CODE = {torch.float32: N.TN_F32, torch.bfloat16: N.TN_BF16, torch.float16: N.TN_F16,
                torch.float64: N.TN_F64}
@@ -97,7 +100,10 @@ def _quantize(tensor: torch.Tensor, format: str = "q4_0") -> QTensor:
     cols = last
     rows = src.numel() // cols if cols else 0
     blob = torch.empty(src.numel() // block * _FORMATS[format][1], dtype=torch.uint8, device=src.device)
-    N.check(N.lib().tn_q4_0_quantize(_ptr(src), _ptr(blob), rows, cols, _stream(src.device)))
+    if format == "q8_0":  # BlockQ8_0::from_float (k_quants.rs:676-706), the same writer as for activations
+        N.check(N.lib().tn_q8_0_quantize(_ptr(src), N.TN_F32, cols, _ptr(blob), rows, cols, _stream(src.device)))
+    else:
+        N.check(N.lib().tn_q4_0_quantize(_ptr(src), _ptr(blob), rows, cols, _stream(src.device)))
     return QTensor(blob, tuple(tensor.shape), format)
 
 
@@ -110,7 +116,8 @@ def _dequantize(q: QTensor) -> torch.Tensor:
     out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
     cols = q.shape[-1]
     rows = out.numel() // cols if cols else 0
-    N.check(N.lib().tn_q4_0_dequantize(_ptr(q.blob), _ptr(out), rows, cols, _stream(q.device)))
+    deq = N.lib().tn_q8_0_dequantize if q.format == "q8_0" else N.lib().tn_q4_0_dequantize
+    N.check(deq(_ptr(q.blob), _ptr(out), rows, cols, _stream(q.device)))
     return out
 
 
@@ -188,9 +195,9 @@ def _quantized_linear(input: torch.Tensor, weight: QTensor, bias: torch.Tensor |
     y = torch.empty((m, out_features), dtype=input.dtype, device=input.device)
     if m and out_features:
         code = _DTYPE_CODE[input.dtype]
-        N.check(N.lib().tn_q4_0_linear(_ptr(x), code, x.stride(0) if m > 1 else in_features, _ptr(weight.blob),
-                                       _ptr(bias), _ptr(y), code, m, out_features, in_features, int(act_mode),
-                                       _stream(input.device)))
+        lin = N.lib().tn_q8_0_linear if weight.format == "q8_0" else N.lib().tn_q4_0_linear
+        N.check(lin(_ptr(x), code, x.stride(0) if m > 1 else in_features, _ptr(weight.blob), _ptr(bias), _ptr(y),
+                    code, m, out_features, in_features, int(act_mode), _stream(input.device)))
     return y.reshape(*lead, out_features)
 
 
