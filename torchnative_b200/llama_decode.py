@@ -75,7 +75,10 @@ class Q4LlamaDecoder:
     full from the seed and sliced, so every group size runs the same model)."""
 
     def __init__(self, shape: LlamaShape, batch: int, capacity: int, device, seed: int = 0,
-                 layers: int | None = None, tp=None, exchange: str = "p2p"):
+                 layers: int | None = None, tp=None, exchange: str = "p2p", weights: dict | None = None):
+        """`weights` (from `from_gguf`): the full model's tensors on `device`
+        -- per layer attn_norm, qkv, o, mlp_norm, gate_up, down as below, plus
+        final_norm, lm_head, embed -- used instead of the seeded random ones."""
         from . import tp as tpm
 
         self.s = shape
@@ -97,8 +100,8 @@ class Q4LlamaDecoder:
         gen.manual_seed(seed)
         bf = torch.bfloat16
         self.layers = []
-        for _ in range(self.n_layers):
-            lw = {
+        for li in range(self.n_layers):
+            lw = dict(weights["layers"][li]) if weights is not None else {
                 "attn_norm": (1.0 + 0.1 * torch.randn(s.hidden, device=dev, generator=gen)).to(bf),
                 "qkv": random_q4_blob(s.qkv, s.hidden, gen, dev),
                 "o": random_q4_blob(s.hidden, s.heads * s.head_dim, gen, dev),
@@ -114,11 +117,17 @@ class Q4LlamaDecoder:
                 lw["gate_up"] = tpm.shard_gate_up_pairs(lw["gate_up"], s.inter, s.hidden, r, G)
                 lw["down"] = tpm.shard_rows(lw["down"], s.hidden, s.inter, r, G)
             self.layers.append(lw)
-        self.final_norm = (1.0 + 0.1 * torch.randn(s.hidden, device=dev, generator=gen)).to(bf)
-        self.lm_head = random_q4_blob(s.vocab, s.hidden, gen, dev)
+        if weights is not None:
+            self.final_norm, self.lm_head = weights["final_norm"], weights["lm_head"]
+        else:
+            self.final_norm = (1.0 + 0.1 * torch.randn(s.hidden, device=dev, generator=gen)).to(bf)
+            self.lm_head = random_q4_blob(s.vocab, s.hidden, gen, dev)
         if G > 1:
             self.lm_head = tpm.shard_rows(self.lm_head, s.vocab, s.hidden, r, G)
-        self.embed = (0.02 * torch.randn((s.vocab, s.hidden), device=dev, generator=gen)).to(bf)
+        if weights is not None:
+            self.embed = weights["embed"]
+        else:
+            self.embed = (0.02 * torch.randn((s.vocab, s.hidden), device=dev, generator=gen)).to(bf)
         self.k_cache = [torch.zeros((batch, self.hkv, capacity, s.head_dim), device=dev, dtype=bf)
                         for _ in range(self.n_layers)]
         self.v_cache = [torch.zeros_like(self.k_cache[0]) for _ in range(self.n_layers)]
@@ -255,6 +264,73 @@ class Q4LlamaDecoder:
         else:
             extra = 1 if (self.tp is not None and self.B > 1) else 0
         return self.kernels_per_layer * self.n_layers + (2 if self.fused else 3) + extra
+
+    @classmethod
+    def from_gguf(cls, path, batch: int, capacity: int, device, layers: int | None = None, tp=None,
+                  exchange: str = "p2p") -> "Q4LlamaDecoder":
+        """A decoder whose weights are a llama GGUF file's own tensors
+        (transformers' GGUF tensor map for llama: blk.N.attn_q / attn_k /
+        attn_v / attn_output / ffn_gate / ffn_up / ffn_down / attn_norm /
+        ffn_norm, token_embd, output_norm, output). Every linear must be Q4_0;
+        its blocks reach HBM byte for byte (torchnative_b200.gguf), q and k with
+        llama.cpp's rotary row order undone by rows, then q/k/v rows are
+        concatenated and gate/up rows interleaved as the fused kernels read
+        them. Norms are held in bf16 (transformers' dtype=bfloat16 load) and the
+        embedding is dequantised to bf16. A missing `output` ties lm_head to
+        token_embd, as transformers does."""
+        from . import gguf as G
+
+        dev = torch.device(device)
+        bf = torch.bfloat16
+        with G.GGUFFile(path) as f:
+            md = f.metadata
+            if md.get("general.architecture") != "llama":
+                raise G.UnsupportedGGUF(f"{f.path}: architecture {md.get('general.architecture')!r}; the decode "
+                                        "engine runs llama")
+
+            def need(key):
+                if key not in md:
+                    raise G.GGUFFormatError(f"{f.path}: metadata {key!r} is missing")
+                return md[key]
+
+            H, I = int(need("llama.embedding_length")), int(need("llama.feed_forward_length"))
+            heads = int(need("llama.attention.head_count"))
+            kv = int(md.get("llama.attention.head_count_kv", heads))
+            n_layers = int(need("llama.block_count"))
+            vocab = f.info("token_embd.weight").shape[0]
+            shape = LlamaShape(H, I, heads, kv, int(md.get("llama.attention.key_length", H // heads)), vocab, n_layers,
+                               float(md.get("llama.rope.freq_base", 10000.0)),
+                               float(md.get("llama.attention.layer_norm_rms_epsilon", 1e-5)))
+
+            def q4(name, heads_perm=None):
+                info = f.info(name)
+                if info.format != "q4_0":
+                    raise G.UnsupportedGGUF(f"{f.path}: {name} is {info.type_name}; the decode engine's linears "
+                                            "are Q4_0")
+                return G.load_tensor(f, name, keep_blocks=True, permute_heads=heads_perm, device=dev).blob
+
+            def dense_bf16(name):
+                t = G.load_tensor(f, name, keep_blocks=False, device=dev)
+                return t.to(bf).contiguous()
+
+            lw_all = []
+            for li in range(n_layers if layers is None else layers):
+                b = f"blk.{li}."
+                gate, up = q4(b + "ffn_gate.weight"), q4(b + "ffn_up.weight")
+                row = len(gate) // I
+                lw_all.append({
+                    "attn_norm": dense_bf16(b + "attn_norm.weight"),
+                    "qkv": torch.cat([q4(b + "attn_q.weight", heads), q4(b + "attn_k.weight", kv),
+                                      q4(b + "attn_v.weight")]),
+                    "o": q4(b + "attn_output.weight"),
+                    "mlp_norm": dense_bf16(b + "ffn_norm.weight"),
+                    "gate_up": torch.stack([gate.view(I, row), up.view(I, row)], dim=1).reshape(-1).contiguous(),
+                    "down": q4(b + "ffn_down.weight"),
+                })
+            lm = "output.weight" if "output.weight" in f.tensors else "token_embd.weight"
+            weights = {"layers": lw_all, "final_norm": dense_bf16("output_norm.weight"), "lm_head": q4(lm),
+                       "embed": dense_bf16("token_embd.weight")}
+        return cls(shape, batch, capacity, dev, layers=layers, tp=tp, exchange=exchange, weights=weights)
 
     def fill_prompt_cache(self, length: int, seed: int = 1) -> None:
         """The prompt's K/V: synthetic N(0,1) values in slots [0, length), and
