@@ -1,4 +1,4 @@
-"""The Q4_0 operator family on a B200, mirroring torchnative's `torch._C`
+"""The Q4_0 and Q8_0 operator family on a B200, mirroring torchnative's `torch._C`
 quant entry points (torchnative/rust/torch_c/src/quant.rs) and its
 `QuantizedLinear` module (torchnative/python/torchnative/quant/__init__.py).
 
