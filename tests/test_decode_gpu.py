@@ -350,3 +350,37 @@ def test_gemv_planar_q8_output_refuses_what_it_cannot_quantise(N, cuda_device):
     assert "bf16" in N.last_error()
     assert call(N.TN_BF16, 48, 0) == N.TN_ERR_SHAPE
     assert call(N.TN_BF16, 32, N.TN_EPILOGUE_SILU_MUL_PAIRS) == N.TN_ERR_SHAPE  # 16 columns of act
+
+
+@pytest.mark.parametrize("with_delta", [True, False])
+def test_fused_rmsnorm_prologue_equals_the_separate_kernels(N, cuda_device, with_delta):
+    """The q/k/v and gate/up GEMVs' fused RMSNorm + Q8_0 prologue (packed bf16
+    arithmetic) against tn_llama_add_rmsnorm_q8 + the planar GEMV (float
+    arithmetic), bit for bit. Activations are multiples of 0.5, so the sum of
+    squares is exact in any reduction order and both sides see the same
+    rsqrt; every other rounding must then agree."""
+    dev, K, Nout, eps = cuda_device, 4096, 512, 1e-5
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = (torch.randint(-4, 5, (1, K), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    d = (torch.randint(-2, 3, (1, K), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(K, generator=g, device=dev)).to(torch.bfloat16)
+    blob = torch.frombuffer(bytearray(q4_exact.random_q4_0_blob(np.random.default_rng(6), Nout, K)),
+                            dtype=torch.uint8).to(dev)
+    delta = P(d.data_ptr()) if with_delta else None
+    h1, h2 = torch.zeros_like(x), torch.zeros_like(x)
+    y1 = torch.full((1, Nout), float("nan"), device=dev, dtype=torch.bfloat16)
+    y2 = torch.full_like(y1, float("nan"))
+    N.check(N.lib().tn_q4_0_linear_fused(N.TN_X_RMSNORM, P(x.data_ptr()), K, delta, P(h1.data_ptr()),
+                                         P(w.data_ptr()), eps, P(blob.data_ptr()), None, P(y1.data_ptr()), N.TN_BF16,
+                                         1, Nout, K, N.TN_WEIGHTS_STATIC, _stream()))
+    codes = torch.empty((1, K), dtype=torch.int8, device=dev)
+    sc, of = torch.empty((1, K // 32), device=dev), torch.empty((1, K // 32), device=dev)
+    N.check(N.lib().tn_llama_add_rmsnorm_q8(P(x.data_ptr()), delta, P(h2.data_ptr()), P(w.data_ptr()), eps, 1, K,
+                                            P(codes.data_ptr()), P(sc.data_ptr()), P(of.data_ptr()), _stream()))
+    N.check(N.lib().tn_q4_0_linear_q8(P(codes.data_ptr()), K, P(sc.data_ptr()), P(of.data_ptr()),
+                                      P(blob.data_ptr()), None, P(y2.data_ptr()), N.TN_BF16, 1, Nout, K,
+                                      N.TN_WEIGHTS_STATIC, _stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(h1, h2) and torch.equal(h1, x + d if with_delta else x)
+    assert torch.equal(y1, y2)
+    N.device_status(reset=True)

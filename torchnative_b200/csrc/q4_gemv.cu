@@ -347,6 +347,49 @@ __device__ __forceinline__ void load8_bf16(const __nv_bfloat16 *src, float *v) {
     }
 }
 
+// Packed bf16 pairs (element 2i in the low half of word i, 2i+1 in the high).
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
+__device__ __forceinline__ __nv_bfloat162 bf2_of(uint32_t u) { return *reinterpret_cast<__nv_bfloat162 *>(&u); }
+__device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+// q8_half_block_to_smem for 16 values that are bf16 already (as 8 packed
+// pairs): the same codes, scale and offset, with the block maximum taken on
+// the packed magnitudes (exact), the codes packed by byte permutes and their
+// sum by one dp4a per word.
+__device__ __forceinline__ void q8_half_block_bf16_to_smem(const uint32_t (&v)[8], int m, int b, int half,
+                                                           const Smem &s, const GemvParams &p, int lane) {
+    const unsigned pm = 3u << (lane & ~1);
+    __nv_bfloat162 mx = bf2_of(v[0] & 0x7fff7fffu);
+#pragma unroll
+    for (int i = 1; i < 8; ++i) mx = __hmax2(mx, bf2_of(v[i] & 0x7fff7fffu));
+    const uint32_t mb = bf2_bits(mx);
+    float amax = fmaxf(bf_lo(mb), bf_hi(mb));
+    amax = fmaxf(amax, __shfl_xor_sync(pm, amax, 1));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[4];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int q0 = sat_i8r(roundf(__fmul_rn(bf_lo(v[2 * k]), id)));
+        const int q1 = sat_i8r(roundf(__fmul_rn(bf_hi(v[2 * k]), id)));
+        const int q2 = sat_i8r(roundf(__fmul_rn(bf_lo(v[2 * k + 1]), id)));
+        const int q3 = sat_i8r(roundf(__fmul_rn(bf_hi(v[2 * k + 1]), id)));
+        w[k] = __byte_perm(__byte_perm((uint32_t)q0, (uint32_t)q1, 0x0040), __byte_perm((uint32_t)q2, (uint32_t)q3, 0x0040),
+                           0x5410);
+        sum = __dp4a((int)w[k], 0x01010101, sum);
+    }
+    sum += __shfl_xor_sync(pm, sum, 1);
+    const int pair = b >> 1, c = (b & 1) * 2 + half;
+    const uint32_t row = s.xs + (uint32_t)m * p.nbp * 32;
+    sts128(row + xchunk(pair, c), make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]));
+    if (half == 0) {
+        stsf(s.xds + (uint32_t)(m * p.nbp + b) * 4, __half2float(__float2half_rn(d)));
+        stsf(s.xcs + (uint32_t)(m * p.nbp + b) * 4, 12582912.0f + 8.0f * (float)sum);
+    }
+}
+
 enum : int { X_PLANAR = 0, X_BF16 = 1, X_NORM = 2, X_SILU = 3 };
 constexpr int kMaxFusedRows = 4;
 
@@ -365,8 +408,11 @@ __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p
         // values stay in registers across the CTA-wide reduction, so the
         // prologue costs one L2 round trip.
         const int b = tid >> 1, hf = tid & 1, e0 = b * 32 + 16 * hf;
-        float h[16];
-        uint32_t wp[8];
+        // h = bf16(x + delta) as packed pairs: a correctly rounded bf16 sum is
+        // the f32 sum rounded to bf16 (the exact sum of two bf16 values either
+        // fits in f32 or differs from the larger by less than a quarter bf16
+        // ulp), so __hadd2 gives transformers' bits
+        uint32_t hb[8], wp[8];
         float ss = 0.0f;
         if (b < p.nb) {
             int4 xr[2], dr[2], wr[2];
@@ -380,23 +426,19 @@ __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p
             for (int c = 0; c < 2; ++c) {
                 const uint32_t xu[4] = {(uint32_t)xr[c].x, (uint32_t)xr[c].y, (uint32_t)xr[c].z, (uint32_t)xr[c].w};
                 const uint32_t du[4] = {(uint32_t)dr[c].x, (uint32_t)dr[c].y, (uint32_t)dr[c].z, (uint32_t)dr[c].w};
-                wp[4 * c + 0] = (uint32_t)wr[c].x;
-                wp[4 * c + 1] = (uint32_t)wr[c].y;
-                wp[4 * c + 2] = (uint32_t)wr[c].z;
-                wp[4 * c + 3] = (uint32_t)wr[c].w;
+                const uint32_t wu[4] = {(uint32_t)wr[c].x, (uint32_t)wr[c].y, (uint32_t)wr[c].z, (uint32_t)wr[c].w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    float lo = __uint_as_float(xu[i] << 16), hi = __uint_as_float(xu[i] & 0xffff0000u);
-                    if (p.xdelta) {
-                        lo = bfr(lo + __uint_as_float(du[i] << 16));
-                        hi = bfr(hi + __uint_as_float(du[i] & 0xffff0000u));
-                    }
-                    h[8 * c + 2 * i] = lo;
-                    h[8 * c + 2 * i + 1] = hi;
+                    hb[4 * c + i] = p.xdelta ? bf2_bits(__hadd2(bf2_of(xu[i]), bf2_of(du[i]))) : xu[i];
+                    wp[4 * c + i] = wu[i];
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) ss = fmaf(h[j], h[j], ss);
+            for (int i = 0; i < 8; ++i) {
+                const float lo = bf_lo(hb[i]), hi = bf_hi(hb[i]);
+                ss = fmaf(lo, lo, ss);
+                ss = fmaf(hi, hi, ss);
+            }
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
@@ -408,26 +450,27 @@ __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p
         const float r = rsqrtf(t / (float)K + p.eps);
         if (b < p.nb) {
             if (p.xh_out && blockIdx.x == 0) {
-                uint32_t o[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    o[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(h[2 * i])) |
-                           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(h[2 * i + 1])) << 16);
                 int4 *dst = reinterpret_cast<int4 *>(p.xh_out + e0);
 #pragma unroll
                 for (int c = 0; c < 2; ++c)
-                    dst[c] = make_int4((int)o[4 * c], (int)o[4 * c + 1], (int)o[4 * c + 2], (int)o[4 * c + 3]);
+                    dst[c] = make_int4((int)hb[4 * c], (int)hb[4 * c + 1], (int)hb[4 * c + 2], (int)hb[4 * c + 3]);
             }
+            // w * bf16(h * r): the f32 products rounded to bf16 in one packed
+            // convert, then one correctly rounded bf16 product per pair (a
+            // product of two bf16 values is exact in f32, so it equals
+            // bf16(f32 product))
+            uint32_t v[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                h[2 * i] = bfr(__uint_as_float(wp[i] << 16) * bfr(h[2 * i] * r));
-                h[2 * i + 1] = bfr(__uint_as_float(wp[i] & 0xffff0000u) * bfr(h[2 * i + 1] * r));
+                const __nv_bfloat162 hr = __floats2bfloat162_rn(bf_lo(hb[i]) * r, bf_hi(hb[i]) * r);
+                v[i] = bf2_bits(__hmul2(bf2_of(wp[i]), hr));
             }
-            q8_half_block_to_smem(h, 0, b, hf, s, p, lane);
+            q8_half_block_bf16_to_smem(v, 0, b, hf, s, p, lane);
         } else if (b < p.nbp) {
+            float z[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) h[j] = 0.0f;
-            q8_half_block_to_smem(h, 0, b, hf, s, p, lane);
+            for (int j = 0; j < 16; ++j) z[j] = 0.0f;
+            q8_half_block_to_smem(z, 0, b, hf, s, p, lane);
         }
         return;
     }
