@@ -61,6 +61,13 @@ def lib():
         L.tno_q8_0_q8_0_dot.restype = ctypes.c_float
         L.tno_q8_0_linear.argtypes = [p, p, p, f32p, i64, i64, i64, ctypes.c_int]
         L.tno_q8_0_linear.restype = None
+        for name in ("tno_q4_k_dequantize", "tno_q8_k_quantize"):
+            getattr(L, name).argtypes = [p, p, i64]
+            getattr(L, name).restype = None
+        L.tno_q4_k_q8_k_dot.argtypes = [p, p, i64]
+        L.tno_q4_k_q8_k_dot.restype = ctypes.c_float
+        L.tno_q4_k_linear.argtypes = [p, p, p, f32p, i64, i64, i64, ctypes.c_int]
+        L.tno_q4_k_linear.restype = None
         L.tno_sdpa.argtypes = [p, p, p, p, ctypes.c_int, p, p, p, ctypes.c_int, i64, i64, i64, i64,
                                i64, i64, p, p, p, ctypes.c_int, ctypes.c_double, ctypes.c_int]
         L.tno_sdpa.restype = None
@@ -137,6 +144,44 @@ def q8_0_linear(x: np.ndarray, w_blob: bytes | np.ndarray, n_out: int, bias: np.
     y = np.empty((m, n_out), dtype=np.float32)
     b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
     lib().tno_q8_0_linear(_ptr(x), _ptr(w), _ptr(b), _ptr(y), m, n_out, k, int(threads))
+    return y.reshape(*lead, n_out)
+
+
+Q4_K_BLOCK_BYTES = 144
+Q8_K_BLOCK_BYTES = 292
+
+
+def q4_k_dequantize(blob: bytes, n: int) -> np.ndarray:
+    """BlockQ4K::to_float (k_quants.rs:1722-1748): n elements (a multiple of 256)."""
+    b = np.frombuffer(blob, dtype=np.uint8)
+    assert b.size == n // 256 * Q4_K_BLOCK_BYTES
+    y = np.empty(n, dtype=np.float32)
+    lib().tno_q4_k_dequantize(_ptr(np.ascontiguousarray(b)), _ptr(y), n)
+    return y
+
+
+def q8_k_quantize(x: np.ndarray) -> bytes:
+    """BlockQ8K::from_float (k_quants.rs:2376-2410): rows of x -> 292-byte blocks."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    assert x.size % 256 == 0
+    out = np.empty(x.size // 256 * Q8_K_BLOCK_BYTES, dtype=np.uint8)
+    lib().tno_q8_k_quantize(_ptr(x), _ptr(out), x.size)
+    return out.tobytes()
+
+
+def q4_k_linear(x: np.ndarray, w_blob: bytes | np.ndarray, n_out: int, bias: np.ndarray | None = None,
+                threads: int = 1) -> np.ndarray:
+    """torch._C._quantized_linear for a Q4_K weight on the CPU (quant.rs:286-369 ->
+    k_quants.rs:2430-2580 with BlockQ4K::vec_dot_unopt, :1478-1544)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    lead, k = x.shape[:-1], x.shape[-1]
+    m = int(np.prod(lead)) if lead else 1
+    w = np.frombuffer(w_blob, dtype=np.uint8) if isinstance(w_blob, (bytes, bytearray)) else w_blob
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    assert w.size == n_out * (k // 256) * Q4_K_BLOCK_BYTES
+    y = np.empty((m, n_out), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    lib().tno_q4_k_linear(_ptr(x), _ptr(w), _ptr(b), _ptr(y), m, n_out, k, int(threads))
     return y.reshape(*lead, n_out)
 
 

@@ -218,6 +218,139 @@ float tno_q8_0_q8_0_dot(const uint8_t *w, const uint8_t *xq, int64_t nblocks) {
     return sumf;
 }
 
+/* ---- Q4_K weights with Q8_K activations ----------------------------------
+ * BlockQ4K (vendor/candle-core/src/quantized/k_quants.rs:153-159): 144 bytes
+ * per 256 elements -- f16 d, f16 dmin, 12 bytes of 6-bit sub-block scales and
+ * mins, 128 bytes of nibbles (qs[32c..32c+32] holds sub-block 2c in the low
+ * nibbles and 2c+1 in the high ones). BlockQ8K (:185-190): f32 d, 256 int8
+ * codes, 16 int16 sums of 16 codes: 292 bytes. */
+
+static void q4k_scale_min(int j, const uint8_t *q, int *sc, int *m) {
+    /* get_scale_min_k4, quantized/utils.rs:50-60 */
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+void tno_q4_k_dequantize(const uint8_t *blob, float *y, int64_t n) {
+    /* BlockQ4K::to_float, k_quants.rs:1722-1748: y = d*sc * q - dmin*m, each
+     * product rounded to f32, then the subtraction */
+    for (int64_t b = 0; b < n / 256; ++b) {
+        const uint8_t *blk = blob + b * 144;
+        const float d = tno_f16_to_f32(get_u16(blk)), mn = tno_f16_to_f32(get_u16(blk + 2));
+        const uint8_t *sc = blk + 4, *qs = blk + 16;
+        float *o = y + b * 256;
+        for (int c = 0; c < 4; ++c) {
+            int s0, m0, s1, m1;
+            q4k_scale_min(2 * c, sc, &s0, &m0);
+            q4k_scale_min(2 * c + 1, sc, &s1, &m1);
+            const float d1 = d * (float)s0, mm1 = mn * (float)m0, d2 = d * (float)s1, mm2 = mn * (float)m1;
+            for (int l = 0; l < 32; ++l) o[64 * c + l] = d1 * (float)(qs[32 * c + l] & 0xF) - mm1;
+            for (int l = 0; l < 32; ++l) o[64 * c + 32 + l] = d2 * (float)(qs[32 * c + l] >> 4) - mm2;
+        }
+    }
+}
+
+static float round_half_away(float v) { return roundf(v); }
+
+void tno_q8_k_quantize(const float *x, uint8_t *blob, int64_t n) {
+    /* BlockQ8K::from_float, k_quants.rs:2376-2410: the signed value of largest
+     * magnitude (first one), iscale = -127/max, q = clamp(round(iscale*x)),
+     * bsums of 16, d = 1/iscale; an all-zero block is d = 0, codes 0 */
+    for (int64_t b = 0; b < n / 256; ++b) {
+        const float *xs = x + b * 256;
+        uint8_t *blk = blob + b * 292;
+        float mx = 0.0f, amax = 0.0f;
+        for (int j = 0; j < 256; ++j)
+            if (amax < fabsf(xs[j])) {
+                amax = fabsf(xs[j]);
+                mx = xs[j];
+            }
+        int8_t q[256];
+        int16_t bs[16];
+        float d = 0.0f;
+        memset(q, 0, sizeof q);
+        memset(bs, 0, sizeof bs);
+        if (amax != 0.0f) {
+            const float iscale = -127.0f / mx;
+            for (int j = 0; j < 256; ++j) {
+                float v = round_half_away(iscale * xs[j]);
+                v = v < -128.0f ? -128.0f : (v > 127.0f ? 127.0f : v);
+                q[j] = (int8_t)v;
+            }
+            for (int j = 0; j < 16; ++j) {
+                int s = 0;
+                for (int i = 0; i < 16; ++i) s += q[16 * j + i];
+                bs[j] = (int16_t)s;
+            }
+            d = 1.0f / iscale;
+        }
+        memcpy(blk, &d, 4);
+        memcpy(blk + 4, q, 256);
+        memcpy(blk + 260, bs, 32);
+    }
+}
+
+float tno_q4_k_q8_k_dot(const uint8_t *w, const uint8_t *xq, int64_t nsb) {
+    /* BlockQ4K::vec_dot_unopt, k_quants.rs:1478-1544, in its order: per
+     * super-block eight i32 lanes aux[l] += sc * (q8 * q4) over the elements
+     * l mod 8, sums[l] += (d_w*d_x) * aux[l], sumf -= (dmin_w*d_x) * sum(bsums *
+     * mins); the result is sumf + (sums[0] + ... + sums[7]). */
+    float sumf = 0.0f, sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t b = 0; b < nsb; ++b) {
+        const uint8_t *wb = w + b * 144, *xb = xq + b * 292;
+        const uint8_t *qs = wb + 16;
+        int8_t a[256];
+        for (int c = 0; c < 4; ++c)
+            for (int l = 0; l < 32; ++l) {
+                a[64 * c + l] = (int8_t)(qs[32 * c + l] & 0xF);
+                a[64 * c + 32 + l] = (int8_t)(qs[32 * c + l] >> 4);
+            }
+        int sc[8], mn[8];
+        for (int j = 0; j < 8; ++j) q4k_scale_min(j, wb + 4, &sc[j], &mn[j]);
+        int16_t bs[16];
+        memcpy(bs, xb + 260, 32);
+        int32_t sumi = 0;
+        for (int j = 0; j < 16; ++j) sumi += (int32_t)bs[j] * mn[j / 2];
+        int32_t aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        const int8_t *q8 = (const int8_t *)(xb + 4);
+        for (int s = 0; s < 8; ++s)
+            for (int g = 0; g < 4; ++g)
+                for (int l = 0; l < 8; ++l) {
+                    const int e = 32 * s + 8 * g + l;
+                    aux[l] += sc[s] * (int32_t)(int16_t)(q8[e] * a[e]);
+                }
+        float dx;
+        memcpy(&dx, xb, 4);
+        const float d = tno_f16_to_f32(get_u16(wb)) * dx;
+        for (int l = 0; l < 8; ++l) sums[l] += d * (float)aux[l];
+        const float dmin = tno_f16_to_f32(get_u16(wb + 2)) * dx;
+        sumf -= dmin * (float)sumi;
+    }
+    float t = 0.0f;
+    for (int l = 0; l < 8; ++l) t += sums[l];
+    return sumf + t;
+}
+
+void tno_q4_k_linear(const float *x, const uint8_t *w_blob, const float *bias, float *y,
+                     int64_t M, int64_t N, int64_t K, int threads) {
+    /* the same matmul steps (k_quants.rs:2430-2580) with Q8_K activations */
+    const int64_t nsb = K / 256;
+    uint8_t *xq = (uint8_t *)malloc((size_t)(M * nsb * 292 + 1));
+    for (int64_t r = 0; r < M; ++r) tno_q8_k_quantize(x + r * K, xq + r * nsb * 292, K);
+    (void)threads;
+    for (int64_t r = 0; r < M; ++r)
+        for (int64_t c = 0; c < N; ++c) y[r * N + c] = tno_q4_k_q8_k_dot(w_blob + c * nsb * 144, xq + r * nsb * 292, nsb);
+    free(xq);
+    if (bias)
+        for (int64_t r = 0; r < M; ++r)
+            for (int64_t c = 0; c < N; ++c) y[r * N + c] = y[r * N + c] + bias[c];
+}
+
 /* ---- the matmul: quads of output columns split across workers ----------- */
 
 typedef float (*dot_fn)(const uint8_t *, const uint8_t *, int64_t);

@@ -66,6 +66,20 @@ void tno_q4_0_linear(const float *x, const uint8_t *w_blob, const float *bias, f
  * order). */
 float tno_q8_0_q8_0_dot(const uint8_t *w_row, const uint8_t *xq_row, int64_t nblocks);
 
+/* Q4_K reader: BlockQ4K::to_float, k_quants.rs:1722-1748 (144-byte
+ * super-blocks of 256, 6-bit scales/mins by get_scale_min_k4, utils.rs:50-60). */
+void tno_q4_k_dequantize(const uint8_t *blob, float *y, int64_t n);
+/* Q8_K activation writer: BlockQ8K::from_float, k_quants.rs:2376-2410
+ * (292-byte blocks: f32 d, 256 int8 codes, 16 int16 sums of 16). */
+void tno_q8_k_quantize(const float *x, uint8_t *blob, int64_t n);
+/* One output element for a Q4_K weight: BlockQ4K::vec_dot_unopt,
+ * k_quants.rs:1478-1544. */
+float tno_q4_k_q8_k_dot(const uint8_t *w_row, const uint8_t *xq_row, int64_t nsuper);
+/* torch._C._quantized_linear for a Q4_K weight (N rows of K/256 super-blocks),
+ * activations quantised to Q8_K row by row. */
+void tno_q4_k_linear(const float *x, const uint8_t *w_blob, const float *bias, float *y,
+                     int64_t M, int64_t N, int64_t K, int threads);
+
 /* torch._C._quantized_linear for a Q8_0 weight (N rows of 34-byte blocks):
  * the same steps as tno_q4_0_linear with tno_q8_0_q8_0_dot per element. */
 void tno_q8_0_linear(const float *x, const uint8_t *w_blob, const float *bias, float *y,

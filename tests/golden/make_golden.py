@@ -8,9 +8,10 @@ Writes two files:
   ``scripts/q4quality/golden_gguf_py.json``: llama.cpp gguf-py's own bytes and
   dequantised bits for ten hand-built blocks (gauss, pos/neg extreme, zero,
   opposite signs, an f16-subnormal scale, two rows; Q8_0 gauss and exact .5
-  ties). Copied value for value with its provenance, so the tests can pin the
-  oracle's codec to them on a machine without the reference tree. The Q4_K
-  case is dropped (not on this path).
+  ties) and its Q4_K case (three super-blocks written by llama.cpp, with
+  gguf-py's dequantised bits). Copied value for value with its provenance, so
+  the tests can pin the oracle's codec to them on a machine without the
+  reference tree.
 
 * ``sdpa_golden.json`` -- the reference's golden SDPA cases for
   ``aten._scaled_dot_product_flash_attention_for_cpu`` (tests/golden/cases.py
@@ -50,9 +51,9 @@ def q4_fixture(reference: str) -> dict:
     src = os.path.join(reference, "scripts", "q4quality", "golden_gguf_py.json")
     with open(src) as fh:
         doc = json.load(fh)
-    cases = [c for c in doc["cases"] if c["format"] in ("q4_0", "q8_0")]
+    cases = [c for c in doc["cases"] if c["format"] in ("q4_0", "q8_0", "q4_k")]
     return {
-        "what": "llama.cpp gguf-py bytes/bits for Q4_0 and Q8_0 blocks, copied from the reference's "
+        "what": "llama.cpp gguf-py bytes/bits for Q4_0, Q8_0 and Q4_K blocks, copied from the reference's "
         "scripts/q4quality/golden_gguf_py.json",
         "provenance": doc["provenance"],
         "cases": cases,
@@ -139,10 +140,13 @@ def run_upstream(case: dict) -> dict:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=None, help="root of the torchnative checkout")
+    ap.add_argument("--q4-only", action="store_true", help="write only q4_gguf_golden.json")
     args = ap.parse_args()
     if args.reference:
         with open(os.path.join(HERE, "q4_gguf_golden.json"), "w") as fh:
             json.dump(q4_fixture(args.reference), fh, indent=1)
+    if args.q4_only:
+        return
     cases = sdpa_cases()
     for c in cases:
         c.update(run_upstream(c))

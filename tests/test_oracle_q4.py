@@ -52,7 +52,7 @@ def test_golden_file_still_exercises_its_edges():
     assert raw & 0x7C00 == 0 and raw & 0x3FF != 0
     ties = _f32(cases[("q8_0", "ties")]["input_f32"])
     assert np.max(np.abs(ties)) == 127.0 and 2.5 in ties and -126.5 in ties
-    assert len(doc["cases"]) == 9
+    assert len(doc["cases"]) == 10
 
 
 @pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
@@ -180,3 +180,80 @@ def test_q8_0_weight_linear_is_the_row_dot_and_lossless_operands_are_exact():
             one = oracle.lib().tno_q8_0_q8_0_dot(np.frombuffer(blob, np.uint8)[c * nb * 34:].ctypes.data,
                                                  np.frombuffer(xq, np.uint8)[r * nb * 34:].ctypes.data, nb)
             assert np.float32(one) == y[r, c]
+
+
+# ---- Q4_K weights with Q8_K activations (k_quants.rs:153-190, 1478-1544) ----
+
+
+def test_q4_k_reader_bits_equal_llama_cpp():
+    cases = [c for c in _golden()["cases"] if c["format"] == "q4_k"]
+    assert len(cases) == 1 and cases[0]["name"] == "foreign"
+    c = cases[0]
+    n = int(np.prod(c["shape"]))
+    assert oracle.q4_k_dequantize(bytes.fromhex(c["blob"]), n).tobytes() == bytes.fromhex(c["dequant_f32"])
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_q4_k_reader_equals_installed_gguf_py(seed):
+    gguf = pytest.importorskip("gguf")
+    from gguf import quants
+
+    rng = np.random.default_rng(seed + 60)
+    blob = q4_exact.q4_k_blob(rng, 3, 512)
+    want = quants.dequantize(np.frombuffer(blob, np.uint8).reshape(3, -1), gguf.GGMLQuantizationType.Q4_K)
+    assert oracle.q4_k_dequantize(blob, 3 * 512).tobytes() == want.astype(np.float32).tobytes()
+
+
+def test_q8_k_activation_writer_follows_its_rules():
+    rng = np.random.default_rng(61)
+    x = (rng.standard_normal((2, 512)) * 3).astype(np.float32)
+    x[0, 300] = -20.0  # negative signed maximum of the second super-block of row 0 (-> code -127)
+    x[1, :256] = 0.0   # an all-zero super-block
+    raw = np.frombuffer(oracle.q8_k_quantize(x), np.uint8).reshape(2, 2, 292)
+    d = raw[:, :, 0:4].copy().view(np.float32)[..., 0]
+    q = raw[:, :, 4:260].copy().view(np.int8).astype(np.int64)
+    bs = raw[:, :, 260:].copy().view(np.int16).astype(np.int64)
+    assert d[1, 0] == 0.0 and not q[1, 0].any() and not bs[1, 0].any()
+    assert q[0, 1, 300 - 256] == -127 and np.float32(d[0, 1]) == np.float32(1.0) / (np.float32(-127.0) / np.float32(-20.0))
+    assert (bs == q.reshape(2, 2, 16, 16).sum(axis=3)).all()
+    for r in range(2):
+        for b in range(2):
+            if d[r, b] == 0:
+                continue
+            xb = x[r, 256 * b:256 * (b + 1)]
+            mx = xb[np.argmax(np.abs(xb))]
+            iscale = np.float32(-127.0) / np.float32(mx)
+            v = (iscale * xb).astype(np.float32)
+            want = np.clip(np.where(v >= 0, np.floor(v + 0.5), np.ceil(v - 0.5)), -128, 127)
+            assert (q[r, b] == want).all()
+
+
+@pytest.mark.parametrize("rows,out_f,in_f,seed", [(1, 8, 256, 62), (3, 12, 1024, 63), (2, 37, 4096, 64)])
+def test_q4_k_linear_within_counted_bound_of_exact_value(rows, out_f, in_f, seed):
+    rng = np.random.default_rng(seed)
+    blob = q4_exact.q4_k_blob(rng, out_f, in_f)
+    x = (rng.standard_normal((rows, in_f)) * 1.3).astype(np.float32)
+    got = oracle.q4_k_linear(x, blob, out_f)
+    xq = oracle.q8_k_quantize(x)
+    exact, abs_sum, ref_err = q4_exact.exact_linear_q4_k(xq, blob, rows, out_f, in_f)
+    bound = q4_exact.linear_bound_q4_k(in_f, abs_sum, ref_err)
+    assert float(np.max(np.abs(got - exact) / bound)) <= 1.0
+    wdq = oracle.q4_k_dequantize(blob, out_f * in_f).astype(np.float64).reshape(out_f, in_f)
+    assert float(np.max(np.abs(x.astype(np.float64) @ wdq.T - exact) / bound)) > 1.0
+    # one element is one row dot
+    xb = np.frombuffer(xq, np.uint8)
+    one = oracle.lib().tno_q4_k_q8_k_dot(np.frombuffer(blob, np.uint8)[(out_f - 1) * (in_f // 256) * 144:].ctypes.data,
+                                        xb[(rows - 1) * (in_f // 256) * 292:].ctypes.data, in_f // 256)
+    assert np.float32(one) == got[rows - 1, out_f - 1]
+
+
+def test_q4_k_lossless_operands_give_the_exact_integer_matmul():
+    rng = np.random.default_rng(65)
+    M, N, K = 3, 10, 512
+    blob = q4_exact.q4_k_blob(rng, N, K, lossless=True)
+    codes = oracle.q4_k_dequantize(blob, N * K).reshape(N, K).astype(np.float64)  # the nibbles themselves
+    assert codes.min() >= 0 and codes.max() <= 15 and (codes == np.round(codes)).all()
+    x = rng.integers(-127, 128, size=(M, K)).astype(np.float32)
+    x[:, ::256] = 127.0  # every super-block's signed maximum is +127 -> d = -1, codes = -x
+    y = oracle.q4_k_linear(x, blob, N)
+    assert (y.astype(np.float64) == x.astype(np.float64) @ codes.T).all()
