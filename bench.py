@@ -58,8 +58,9 @@ def parse():
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
     ap.add_argument("--rows", type=int, default=1, help="activation rows M for --case gemv")
     ap.add_argument("--shape", default=None, help="one N,K for --case gemv (default: BASELINE's four shapes)")
-    ap.add_argument("--format", default="q4_0", choices=["q4_0", "q8_0"],
-                    help="weight format for --case gemv (q8_0 times tn_q8_0_linear: quantiser + GEMV)")
+    ap.add_argument("--format", default="q4_0", choices=["q4_0", "q8_0", "q4_k"],
+                    help="weight format for --case gemv (q8_0 / q4_k time tn_q8_0_linear / tn_q4_k_linear: "
+                         "activation quantiser + GEMV)")
     ap.add_argument("--batch", type=int, default=1, help="sequences decoded together (BASELINE: 1 and 16)")
     ap.add_argument("--seqs", default="512,4096,16384", help="sequence lengths for --case sdpa_prefill")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
@@ -139,6 +140,18 @@ def random_q8_blob(n: int, k: int, gen, dev):
     blob = torch.randint(0, 256, (nb * 34,), device=dev, dtype=torch.uint8, generator=gen)
     d = (torch.randn(nb, device=dev, generator=gen).abs() * 0.001).to(torch.float16)
     blob.view(nb, 34)[:, 0:2] = d.view(torch.uint8).view(nb, 2)
+    return blob
+
+
+def random_q4k_blob(n: int, k: int, gen, dev):
+    """A synthetic Q4_K weight on the device: random scale/min and nibble
+    bytes, d and dmin f16(|N(0,1)| * 0.001), in BlockQ4K's 144-byte layout."""
+    import torch
+
+    nb = n * (k // 256)
+    blob = torch.randint(0, 256, (nb * 144,), device=dev, dtype=torch.uint8, generator=gen)
+    d = (torch.randn(nb, 2, device=dev, generator=gen).abs() * 0.001).to(torch.float16)
+    blob.view(nb, 144)[:, 0:4] = d.view(torch.uint8).view(nb, 4)
     return blob
 
 
@@ -616,11 +629,12 @@ def run_case_gemv(args):
     shapes = ((14336, 4096), (4096, 14336), (6144, 4096), (28672, 4096))
     if args.shape:
         shapes = (tuple(int(x) for x in args.shape.split(",")),)
-    q8w = args.format == "q8_0"
+    q8w, q4k = args.format == "q8_0", args.format == "q4_k"
     for n, k in shapes:
-        wbytes = n * (k // 32) * 34 if q8w else q4_bytes(n, k)
+        wbytes = n * (k // 32) * 34 if q8w else (n * (k // 256) * 144 if q4k else q4_bytes(n, k))
         copies = max(2, -(-300_000_000 // wbytes))
-        ws = [random_q8_blob(n, k, gen, dev) if q8w else random_q4_blob(n, k, gen, dev) for _ in range(copies)]
+        mk = random_q8_blob if q8w else (random_q4k_blob if q4k else random_q4_blob)
+        ws = [mk(n, k, gen, dev) for _ in range(copies)]
         x = torch.randn((M, k), device=dev, generator=gen).to(torch.bfloat16)
         codes = torch.empty((M, k), device=dev, dtype=torch.int8)
         scales = torch.empty((M, k // 32), device=dev)
@@ -631,9 +645,10 @@ def run_case_gemv(args):
                                           P(scales.data_ptr()), P(offs.data_ptr()), M, k, s()))
 
         def launch(w):
-            if q8w:  # the bf16 activation's quantiser launch, then the Q8_0-weight GEMV
-                N.check(L.tn_q8_0_linear(P(x.data_ptr()), N.TN_BF16, k, P(w.data_ptr()), None, P(y.data_ptr()),
-                                         N.TN_BF16, M, n, k, N.TN_ACT_Q8_0, s()))
+            if q8w or q4k:  # the bf16 activation's quantiser launch, then the GEMV of that weight format
+                fn = L.tn_q8_0_linear if q8w else L.tn_q4_k_linear
+                N.check(fn(P(x.data_ptr()), N.TN_BF16, k, P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, M, n, k,
+                           N.TN_ACT_Q8_0, s()))
                 return
             N.check(L.tn_q4_0_linear_q8(P(codes.data_ptr()), k, P(scales.data_ptr()), P(offs.data_ptr()),
                                         P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, M, n, k,

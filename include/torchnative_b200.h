@@ -163,6 +163,27 @@ TN_API int tn_q8_0_linear(const void *x, int x_dtype, int64_t x_row_stride, cons
                           const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
                           int act_mode, void *stream);
 
+/* Q4_K reader: blob of rows * cols/256 BlockQ4K super-blocks (144 bytes: f16
+ * d, f16 dmin, 12 bytes of 6-bit scales and mins, 128 bytes of nibbles;
+ * vendor/candle-core/src/quantized/k_quants.rs:153-159) -> float32 [rows,
+ * cols], bit-identical to BlockQ4K::to_float (k_quants.rs:1722-1748), behind
+ * torch._C._dequantize of a q4_k weight (quant.rs:180-189); replaces candle's
+ * dequantize_block_q4_K (quantized/cuda.rs:105-160). */
+TN_API int tn_q4_k_dequantize(const void *blob, float *out, int64_t rows, int64_t cols, void *stream);
+
+/* torch._C._quantized_linear for a Q4_K weight (quant.rs:286-369 with format
+ * "q4_k"): the activation rows are quantised to Q8_K (BlockQ8K::from_float,
+ * k_quants.rs:2376-2410: per 256 elements iscale = -127/max, f32 d = 1/iscale)
+ * and every output element is BlockQ4K::vec_dot_unopt's sum (k_quants.rs:
+ * 1478-1544) of d_w*d_x * sum sc*(q4.q8) - dmin_w*d_x * sum m*(code sums), with
+ * exact integer sub-block sums. K % 256 == 0, w_blob 16-byte aligned; every M
+ * on the decode GEMV (chunks of up to 16 rows). Same arguments and refusals as
+ * tn_q4_0_linear. Replaces candle's CUDA arm for GgmlDType::Q4K
+ * (quantized/cuda.rs:846-877). */
+TN_API int tn_q4_k_linear(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob,
+                          const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
+                          int act_mode, void *stream);
+
 /* The same linear split in two, for callers that fuse the activation
  * quantisation into the kernel that produces the activations (an RMSNorm or a
  * SiLU*mul epilogue) -- the reference does the two steps back to back too

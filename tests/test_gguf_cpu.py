@@ -98,14 +98,14 @@ def test_malformed_files_are_refused_by_name(tmp_path):
 def test_refused_and_kernel_less_types(tmp_path):
     data = b"\0" * 1024
     p = _file(tmp_path, gguf_util.raw_gguf(
-        tensors=[("q81", (32, 1), 9, 0), ("q4k", (256, 1), 12, 64), ("odd", (4, 1), 99, 256)], data=data))
+        tensors=[("q81", (32, 1), 9, 0), ("q6k", (256, 1), 14, 64), ("odd", (4, 1), 99, 320)], data=data))
     with G.GGUFFile(p) as f:
         with pytest.raises(G.UnsupportedGGUF, match="Q8_1.*activation"):
             f.raw("q81")
-        assert len(f.raw("q4k")) == 144  # readable bytes, no kernel
-        assert isinstance(G.refusal(12, "q4k"), G.UnsupportedGGUF) and "without a B200 kernel" in str(G.refusal(12))
-        assert G.refusal(2) is None and G.refusal(8) is None and G.refusal(0) is None
+        assert len(f.raw("q6k")) == 210  # readable bytes, no kernel
+        assert isinstance(G.refusal(14, "q6k"), G.UnsupportedGGUF) and "without a B200 kernel" in str(G.refusal(14))
+        assert G.refusal(2) is None and G.refusal(8) is None and G.refusal(12) is None and G.refusal(0) is None
         with pytest.raises(G.UnsupportedGGUF, match="type id 99"):
             f.raw("odd")
         with pytest.raises(G.UnsupportedGGUF, match="without a B200 kernel"):
-            G.load_tensor(f, "q4k")
+            G.load_tensor(f, "q6k")

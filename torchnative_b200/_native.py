@@ -65,6 +65,8 @@ SIGNATURES = {
     "tn_q8_0_quantize": (_I, [_P, _I, _I64, _P, _I64, _I64, _P]),
     "tn_q4_0_linear": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
     "tn_q8_0_linear": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
+    "tn_q4_k_linear": (_I, [_P, _I, _I64, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
+    "tn_q4_k_dequantize": (_I, [_P, _P, _I64, _I64, _P]),
     "tn_q8_0_quantize_planar": (_I, [_P, _I, _I64, _P, _I64, _P, _P, _I64, _I64, _P]),
     "tn_q4_0_linear_q8": (_I, [_P, _I64, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
     "tn_q4_0_linear_fused": (_I, [_I, _P, _I64, _P, _P, _P, ctypes.c_float, _P, _P, _P, _I, _I64, _I64, _I64, _I,

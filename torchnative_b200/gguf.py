@@ -11,7 +11,7 @@ What differs from the reference is where the bytes land: the reference hands
 them to candle's host QTensor (`torch._C._quantized_from_blob`); here they go
 from the memory map through one pinned staging buffer to HBM
 (`cudaMemcpyAsync` by torch), and the block formats that have B200 kernels
-(Q4_0, Q8_0) become a `QTensor` on the device. Other GGML block formats are
+(Q4_0, Q8_0, Q4_K) become a `QTensor` on the device. Other GGML block formats are
 listed and readable as raw bytes but refused by name when asked to become a
 tensor, as are the types the reference refuses.
 
@@ -46,7 +46,7 @@ class UnsupportedGGUF(NotImplementedError):
 
 _ACT_SIDE = ("is a block format llama.cpp uses only for the activation operand inside its dot products, "
              "never as a stored weight")
-_NO_KERNEL = ("is a GGML block format without a B200 kernel in this backend (Q4_0 and Q8_0 have one); its "
+_NO_KERNEL = ("is a GGML block format without a B200 kernel in this backend (Q4_0, Q8_0 and Q4_K have one); its "
               "bytes can be read with GGUFFile.raw, not turned into a tensor")
 _NO_CANDLE = "has no candle GgmlDType in the reference, so neither side has storage or a kernel for it"
 _NOT_WEIGHT = "is a plain numeric type no LLM checkpoint uses for weights; refused rather than guessed at"
@@ -68,7 +68,7 @@ GGML_TYPES = {
     9: ("Q8_1", 32, 36, "refused", _ACT_SIDE),
     10: ("Q2_K", 256, 84, "raw", _NO_KERNEL),
     11: ("Q3_K", 256, 110, "raw", _NO_KERNEL),
-    12: ("Q4_K", 256, 144, "raw", _NO_KERNEL),
+    12: ("Q4_K", 256, 144, "block", "q4_k"),
     13: ("Q5_K", 256, 176, "raw", _NO_KERNEL),
     14: ("Q6_K", 256, 210, "raw", _NO_KERNEL),
     15: ("Q8_K", 256, 292, "refused", _ACT_SIDE),
@@ -381,7 +381,7 @@ def load_tensor(f: GGUFFile, name: str, keep_blocks: bool = False, permute_heads
     """One tensor of `f` on `device` (reference: torchnative.gguf.load_tensor).
 
     F32 / F16 / BF16: a dense tensor of that dtype, bit for bit.
-    Q4_0 / Q8_0: with keep_blocks a QTensor holding the file's blocks
+    Q4_0 / Q8_0 / Q4_K: with keep_blocks a QTensor holding the file's blocks
     unchanged, else their dequantisation as float32 (bit-exact, the reference's
     to_float). Other GGML types are refused by name.
     permute_heads (Llama's .attn_q. / .attn_k.): undo llama.cpp's rotary row

@@ -20,7 +20,10 @@ Q4_0_BLOCK_BYTES = 18
 Q8_0_BLOCK_BYTES = 34
 # format -> (elements per block, bytes per block); the formats that have B200
 # kernels (quant.rs format_name spellings)
-_FORMATS = {"q4_0": (Q4_0_BLOCK_ELEMS, Q4_0_BLOCK_BYTES), "q8_0": (Q4_0_BLOCK_ELEMS, Q8_0_BLOCK_BYTES)}
+_FORMATS = {"q4_0": (Q4_0_BLOCK_ELEMS, Q4_0_BLOCK_BYTES), "q8_0": (Q4_0_BLOCK_ELEMS, Q8_0_BLOCK_BYTES),
+            "q4_k": (256, 144)}
+_LINEAR = {"q4_0": "tn_q4_0_linear", "q8_0": "tn_q8_0_linear", "q4_k": "tn_q4_k_linear"}
+_DEQUANT = {"q4_0": "tn_q4_0_dequantize", "q8_0": "tn_q8_0_dequantize", "q4_k": "tn_q4_k_dequantize"}
 
 _DTYPE_CODE = {torch.float32: N.TN_F32, torch.bfloat16: N.TN_BF16, torch.float16: N.TN_F16,
                torch.float64: N.TN_F64}
@@ -88,6 +91,9 @@ def _quantize(tensor: torch.Tensor, format: str = "q4_0") -> QTensor:
     if format not in _FORMATS:
         raise NotImplementedError(f"{op}: format {format!r} is not implemented on this backend")
     _require_cuda(op, tensor)
+    if format == "q4_k":
+        raise NotImplementedError(f"{op}: the q4_k writer (llama.cpp's weighted make_qkx2_quants search) is not on "
+                                  "this backend; q4_k weights come from GGUF files (torchnative_b200.gguf)")
     if tensor.dim() == 0:
         raise NotImplementedError(f"{op}: a 0-d tensor cannot be quantised")
     block = _FORMATS[format][0]
@@ -116,8 +122,7 @@ def _dequantize(q: QTensor) -> torch.Tensor:
     out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
     cols = q.shape[-1]
     rows = out.numel() // cols if cols else 0
-    deq = N.lib().tn_q8_0_dequantize if q.format == "q8_0" else N.lib().tn_q4_0_dequantize
-    N.check(deq(_ptr(q.blob), _ptr(out), rows, cols, _stream(q.device)))
+    N.check(getattr(N.lib(), _DEQUANT[q.format])(_ptr(q.blob), _ptr(out), rows, cols, _stream(q.device)))
     return out
 
 
@@ -195,7 +200,7 @@ def _quantized_linear(input: torch.Tensor, weight: QTensor, bias: torch.Tensor |
     y = torch.empty((m, out_features), dtype=input.dtype, device=input.device)
     if m and out_features:
         code = _DTYPE_CODE[input.dtype]
-        lin = N.lib().tn_q8_0_linear if weight.format == "q8_0" else N.lib().tn_q4_0_linear
+        lin = getattr(N.lib(), _LINEAR[weight.format])
         N.check(lin(_ptr(x), code, x.stride(0) if m > 1 else in_features, _ptr(weight.blob), _ptr(bias), _ptr(y),
                     code, m, out_features, in_features, int(act_mode), _stream(input.device)))
     return y.reshape(*lead, out_features)
