@@ -80,7 +80,7 @@ struct GemvParams {
     int8_t *oq;
     float *od, *oc;
     int64_t oq_row_stride;
-    int wfmt;  // weight format: 0 = Q4_0 (18-byte blocks), 1 = Q8_0 (34-byte blocks)
+    int wfmt;  // weight format: 0 = Q4_0 (18-byte blocks), 1 = Q8_0 (34-byte blocks), 2 = Q4_K (144 per 256)
 };
 
 // Shared-memory layout (dynamic), as 32-bit shared-window addresses:
@@ -708,6 +708,70 @@ __device__ __forceinline__ void global_rows8(const Smem &s, const GemvParams &p,
     }
 }
 
+// Q4_K weights (BlockQ4K, k_quants.rs:153-159; dot product :1478-1544): a lane
+// takes sub-block pair c (64 elements) of super-block sb at a time -- the
+// super-block's 16-byte header (f16 d, f16 dmin, 6-bit scales/mins) and its
+// 32 nibble bytes -- against the staged Q8_K codes of 32-blocks 8 sb + 2c and
+// + 1 (the same block pair the Q4_0 path reads), whose staged scale is the
+// super-block's d and whose "offset" slot holds the block's code sum. Per
+// pair: acc += (d_w d_x) * (sc0 i0 + sc1 i1) - (dmin_w d_x) * (m0 s0 + m1 s1),
+// both integer sums exact in f32.
+template <int MT, bool TWO>
+__device__ __forceinline__ void staged_rows_k(const Smem &s, const GemvParams &p, uint32_t rowA, uint32_t rowB,
+                                              int lane, float (&acc)[2][MT]) {
+    const int nsp = p.nb >> 1;  // sub-block pairs per row
+    const uint32_t xrow = (uint32_t)p.nbp * 32;
+    for (int sp = lane; sp < nsp; sp += 32) {
+        const int sb = sp >> 2, c = sp & 3;
+        int4 hdr[2], qa[2], qb[2];
+#pragma unroll
+        for (int r = 0; r < (TWO ? 2 : 1); ++r) {
+            const uint32_t base = (r ? rowB : rowA) + (uint32_t)sb * 144u;
+            hdr[r] = lds128(base);
+            qa[r] = lds128(base + 16u + 32u * c);
+            qb[r] = lds128(base + 32u + 32u * c);
+        }
+        const uint32_t c0 = xchunk(sp, 0), c1 = xchunk(sp, 1), c2 = xchunk(sp, 2), c3 = xchunk(sp, 3);
+#pragma unroll
+        for (int r = 0; r < (TWO ? 2 : 1); ++r) {
+            const uint32_t W0 = (uint32_t)hdr[r].y, W1 = (uint32_t)hdr[r].z, W2 = (uint32_t)hdr[r].w;
+            const float dw = half_bits_to_f32((uint32_t)hdr[r].x & 0xffffu), dmw = half_bits_to_f32((uint32_t)hdr[r].x >> 16);
+            // get_scale_min_k4 (quantized/utils.rs:50-60) for sub-blocks j0 = 2c, j1 = 2c + 1
+            const bool hi = c >= 2;
+            const uint32_t scw = hi ? ((W2 & 0x0f0f0f0fu) | (((W0 >> 6) & 0x03030303u) << 4)) : (W0 & 0x3f3f3f3fu);
+            const uint32_t mnw = hi ? (((W2 >> 4) & 0x0f0f0f0fu) | (((W1 >> 6) & 0x03030303u) << 4)) : (W1 & 0x3f3f3f3fu);
+            const int sh = 16 * (c & 1);
+            const int sc0 = (int)((scw >> sh) & 0xffu), sc1 = (int)((scw >> (sh + 8)) & 0xffu);
+            const int m0 = (int)((mnw >> sh) & 0xffu), m1 = (int)((mnw >> (sh + 8)) & 0xffu);
+            const uint32_t q[8] = {(uint32_t)qa[r].x, (uint32_t)qa[r].y, (uint32_t)qa[r].z, (uint32_t)qa[r].w,
+                                   (uint32_t)qb[r].x, (uint32_t)qb[r].y, (uint32_t)qb[r].z, (uint32_t)qb[r].w};
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                if (m < p.M) {
+                    const uint32_t xb = s.xs + m * xrow;
+                    const int4 x0 = lds128(xb + c0), x1 = lds128(xb + c1), x2 = lds128(xb + c2), x3 = lds128(xb + c3);
+                    const uint32_t xl[8] = {(uint32_t)x0.x, (uint32_t)x0.y, (uint32_t)x0.z, (uint32_t)x0.w,
+                                            (uint32_t)x1.x, (uint32_t)x1.y, (uint32_t)x1.z, (uint32_t)x1.w};
+                    const uint32_t xh[8] = {(uint32_t)x2.x, (uint32_t)x2.y, (uint32_t)x2.z, (uint32_t)x2.w,
+                                            (uint32_t)x3.x, (uint32_t)x3.y, (uint32_t)x3.z, (uint32_t)x3.w};
+                    int i0 = 0, i1 = 0;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        i0 = __dp4a((int)(q[i] & 0x0F0F0F0Fu), (int)xl[i], i0);
+                        i1 = __dp4a((int)((q[i] >> 4) & 0x0F0F0F0Fu), (int)xh[i], i1);
+                    }
+                    const uint32_t so = (uint32_t)(m * p.nbp + 2 * sp) * 4;
+                    const float2 xd = lds64f(s.xds + so), xs2 = lds64f(s.xcs + so);
+                    const float S = (float)(sc0 * i0 + sc1 * i1);
+                    const float Mv = fmaf((float)m1, xs2.y, (float)m0 * xs2.x);
+                    acc[r][m] = fmaf(dw * xd.x, S, acc[r][m]);
+                    acc[r][m] = fmaf(-(dmw * xd.x), Mv, acc[r][m]);
+                }
+            }
+        }
+    }
+}
+
 template <int MT, bool TWO>
 __device__ __forceinline__ void staged_rows(const Smem &s, const GemvParams &p, uint32_t rowA, uint32_t rowB,
                                             int lane, float (&acc)[2][MT]) {
@@ -744,7 +808,7 @@ __device__ __forceinline__ void global_rows(const Smem &s, const GemvParams &p, 
     }
 }
 
-// WF: weight format, 0 = Q4_0, 1 = Q8_0.
+// WF: weight format, 0 = Q4_0, 1 = Q8_0, 2 = Q4_K.
 template <int MT, bool STAGED, int XM, int WF>
 __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -853,6 +917,11 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
                     staged_rows8<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
                 else if (has_a)
                     staged_rows8<MT, false>(s, p, ra, ra, lane, acc);
+            } else if constexpr (WF == 2) {
+                if (has_b)
+                    staged_rows_k<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
+                else if (has_a)
+                    staged_rows_k<MT, false>(s, p, ra, ra, lane, acc);
             } else {
                 if (has_b)
                     staged_rows<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
@@ -868,6 +937,8 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
                     global_rows8<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
                 else
                     global_rows8<MT, false>(s, p, ra, ra, lane, acc);
+            } else if constexpr (WF == 2) {
+                // Q4_K launches are always staged (16-byte aligned rows of 144-byte super-blocks)
             } else {
                 if (has_b)
                     global_rows<MT, true>(s, p, ra, ra + p.rowbytes, lane, acc);
@@ -1031,7 +1102,8 @@ Plan plan_slots(int M, int nbp, int rowbytes, bool staged, size_t budget, size_t
 int q4_gemv_max_rows(int64_t K, int wfmt) {
     DeviceFacts f{};
     if (device_facts(&f)) return 0;
-    const int nb = (int)(K / 32), nbp = (nb + 1) & ~1, rowbytes = (wfmt ? 34 : 18) * nb;
+    const int nb = (int)(K / 32), nbp = (nb + 1) & ~1;
+    const int rowbytes = wfmt == 2 ? (int)(K / 256) * 144 : (wfmt ? 34 : 18) * nb;
     const bool staged = (K % 256 == 0);
     for (int mt = 16; mt >= 1; mt >>= 1) {
         if (staged && plan_slots(mt, nbp, rowbytes, true, (size_t)f.smem_optin - 1024, 128 * 1024).ok) return mt;
@@ -1054,7 +1126,7 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
     p.M = M;
     p.nb = (int)(K / 32);
     p.nbp = (p.nb + 1) & ~1;
-    p.rowbytes = (p.wfmt ? 34 : 18) * p.nb;
+    p.rowbytes = p.wfmt == 2 ? (int)(K / 256) * 144 : (p.wfmt ? 34 : 18) * p.nb;
     p.err = device_error_word();
     bool staged = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(p.w) & 15) == 0);
     const int ycols = p.oq ? kYCap : 0;
@@ -1110,6 +1182,19 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
         case X_SILU: TN_GEMV_LAUNCH(MT, X_SILU)                                            \
         default: TN_GEMV_LAUNCH(MT, X_PLANAR)                                              \
         }                                                                                  \
+    }
+    if (p.wfmt == 2) {  // Q4_K weights: planar Q8_K activations, staged rows only
+        if (p.x_mode != X_PLANAR || p.oq || !staged)
+            return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: Q4_K weights take planar "
+                                                                       "activations and 16-byte aligned staged rows");
+#define TN_GEMV_LAUNCHK(MT) return launch_variant<MT, true, X_PLANAR, 2>(p, (int)grid, smem, stream);
+        if (M <= 1) TN_GEMV_LAUNCHK(1)
+        if (M <= 2) TN_GEMV_LAUNCHK(2)
+        if (M <= 4) TN_GEMV_LAUNCHK(4)
+        if (M <= 8) TN_GEMV_LAUNCHK(8)
+        if (M <= 16) TN_GEMV_LAUNCHK(16)
+#undef TN_GEMV_LAUNCHK
+        return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: GEMV called with M > 16");
     }
     if (p.wfmt == 1) {  // Q8_0 weights: planar activations only
         if (p.x_mode != X_PLANAR || p.oq)
@@ -1193,6 +1278,25 @@ int launch_q8w_gemv(const uint8_t *w, const int8_t *xq, const float *xd, const f
     p.x_mode = X_PLANAR;
     p.wfmt = 1;
     return launch_gemv(p, M, N, K, flags & ~TN_EPILOGUE_SILU_MUL_PAIRS, stream);
+}
+
+int launch_q4k_gemv(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
+                    const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
+                    cudaStream_t stream) {
+    GemvParams p{};
+    set_link(p, nullptr, N);
+    p.w = w;
+    p.xq = xq;
+    p.xd = xd;
+    p.xc = xc;
+    p.bias = bias;
+    p.y = y;
+    p.xq_row_stride = xq_row_stride;
+    p.y_row_stride = y_row_stride;
+    p.y_dtype = y_dtype;
+    p.x_mode = X_PLANAR;
+    p.wfmt = 2;
+    return launch_gemv(p, M, N, K, TN_WEIGHTS_STATIC, stream);
 }
 
 int launch_q4_gemv_fused(int x_mode, const void *xb, int64_t xb_row_stride, const void *xdelta, void *xh_out,

@@ -35,6 +35,13 @@ int launch_q8w_gemv(const uint8_t *w, const int8_t *xq, const float *xd, const f
                     const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
                     int flags, cudaStream_t stream);
 
+// Decode GEMV of Q4_K weights (144-byte super-blocks of 256) over planar Q8_K
+// activations: codes, per 32-block the super-block's d (xd) and the block's
+// code sum (xc); y[m, n] for m < M (M <= 16). Rows must be 16-byte aligned.
+int launch_q4k_gemv(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
+                    const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
+                    cudaStream_t stream);
+
 // Decode GEMV over planar Q8_0 activations: y[m, n] for m < M (M <= 16).
 int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
                       const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
