@@ -74,6 +74,26 @@ __device__ __forceinline__ uint32_t pack_t(float lo, float hi, int bf16) {
     return *reinterpret_cast<const uint32_t *>(&v);
 }
 
+// Packed f32 pairs (sm_100 f32x2: two lanes per instruction, each rounded as
+// the scalar operation) and the MUFU base-2 exponential.
+__device__ __forceinline__ void fma2r(float &d0, float &d1, float x0, float x1, float y, float z) {
+    asm("{\n\t.reg .b64 rd, rx, ry, rz;\n\tmov.b64 rx, {%2, %3};\n\tmov.b64 ry, {%4, %4};\n\tmov.b64 rz, {%5, %5};\n\t"
+        "fma.rn.f32x2 rd, rx, ry, rz;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(x0), "f"(x1), "f"(y), "f"(z));
+}
+__device__ __forceinline__ void add2(float &a0, float &a1, float x0, float x1) {
+    asm("{\n\t.reg .b64 ra, rx;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rx, {%2, %3};\n\t"
+        "add.rn.f32x2 ra, ra, rx;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(x0), "f"(x1));
+}
+__device__ __forceinline__ float ex2a(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Key tiles of query tile k (rows q0 + 128 k ...): none past the sequence,
 // and up to its diagonal when causal.
 __device__ __forceinline__ int tiles_of(const Args &a, int q0, int k) {
@@ -253,19 +273,21 @@ __global__ void __launch_bounds__(THREADS, 1) sdpa_prefill2_kernel(const __grid_
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[k * 2 + buf]);
             const bool full = (t + 1) * BN <= a.S && (!a.causal || (t + 1) * BN - 1 <= row0);
-            float mx = -INFINITY;
+            // four independent maxima (short dependency chains), then one
+            float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             if (full) {
 #pragma unroll
-                for (int c = 0; c < 64; ++c) mx = fmaxf(mx, sv[c]);
+                for (int c = 0; c < 64; ++c) mq[c & 3] = fmaxf(mq[c & 3], sv[c]);
             } else {
 #pragma unroll
                 for (int c = 0; c < 64; ++c) {
                     const int key = t * BN + c;
                     const bool masked = key >= a.S || (a.causal && key > row);
                     sv[c] = masked ? -INFINITY : sv[c];
-                    mx = fmaxf(mx, sv[c]);
+                    mq[c & 3] = fmaxf(mq[c & 3], sv[c]);
                 }
             }
+            float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
             mx *= c2;
             // the exponent's maximum moves only by more than 2^8
             float alpha = 1.0f;
@@ -278,12 +300,20 @@ __global__ void __launch_bounds__(THREADS, 1) sdpa_prefill2_kernel(const __grid_
 #pragma unroll
                 for (int c = 0; c < 64; ++c) sv[c] = 0.0f;
             } else {
+                // p = 2^(s c2 - m): packed exponent arguments, MUFU ex2, two
+                // packed partial sums
+                const float nm = -m_used;
+                float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    const float p = exp2f(fmaf(sv[c], c2, -m_used));
-                    sv[c] = p;
-                    sum += p;
+                for (int c = 0; c < 64; c += 2) {
+                    float e0, e1;
+                    fma2r(e0, e1, sv[c], sv[c + 1], c2, nm);
+                    const float p0 = ex2a(e0), p1 = ex2a(e1);
+                    sv[c] = p0;
+                    sv[c + 1] = p1;
+                    add2(s0, s1, p0, p1);
                 }
+                sum = s0 + s1;
             }
             l = l * alpha + sum;
             // PV_{t-1} has read P and written O: P may be rewritten, O rescaled
