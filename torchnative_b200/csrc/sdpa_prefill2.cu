@@ -75,18 +75,30 @@ __device__ __forceinline__ uint32_t pack_t(float lo, float hi, int bf16) {
 }
 
 // Packed f32 pairs (sm_100 f32x2: two lanes per instruction, each rounded as
-// the scalar operation) and the MUFU base-2 exponential.
-__device__ __forceinline__ void fma2r(float &d0, float &d1, float x0, float x1, float y, float z) {
-    asm("{\n\t.reg .b64 rd, rx, ry, rz;\n\tmov.b64 rx, {%2, %3};\n\tmov.b64 ry, {%4, %4};\n\tmov.b64 rz, {%5, %5};\n\t"
-        "fma.rn.f32x2 rd, rx, ry, rz;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(x0), "f"(x1), "f"(y), "f"(z));
+// the scalar operation) on 64-bit pair registers, so loop-invariant pairs are
+// packed once; the MUFU base-2 exponential; a three-input maximum.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
 }
-__device__ __forceinline__ void add2(float &a0, float &a1, float x0, float x1) {
-    asm("{\n\t.reg .b64 ra, rx;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rx, {%2, %3};\n\t"
-        "add.rn.f32x2 ra, ra, rx;\n\tmov.b64 {%0, %1}, ra;\n\t}"
-        : "+f"(a0), "+f"(a1)
-        : "f"(x0), "f"(x1));
+__device__ __forceinline__ void upk2(uint64_t r, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2p(uint64_t x, uint64_t y, uint64_t z) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(x), "l"(y), "l"(z));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2p(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float y;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+    return y;
 }
 __device__ __forceinline__ float ex2a(float x) {
     float y;
@@ -273,20 +285,19 @@ __global__ void __launch_bounds__(THREADS, 1) sdpa_prefill2_kernel(const __grid_
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[k * 2 + buf]);
             const bool full = (t + 1) * BN <= a.S && (!a.causal || (t + 1) * BN - 1 <= row0);
-            // four independent maxima (short dependency chains), then one
+            // four independent maxima (short dependency chains), two new
+            // values per three-input max, then one
             float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-            if (full) {
-#pragma unroll
-                for (int c = 0; c < 64; ++c) mq[c & 3] = fmaxf(mq[c & 3], sv[c]);
-            } else {
+            if (!full) {
 #pragma unroll
                 for (int c = 0; c < 64; ++c) {
                     const int key = t * BN + c;
                     const bool masked = key >= a.S || (a.causal && key > row);
                     sv[c] = masked ? -INFINITY : sv[c];
-                    mq[c & 3] = fmaxf(mq[c & 3], sv[c]);
                 }
             }
+#pragma unroll
+            for (int c = 0; c < 64; c += 2) mq[(c >> 1) & 3] = max3(mq[(c >> 1) & 3], sv[c], sv[c + 1]);
             float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
             mx *= c2;
             // the exponent's maximum moves only by more than 2^8
@@ -302,17 +313,19 @@ __global__ void __launch_bounds__(THREADS, 1) sdpa_prefill2_kernel(const __grid_
             } else {
                 // p = 2^(s c2 - m): packed exponent arguments, MUFU ex2, two
                 // packed partial sums
-                const float nm = -m_used;
-                float s0 = 0.0f, s1 = 0.0f;
+                const uint64_t c2p = pk2(c2, c2), nmp = pk2(-m_used, -m_used);
+                uint64_t sp = pk2(0.0f, 0.0f);
 #pragma unroll
                 for (int c = 0; c < 64; c += 2) {
                     float e0, e1;
-                    fma2r(e0, e1, sv[c], sv[c + 1], c2, nm);
+                    upk2(fma2p(pk2(sv[c], sv[c + 1]), c2p, nmp), e0, e1);
                     const float p0 = ex2a(e0), p1 = ex2a(e1);
                     sv[c] = p0;
                     sv[c + 1] = p1;
-                    add2(s0, s1, p0, p1);
+                    sp = add2p(sp, pk2(p0, p1));
                 }
+                float s0, s1;
+                upk2(sp, s0, s1);
                 sum = s0 + s1;
             }
             l = l * alpha + sum;
