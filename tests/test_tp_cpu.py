@@ -1,4 +1,4 @@
-"""Tensor-parallel sharding on the CPU (no GPU): world-size-2 gloo ranks each
+"""Tensor-parallel sharding on the CPU (no GPU): world-size-2 and -4 gloo ranks each
 take their shard of the Q4_0 weights with torchnative_b200.tp, run the oracle
 (the reference's CPU arithmetic) on it, and all-gather; the gathered rows equal
 the unsharded oracle output bit for bit, because a column shard changes which
@@ -87,11 +87,12 @@ def _worker(rank, world, port, failures):
         dist.destroy_process_group()
 
 
-def test_two_gloo_ranks_rebuild_the_unsharded_outputs():
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_rebuild_the_unsharded_outputs(world):
     ctx = mp.get_context("spawn")
     failures = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, failures)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, failures)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
