@@ -1,6 +1,7 @@
 """Tensor parallelism on the GPU: the layout step of the per-layer all-gather
-(one GPU), and a 2-rank NCCL decode that must produce the single-GPU token
-stream of the same seeded model (skipped with fewer than 2 GPUs)."""
+(one GPU), and 2-, 4- and 8-rank NCCL decodes that must produce the
+single-GPU token stream of the same seeded model (each skipped with fewer GPUs
+than ranks)."""
 
 import ctypes
 import os
@@ -13,6 +14,18 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 SMALL = dict(hidden=512, inter=1024, heads=8, kv_heads=4, head_dim=64, vocab=4096, layers=2, rope_theta=10000.0)
+WORLDS = [2, 4, 8]
+
+
+def _small(world: int) -> dict:
+    """SMALL with enough KV heads for every rank to own at least one."""
+    kv = max(SMALL["kv_heads"], world)
+    return dict(SMALL, kv_heads=kv, heads=2 * kv)
+
+
+def _need(world: int) -> None:
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
 
 
 def test_unshard_is_the_rank_major_transpose(cuda_device):
@@ -80,13 +93,13 @@ def _gather_worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def test_peer_allgather_two_ranks(cuda_device):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", WORLDS)
+def test_peer_allgather(cuda_device, world):
+    _need(world)
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, out), daemon=True) for r in range(2)]
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, out), daemon=True) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -124,7 +137,7 @@ def _run(rank, world, port, batch, steps, exchange, out):
                             device_id=torch.device("cuda", rank))
     try:
         build.build()
-        shape = LlamaShape(**SMALL)
+        shape = LlamaShape(**_small(world))
         dec = Q4LlamaDecoder(shape, batch=batch, capacity=64, device=f"cuda:{rank}", seed=3,
                              tp=TPGroup(rank, world, dist.group.WORLD), exchange=exchange)
         first = torch.arange(batch, device=f"cuda:{rank}", dtype=torch.int32) * 7 + 1
@@ -153,15 +166,15 @@ def _run(rank, world, port, batch, steps, exchange, out):
 
 @pytest.mark.parametrize("exchange", ["p2p", "nccl"])
 @pytest.mark.parametrize("batch", [1, 2])
-def test_two_rank_decode_matches_one_gpu(cuda_device, batch, exchange):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_decode_matches_one_gpu(cuda_device, world, batch, exchange):
+    _need(world)
     from torchnative_b200 import build
     from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
 
     build.build()
     steps = 6
-    dec = Q4LlamaDecoder(LlamaShape(**SMALL), batch=batch, capacity=64, device=cuda_device, seed=3)
+    dec = Q4LlamaDecoder(LlamaShape(**_small(world)), batch=batch, capacity=64, device=cuda_device, seed=3)
     first = torch.arange(batch, device=cuda_device, dtype=torch.int32) * 7 + 1
     dec.fill_prompt_cache(16)
     dec.start(first)
@@ -178,7 +191,8 @@ def test_two_rank_decode_matches_one_gpu(cuda_device, batch, exchange):
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, 2, port, batch, steps, exchange, out), daemon=True) for r in range(2)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, batch, steps, exchange, out), daemon=True)
+             for r in range(world)]
     for p in procs:
         p.start()
     try:
