@@ -223,6 +223,8 @@ TN_API int tn_q4_0_linear_q8(const int8_t *codes, int64_t codes_row_stride, cons
  *   TN_X_RMSNORM   transformers' LlamaRMSNorm of h = bf16(x + delta)
  *                  (delta may be NULL): norm_weight * bf16(h32 * rsqrt(mean(h32^2) + eps));
  *                  h is also written to h_out (if not NULL; must not alias x or delta);
+ *                  x, delta, h_out and norm_weight 16-byte aligned, rows of x_row_stride
+ *                  elements (a multiple of 8) in all three;
  *   TN_X_SILU_MUL  bf16(bf16(silu(gate)) * up) from rows [gate (K) | up (K)].
  * Then the Q8_0 quantiser (k_quants.rs:676-706) and the same GEMV as
  * tn_q4_0_linear_q8. No reference counterpart as one call: the reference runs

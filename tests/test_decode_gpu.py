@@ -189,17 +189,19 @@ def _host_reference_step(dec, tok, pos):
     return exact
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["fused-5-kernels", "separate-11-kernels"])
-def test_one_decode_step_of_a_small_q4_llama_against_the_host_reference(N, cuda_device, fused):
+@pytest.mark.parametrize("fused,B", [(True, 2), (False, 2), (False, 16)],
+                         ids=["fused-5-kernels", "separate-11-kernels", "separate-11-kernels-batch16"])
+def test_one_decode_step_of_a_small_q4_llama_against_the_host_reference(N, cuda_device, fused, B):
     from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
 
     shape = LlamaShape(hidden=512, inter=1024, heads=8, kv_heads=2, head_dim=64, vocab=2048, layers=2,
                        rope_theta=10000.0)
-    B, prompt = 2, 40
+    prompt = 40
     dec = Q4LlamaDecoder(shape, batch=B, capacity=64, device=cuda_device, seed=11)
+    assert dec.fused == (B <= 4)
     dec.fused = fused
     dec.fill_prompt_cache(prompt)
-    tok = torch.tensor([5, 1234], dtype=torch.int32)
+    tok = torch.tensor([5, 1234] + [(97 * i + 11) % 2048 for i in range(B - 2)], dtype=torch.int32)
     ref = _host_reference_step(dec, tok.long(), prompt)
     dec.start(tok.to(cuda_device))
     dec.step()
@@ -215,21 +217,22 @@ def test_one_decode_step_of_a_small_q4_llama_against_the_host_reference(N, cuda_
     N.device_status(reset=True)
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["fused-5-kernels", "separate-11-kernels"])
-def test_decode_step_replays_as_one_graph(N, cuda_device, fused):
+@pytest.mark.parametrize("fused,B", [(True, 1), (False, 1), (False, 16)],
+                         ids=["fused-5-kernels", "separate-11-kernels", "separate-11-kernels-batch16"])
+def test_decode_step_replays_as_one_graph(N, cuda_device, fused, B):
     from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
 
     shape = LlamaShape(hidden=512, inter=1024, heads=8, kv_heads=2, head_dim=64, vocab=2048, layers=2,
                        rope_theta=10000.0)
-    dec = Q4LlamaDecoder(shape, batch=1, capacity=80, device=cuda_device, seed=12)
+    dec = Q4LlamaDecoder(shape, batch=B, capacity=80, device=cuda_device, seed=12)
     dec.fused = fused
-    first = torch.tensor([7], dtype=torch.int32, device=cuda_device)
+    first = (torch.arange(B, dtype=torch.int32, device=cuda_device) * 131 + 7) % 2048
     dec.fill_prompt_cache(30)
     dec.start(first)
     eager = []
     for _ in range(4):
         dec.step()
-        eager.append(int(dec.tokens[0]))
+        eager.append(dec.tokens.tolist())
     dec.fill_prompt_cache(30)
     dec.start(first)
     g = dec.capture()
@@ -238,7 +241,7 @@ def test_decode_step_replays_as_one_graph(N, cuda_device, fused):
     replay = []
     for _ in range(4):
         g.replay()
-        replay.append(int(dec.tokens[0]))
+        replay.append(dec.tokens.tolist())
     assert replay == eager
     assert int(dec.pos.item()) == 34
 
@@ -352,35 +355,53 @@ def test_gemv_planar_q8_output_refuses_what_it_cannot_quantise(N, cuda_device):
     assert call(N.TN_BF16, 32, N.TN_EPILOGUE_SILU_MUL_PAIRS) == N.TN_ERR_SHAPE  # 16 columns of act
 
 
+@pytest.mark.parametrize("M,K", [(1, 4096), (3, 4096), (4, 4096), (2, 8192)])
 @pytest.mark.parametrize("with_delta", [True, False])
-def test_fused_rmsnorm_prologue_equals_the_separate_kernels(N, cuda_device, with_delta):
+def test_fused_rmsnorm_prologue_equals_the_separate_kernels(N, cuda_device, with_delta, M, K):
     """The q/k/v and gate/up GEMVs' fused RMSNorm + Q8_0 prologue (packed bf16
-    arithmetic) against tn_llama_add_rmsnorm_q8 + the planar GEMV (float
-    arithmetic), bit for bit. Activations are multiples of 0.5, so the sum of
-    squares is exact in any reduction order and both sides see the same
-    rsqrt; every other rounding must then agree."""
-    dev, K, Nout, eps = cuda_device, 4096, 512, 1e-5
-    g = torch.Generator(device=dev).manual_seed(5)
-    x = (torch.randint(-4, 5, (1, K), generator=g, device=dev) * 0.5).to(torch.bfloat16)
-    d = (torch.randint(-2, 3, (1, K), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    arithmetic with all rows' loads in flight at once up to K = 4096, the
+    per-element loop above) against tn_llama_add_rmsnorm_q8 + the planar GEMV
+    (float arithmetic), bit for bit. Activations are multiples of 0.5, so the
+    sum of squares is exact in any reduction order and both sides see the
+    same rsqrt; every other rounding must then agree."""
+    dev, Nout, eps = cuda_device, 512, 1e-5
+    g = torch.Generator(device=dev).manual_seed(5 + M)
+    x = (torch.randint(-4, 5, (M, K), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    d = (torch.randint(-2, 3, (M, K), generator=g, device=dev) * 0.5).to(torch.bfloat16)
     w = (1 + 0.1 * torch.randn(K, generator=g, device=dev)).to(torch.bfloat16)
     blob = torch.frombuffer(bytearray(q4_exact.random_q4_0_blob(np.random.default_rng(6), Nout, K)),
                             dtype=torch.uint8).to(dev)
     delta = P(d.data_ptr()) if with_delta else None
     h1, h2 = torch.zeros_like(x), torch.zeros_like(x)
-    y1 = torch.full((1, Nout), float("nan"), device=dev, dtype=torch.bfloat16)
+    y1 = torch.full((M, Nout), float("nan"), device=dev, dtype=torch.bfloat16)
     y2 = torch.full_like(y1, float("nan"))
     N.check(N.lib().tn_q4_0_linear_fused(N.TN_X_RMSNORM, P(x.data_ptr()), K, delta, P(h1.data_ptr()),
                                          P(w.data_ptr()), eps, P(blob.data_ptr()), None, P(y1.data_ptr()), N.TN_BF16,
-                                         1, Nout, K, N.TN_WEIGHTS_STATIC, _stream()))
-    codes = torch.empty((1, K), dtype=torch.int8, device=dev)
-    sc, of = torch.empty((1, K // 32), device=dev), torch.empty((1, K // 32), device=dev)
-    N.check(N.lib().tn_llama_add_rmsnorm_q8(P(x.data_ptr()), delta, P(h2.data_ptr()), P(w.data_ptr()), eps, 1, K,
+                                         M, Nout, K, N.TN_WEIGHTS_STATIC, _stream()))
+    codes = torch.empty((M, K), dtype=torch.int8, device=dev)
+    sc, of = torch.empty((M, K // 32), device=dev), torch.empty((M, K // 32), device=dev)
+    N.check(N.lib().tn_llama_add_rmsnorm_q8(P(x.data_ptr()), delta, P(h2.data_ptr()), P(w.data_ptr()), eps, M, K,
                                             P(codes.data_ptr()), P(sc.data_ptr()), P(of.data_ptr()), _stream()))
     N.check(N.lib().tn_q4_0_linear_q8(P(codes.data_ptr()), K, P(sc.data_ptr()), P(of.data_ptr()),
-                                      P(blob.data_ptr()), None, P(y2.data_ptr()), N.TN_BF16, 1, Nout, K,
+                                      P(blob.data_ptr()), None, P(y2.data_ptr()), N.TN_BF16, M, Nout, K,
                                       N.TN_WEIGHTS_STATIC, _stream()))
     torch.cuda.synchronize()
     assert torch.equal(h1, h2) and torch.equal(h1, x + d if with_delta else x)
     assert torch.equal(y1, y2)
     N.device_status(reset=True)
+
+
+def test_fused_rmsnorm_refuses_a_misaligned_h_out(N, cuda_device):
+    """h_out is written 16 bytes at a time: an unaligned one is refused before
+    anything is launched."""
+    dev, K = cuda_device, 256
+    x = torch.zeros((1, K), device=dev, dtype=torch.bfloat16)
+    h = torch.zeros(K + 1, device=dev, dtype=torch.bfloat16)
+    w = torch.zeros(K, device=dev, dtype=torch.bfloat16)
+    blob = torch.zeros(64 * K // 32 * 18, device=dev, dtype=torch.uint8)
+    y = torch.zeros((1, 64), device=dev, dtype=torch.bfloat16)
+    rc = N.lib().tn_q4_0_linear_fused(N.TN_X_RMSNORM, P(x.data_ptr()), K, None, P(h.data_ptr() + 2),
+                                      P(w.data_ptr()), 1e-5, P(blob.data_ptr()), None, P(y.data_ptr()), N.TN_BF16,
+                                      1, 64, K, 0, _stream())
+    assert rc == N.TN_ERR_INVALID
+    assert "16-byte aligned" in N.last_error()

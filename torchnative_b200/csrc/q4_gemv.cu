@@ -398,79 +398,116 @@ constexpr int kMaxFusedRows = 4;
 // rsqrt(mean(x^2) + eps)), x = bf16(h + delta)), or bf16(bf16(silu(g)) * u)
 // (X_SILU). Consumer threads only; `red` is kMaxFusedRows * kConsumerWarps
 // floats of shared scratch.
-template <int XM>
+template <int MT, int XM>
 __device__ __forceinline__ void stage_x_fused(const Smem &s, const GemvParams &p, int tid, int warp, int lane,
                                               float *red) {
     const int K = p.nb * 32, nthr = kConsumerWarps * 32;
-    if (XM == X_NORM && p.M == 1 && 2 * p.nb <= nthr) {
-        // The decode case: one row, half a block per thread (lanes 2i, 2i + 1
-        // share block i). Every load is issued before the first use and the
-        // values stay in registers across the CTA-wide reduction, so the
-        // prologue costs one L2 round trip.
-        const int b = tid >> 1, hf = tid & 1, e0 = b * 32 + 16 * hf;
+    if (XM == X_NORM && 2 * p.nb <= nthr) {
+        // The decode case (K <= 16 x consumer threads): half a block per
+        // thread and row (lanes 2i, 2i + 1 share block i). Every load of
+        // every row is issued before the first use and the values stay in
+        // registers across the CTA-wide reduction, so the prologue costs one
+        // L2 round trip whatever the row count.
         // h = bf16(x + delta) as packed pairs: a correctly rounded bf16 sum is
         // the f32 sum rounded to bf16 (the exact sum of two bf16 values either
         // fits in f32 or differs from the larger by less than a quarter bf16
         // ulp), so __hadd2 gives transformers' bits
-        uint32_t hb[8], wp[8];
-        float ss = 0.0f;
+        constexpr int R = MT < kMaxFusedRows ? MT : kMaxFusedRows;
+        const int b = tid >> 1, hf = tid & 1, e0 = b * 32 + 16 * hf;
+        uint32_t hb[R][8], wp[8];
+        float ss[R];
+#pragma unroll
+        for (int m = 0; m < R; ++m) ss[m] = 0.0f;
         if (b < p.nb) {
-            int4 xr[2], dr[2], wr[2];
+            int4 xr[R][2], dr[R][2], wr[2];
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                xr[c] = __ldg(reinterpret_cast<const int4 *>(p.xb + e0) + c);
-                dr[c] = p.xdelta ? __ldg(reinterpret_cast<const int4 *>(p.xdelta + e0) + c) : make_int4(0, 0, 0, 0);
-                wr[c] = __ldg(reinterpret_cast<const int4 *>(p.xw + e0) + c);
-            }
+            for (int c = 0; c < 2; ++c) wr[c] = __ldg(reinterpret_cast<const int4 *>(p.xw + e0) + c);
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                const uint32_t xu[4] = {(uint32_t)xr[c].x, (uint32_t)xr[c].y, (uint32_t)xr[c].z, (uint32_t)xr[c].w};
-                const uint32_t du[4] = {(uint32_t)dr[c].x, (uint32_t)dr[c].y, (uint32_t)dr[c].z, (uint32_t)dr[c].w};
-                const uint32_t wu[4] = {(uint32_t)wr[c].x, (uint32_t)wr[c].y, (uint32_t)wr[c].z, (uint32_t)wr[c].w};
+            for (int m = 0; m < R; ++m) {
+                if (m >= p.M) continue;
+                const int64_t o = m * p.xb_row_stride + e0;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    hb[4 * c + i] = p.xdelta ? bf2_bits(__hadd2(bf2_of(xu[i]), bf2_of(du[i]))) : xu[i];
-                    wp[4 * c + i] = wu[i];
+                for (int c = 0; c < 2; ++c) {
+                    xr[m][c] = __ldg(reinterpret_cast<const int4 *>(p.xb + o) + c);
+                    dr[m][c] = p.xdelta ? __ldg(reinterpret_cast<const int4 *>(p.xdelta + o) + c)
+                                        : make_int4(0, 0, 0, 0);
                 }
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float lo = bf_lo(hb[i]), hi = bf_hi(hb[i]);
-                ss = fmaf(lo, lo, ss);
-                ss = fmaf(hi, hi, ss);
+            for (int c = 0; c < 2; ++c) {
+                wp[4 * c] = (uint32_t)wr[c].x;
+                wp[4 * c + 1] = (uint32_t)wr[c].y;
+                wp[4 * c + 2] = (uint32_t)wr[c].z;
+                wp[4 * c + 3] = (uint32_t)wr[c].w;
+            }
+#pragma unroll
+            for (int m = 0; m < R; ++m) {
+                if (m >= p.M) continue;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const uint32_t xu[4] = {(uint32_t)xr[m][c].x, (uint32_t)xr[m][c].y, (uint32_t)xr[m][c].z,
+                                            (uint32_t)xr[m][c].w};
+                    const uint32_t du[4] = {(uint32_t)dr[m][c].x, (uint32_t)dr[m][c].y, (uint32_t)dr[m][c].z,
+                                            (uint32_t)dr[m][c].w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        hb[m][4 * c + i] = p.xdelta ? bf2_bits(__hadd2(bf2_of(xu[i]), bf2_of(du[i]))) : xu[i];
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float lo = bf_lo(hb[m][i]), hi = bf_hi(hb[m][i]);
+                    ss[m] = fmaf(lo, lo, ss[m]);
+                    ss[m] = fmaf(hi, hi, ss[m]);
+                }
             }
         }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        if (lane == 0) red[warp] = ss;
+        for (int m = 0; m < R; ++m) {
+            if (m >= p.M) continue;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], off);
+            if (lane == 0) red[m * kConsumerWarps + warp] = ss[m];
+        }
         asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-        float t = 0.0f;
+        float r[R];
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) t += red[w];
-        const float r = rsqrtf(t / (float)K + p.eps);
+        for (int m = 0; m < R; ++m) {
+            float t = 0.0f;
+            if (m < p.M)
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) t += red[m * kConsumerWarps + w];
+            r[m] = rsqrtf(t / (float)K + p.eps);
+        }
         if (b < p.nb) {
-            if (p.xh_out && blockIdx.x == 0) {
-                int4 *dst = reinterpret_cast<int4 *>(p.xh_out + e0);
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-                    dst[c] = make_int4((int)hb[4 * c], (int)hb[4 * c + 1], (int)hb[4 * c + 2], (int)hb[4 * c + 3]);
-            }
-            // w * bf16(h * r): the f32 products rounded to bf16 in one packed
-            // convert, then one correctly rounded bf16 product per pair (a
-            // product of two bf16 values is exact in f32, so it equals
-            // bf16(f32 product))
-            uint32_t v[8];
+            for (int m = 0; m < R; ++m) {
+                if (m >= p.M) continue;
+                if (p.xh_out && blockIdx.x == 0) {
+                    int4 *dst = reinterpret_cast<int4 *>(p.xh_out + m * p.xb_row_stride + e0);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const __nv_bfloat162 hr = __floats2bfloat162_rn(bf_lo(hb[i]) * r, bf_hi(hb[i]) * r);
-                v[i] = bf2_bits(__hmul2(bf2_of(wp[i]), hr));
+                    for (int c = 0; c < 2; ++c)
+                        dst[c] = make_int4((int)hb[m][4 * c], (int)hb[m][4 * c + 1], (int)hb[m][4 * c + 2],
+                                           (int)hb[m][4 * c + 3]);
+                }
+                // w * bf16(h * r): the f32 products rounded to bf16 in one
+                // packed convert, then one correctly rounded bf16 product per
+                // pair (a product of two bf16 values is exact in f32, so it
+                // equals bf16(f32 product))
+                uint32_t v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const __nv_bfloat162 hr = __floats2bfloat162_rn(bf_lo(hb[m][i]) * r[m], bf_hi(hb[m][i]) * r[m]);
+                    v[i] = bf2_bits(__hmul2(bf2_of(wp[i]), hr));
+                }
+                q8_half_block_bf16_to_smem(v, m, b, hf, s, p, lane);
             }
-            q8_half_block_bf16_to_smem(v, 0, b, hf, s, p, lane);
         } else if (b < p.nbp) {
             float z[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) z[j] = 0.0f;
-            q8_half_block_to_smem(z, 0, b, hf, s, p, lane);
+#pragma unroll
+            for (int m = 0; m < R; ++m)
+                if (m < p.M) q8_half_block_to_smem(z, m, b, hf, s, p, lane);
         }
         return;
     }
@@ -890,7 +927,7 @@ __global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel
         stage_x(s, p, threadIdx.x, kConsumerWarps * 32);
     } else {
         __shared__ float red[kMaxFusedRows * kConsumerWarps];
-        stage_x_fused<XM>(s, p, threadIdx.x, warp, lane, red);
+        stage_x_fused<MT, XM>(s, p, threadIdx.x, warp, lane, red);
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 

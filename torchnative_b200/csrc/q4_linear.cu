@@ -245,7 +245,7 @@ int linear_fused(const std::string &op, int x_mode, const void *x, int64_t x_row
     if ((reinterpret_cast<uintptr_t>(w_blob) & 1) != 0)
         return tn::set_error(TN_ERR_INVALID, op + ": the q4_0 blob must be at least 2-byte aligned");
     const uintptr_t a = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(delta) |
-                        reinterpret_cast<uintptr_t>(norm_weight);
+                        reinterpret_cast<uintptr_t>(norm_weight) | reinterpret_cast<uintptr_t>(h_out);
     if ((a & 15) != 0 || (x_row_stride * 2) % 16 != 0)
         return tn::set_error(TN_ERR_INVALID, op + ": bf16 rows must be 16-byte aligned");
     const bool pairs = (flags & TN_EPILOGUE_SILU_MUL_PAIRS) != 0;
