@@ -847,7 +847,7 @@ __device__ __forceinline__ void global_rows(const Smem &s, const GemvParams &p, 
 
 // WF: weight format, 0 = Q4_0, 1 = Q8_0, 2 = Q4_K.
 template <int MT, bool STAGED, int XM, int WF>
-__global__ void __launch_bounds__(kThreads, (MT <= 2) ? 2 : 1) q4_gemv_q8_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kThreads, (MT <= 8) ? 2 : 1) q4_gemv_q8_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, p);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1167,11 +1167,14 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
     p.err = device_error_word();
     bool staged = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(p.w) & 15) == 0);
     const int ycols = p.oq ? kYCap : 0;
-    // Two CTAs per SM for M <= 2 (each with ~64 KB in flight): the next
-    // kernel's CTAs can then start streaming while this one's last CTAs drain.
+    // Two CTAs per SM for M <= 8 when both fit (each with ~64 KB in flight):
+    // the next kernel's CTAs can then start streaming while this one's last
+    // CTAs drain, and from 3 rows on the dot products, not HBM, bound one
+    // CTA's 8 consumer warps -- a second CTA doubles the warps that hide
+    // their latency.
     Plan plan{false, 1, 0, 0, 2};
     int ctas_per_sm = 1;
-    if (M <= 2) {
+    if (M <= 8) {
         plan = plan_slots(M, p.nbp, p.rowbytes, staged, kTwoCtaBudget, 64 * 1024, ycols);
         if (plan.ok) ctas_per_sm = 2;
     }
