@@ -294,14 +294,25 @@ def run_ours(args, rank, world, local):
     dec.fill_prompt_cache(PROMPT)
     dec.start(first)
 
-    # the dominant kernel alone: 32 back-to-back gate/up GEMVs over the 32 layers' weights
-    gd = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gd):
+    # the dominant kernel alone: 32 back-to-back gate/up linears over the 32
+    # layers' weights (run once on the capture stream first: the library's
+    # workspaces are per stream, and nothing may allocate while capturing)
+    def gate_up_layers():
         for lw in dec.layers:
             _native.check(_native.lib().tn_q4_0_linear_q8(
                 P(dec.codes.data_ptr()), HIDDEN, P(dec.scales.data_ptr()), P(dec.offsets.data_ptr()),
                 P(lw["gate_up"].data_ptr()), None, P(dec.act_l.data_ptr()), _native.TN_BF16, B, 2 * dec.i_l, HIDDEN,
                 _native.TN_WEIGHTS_STATIC | _native.TN_EPILOGUE_SILU_MUL_PAIRS, cur()))
+
+    gs = torch.cuda.Stream(dev)
+    gs.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(gs):
+        gate_up_layers()
+    gs.synchronize()
+    gd = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gd, stream=gs):
+        gate_up_layers()
+    torch.cuda.current_stream(dev).wait_stream(gs)
 
     for _ in range(args.warmup):
         g.replay()
@@ -402,7 +413,8 @@ def run_ours(args, rank, world, local):
                    "l2": "inputs larger than L2 (4.22 GB of weights per step)",
                    "mean_context": mean_ctx, "bytes_per_step": step_bytes,
                    "hbm_roofline_tok_s": B * peak * 1e9 / step_bytes},
-        "roofline": {"bound": "hbm", "kernel": f"q4_gemv_q8_kernel (gate/up {n}x{k} on this rank, SiLU*up epilogue)",
+        "roofline": {"bound": "hbm", "kernel": f"{'q4_skinny_kernel' if 9 <= B <= 32 else 'q4_gemv_q8_kernel'} "
+                                               f"(gate/up {n}x{k} on this rank, SiLU*up epilogue)",
                      "achieved": achieved,
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": scaled_traffic(n), "algorithmic_bytes": algo, "avg_launch_us": dom_us},
@@ -677,7 +689,9 @@ def run_case_gemv(args):
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / (args.steps * copies)
         algo = wbytes + M * (k + k // 32 * 8) + M * n * 2
-        print(json.dumps({"case": "gemv", "format": args.format, "M": M, "N": n, "K": k, "us_per_launch": us,
+        kernel = "q4_skinny_kernel" if args.format == "q4_0" and 9 <= M <= 32 and k % 256 == 0 else "q4_gemv_q8_kernel"
+        print(json.dumps({"case": "gemv", "format": args.format, "kernel": kernel, "M": M, "N": n, "K": k,
+                          "us_per_launch": us,
                           "GBps": algo / us / 1e3, "frac": algo / us / 1e3 / peak, "peak": peak,
                           "peak_kind": peak_kind, "copies": copies}), flush=True)
         del ws

@@ -96,7 +96,8 @@ typedef struct {
     uint64_t sdpa_decode_launches; /* split-KV decode kernels */
     uint64_t sdpa_prefill_launches;
     uint64_t bytes_allocated;
-    uint64_t reserved[6];
+    uint64_t q4_skinny_launches;   /* batched-decode (9..32 rows) tensor-core launches */
+    uint64_t reserved[5];
 } tn_counters;
 TN_API int tn_get_counters(tn_counters *out);
 TN_API int tn_reset_counters(void);

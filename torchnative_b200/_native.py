@@ -43,8 +43,8 @@ _PI64 = ctypes.POINTER(ctypes.c_int64)
 class Counters(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in (
         "q4_linear_calls", "q4_gemv_launches", "q4_gemv_generic", "q4_gemm_launches", "q8_quant_launches",
-        "q4_codec_launches", "sdpa_calls", "sdpa_decode_launches", "sdpa_prefill_launches", "bytes_allocated")] + [
-        ("reserved", ctypes.c_uint64 * 6)]
+        "q4_codec_launches", "sdpa_calls", "sdpa_decode_launches", "sdpa_prefill_launches", "bytes_allocated",
+        "q4_skinny_launches")] + [("reserved", ctypes.c_uint64 * 5)]
 
 
 SIGNATURES = {

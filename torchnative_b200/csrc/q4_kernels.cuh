@@ -24,6 +24,20 @@ constexpr int64_t kQ4GemmMinRows = 48;
 int launch_q4_gemm(const __half *xq, int64_t xq_row_stride, const float *xd, const uint8_t *w, const float *bias,
                    void *y, int y_dtype, int64_t y_row_stride, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
 
+// Batched decode (kQ4SkinnyMinRows <= M <= kQ4SkinnyMaxRows) on tcgen05 with
+// the weights on the MMA's 128-row side: planar Q8_0 activations (codes
+// [M][xq_row_stride] int8, 16-byte aligned rows; xd and xc [M][K/32], 16-byte
+// aligned); needs K % 256 == 0 and a 16-byte aligned blob. flags:
+// TN_EPILOGUE_SILU_MUL_PAIRS.
+// From 9 rows on (below, the GEMV's 2-CTA plans stream faster; at 16 rows the
+// GEMV needs row chunks for K = 14336 and this kernel halves down_proj).
+constexpr int64_t kQ4SkinnyMinRows = 9, kQ4SkinnyMaxRows = 32;
+bool q4_skinny_applies(const void *w_blob, const float *xd, const float *xc, int64_t M, int64_t N, int64_t K,
+                       int flags);
+int launch_q4_skinny(const int8_t *xq, int64_t xq_row_stride, const float *xd, const float *xc, const uint8_t *w,
+                     const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
+                     int flags, cudaStream_t stream);
+
 // Largest activation-row count (<= 16) one GEMV launch holds in shared memory
 // for this K (wfmt 0: Q4_0 weights, 1: Q8_0 weights); 0 if even one row does
 // not fit.

@@ -78,6 +78,9 @@ extern "C" int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, 
     float *xc = xd + (size_t)M * nb;
     st = tn::launch_q8_planar(x, x_dtype, x_row_stride, xq, xd, xc, M, nb, K, stream);
     if (st) return st;
+    if (tn::q4_skinny_applies(w_blob, xd, xc, M, N, K, 0))  // batched decode: the tensor cores
+        return tn::launch_q4_skinny(xq, K, xd, xc, static_cast<const uint8_t *>(w_blob), bias, y, y_dtype, N, (int)M,
+                                    N, K, 0, stream);
 
     const int chunk = tn::q4_gemv_max_rows(K);
     if (chunk <= 0)
@@ -200,6 +203,9 @@ extern "C" int tn_q4_0_linear_q8_tp(const int8_t *codes, int64_t codes_row_strid
         if (M > chunk) return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": a tensor-parallel link needs one launch (M <= " +
                                                                         std::to_string(chunk) + ")");
     }
+    if (!link && tn::q4_skinny_applies(w_blob, scales, offsets, M, N, K, flags))  // batched decode: tensor cores
+        return tn::launch_q4_skinny(codes, codes_row_stride, scales, offsets, static_cast<const uint8_t *>(w_blob),
+                                    bias, y, y_dtype, ycols, (int)M, N, K, flags, stream);
     const size_t ysz = tn_dtype_size(y_dtype);
     for (int64_t m0 = 0; m0 < M; m0 += chunk) {
         const int mc = (int)((M - m0) < chunk ? (M - m0) : chunk);
