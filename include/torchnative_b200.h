@@ -256,8 +256,11 @@ TN_API int tn_q4_0_linear_fused_q8out(int x_mode, const void *x, int64_t x_row_s
  * reference: it exists for hosts that cannot let a library call cudaMalloc
  * while they run -- an engine that owns a preplanned arena of HBM, work being
  * recorded into a CUDA graph under global capture mode, a loop that cannot
- * absorb cudaMalloc's implicit synchronisation. Same arguments, arithmetic and
- * result as tn_q4_0_linear in TN_ACT_Q8_0 mode; the Q8_0 activation blocks go
+ * absorb cudaMalloc's implicit synchronisation. Same arguments and arithmetic
+ * as tn_q4_0_linear in TN_ACT_Q8_0 mode, through the decode GEMV: the same
+ * result bit for bit up to 8 rows; from 9 rows tn_q4_0_linear takes the
+ * tensor-core kernel, whose summation order differs (both lie within the
+ * counted error bound of the exact value). The Q8_0 activation blocks go
  * to a fixed __device__ array inside this library (320 KB, held on every GPU
  * that loads the library until the process exits) instead of the allocator.
  * Limits: M <= TN_NOALLOC_MAX_ROWS and K <= TN_NOALLOC_MAX_IN; larger calls

@@ -2,8 +2,11 @@
 device allocation while they run (a preplanned HBM arena, recording a CUDA
 graph under global capture, a loop that cannot absorb cudaMalloc's implicit
 synchronisation). It keeps its activation blocks in a fixed device array in
-the library instead of the allocator, so its results must be the allocating
-entry point's, call after call, while the shared array is reused.
+the library instead of the allocator and runs the decode GEMV, so up to 8 rows
+its results must be the allocating entry point's bit for bit, call after call,
+while the shared array is reused; from 9 rows the allocating entry point takes
+the tensor-core kernel (another summation order), and both must lie within the
+counted bound of the exact value.
 
 Collected last (test_zz_*) so a failure here stops a `-x` run only after every
 other test has run; it also passes alone in a fresh process.
@@ -41,7 +44,8 @@ def _call(N, fn, x, w, y, M, Nout, K, bias=None):
     N.check(getattr(N.lib(), fn)(*args))
 
 
-@pytest.mark.parametrize("M,Nout,K", [(1, 4096, 4096), (16, 1000, 4096), (3, 517, 14336), (5, 64, 576)])
+@pytest.mark.parametrize("M,Nout,K", [(1, 4096, 4096), (8, 1000, 4096), (16, 1000, 4096), (3, 517, 14336),
+                                       (5, 64, 576)])
 def test_noalloc_matches_the_allocating_entry_point_twice_in_a_row(lib, cuda_device, M, Nout, K):
     rng = np.random.default_rng(M + Nout + K)
     blob = q4_exact.random_q4_0_blob(rng, Nout, K)
@@ -54,11 +58,14 @@ def test_noalloc_matches_the_allocating_entry_point_twice_in_a_row(lib, cuda_dev
         _call(lib, "tn_q4_0_linear", x, w, want, M, Nout, K)
         _call(lib, "tn_q4_0_linear_noalloc", x, w, got, M, Nout, K)
         torch.cuda.synchronize()
-        # the same kernels on the same blocks: identical, and inside the counted bound
-        assert torch.equal(got, want), f"call {call}: differs from tn_q4_0_linear"
+        # up to 8 rows the same kernels on the same blocks: identical; always
+        # inside the counted bound
+        if M <= 8:
+            assert torch.equal(got, want), f"call {call}: differs from tn_q4_0_linear"
         exact, abs_sum, ref_err = q4_exact.exact_linear_q4_0(oracle.q8_0_quantize(x_np), blob, M, Nout, K)
         bound = q4_exact.linear_bound(K, abs_sum, ref_err)
         assert float(np.max(np.abs(got.cpu().numpy().astype(np.float64) - exact) / bound)) <= 1.0
+        assert float(np.max(np.abs(want.cpu().numpy().astype(np.float64) - exact) / bound)) <= 1.0
     lib.device_status(reset=True)
 
 
