@@ -1,5 +1,5 @@
 // q4_skinny.cu -- the Q4_0 linear for a few activation rows (batched decode:
-// 3 <= M <= 32) on the 5th generation tensor cores, weights on the MMA's
+// 9 <= M <= 32) on the 5th generation tensor cores, weights on the MMA's
 // 128-row side and the activation rows as its N (16 or 32).
 //
 // Arithmetic (the reference's, k_quants.rs:312-330): y[m, n] = sum over
@@ -13,19 +13,22 @@
 // apply acc = fma(isum * d_w, d_x, acc) in f32, block by block.
 //
 // One CTA = 128 weight rows x all activation rows x one range of K (a split;
-// splits > 1 when the weight has too few 128-row tiles to fill the GPU), 10
-// warps:
-//   warp 0      TMA producer: activation panels (NP rows x 128 int8 codes,
-//               128-byte swizzle) and raw weight chunks (128 rows x 144 bytes =
-//               8 Q4_0 blocks per row, straight from the GGML blob)
+// splits > 1 when the weight has too few 128-row tiles to fill the GPU in one
+// wave of two CTAs per SM), 14 warps:
+//   warp 0      TMA producer: per 256-wide chunk of K, the activation code
+//               panels (NP rows x 128 int8 codes, 128-byte swizzle) with the
+//               chunk's activation scales and offsets (NP rows x 8 blocks of
+//               f32), and the raw weight chunk (128 rows x 144 bytes = 8 Q4_0
+//               blocks per row, straight from the GGML blob)
 //   warp 1      TMEM owner and MMA issuer (one thread): one K = 32 MMA per
 //               block, M = 128, N = NP
 //   warps 2-5   converters (thread = weight row): raw blocks -> nibble bytes in
 //               K order in the swizzled K-major panel the MMA reads, and the
 //               f32 block scales d_w
-//   warps 6-9   epilogue (thread = weight row = TMEM lane): per block one TMEM
-//               load of NP columns, then the scale-and-accumulate for every
-//               activation row
+//   warps 6-13  epilogue (thread = weight row = TMEM lane; the two warps of a
+//               lane quarter take half of the activation rows each): TMEM
+//               loads of a group of blocks per wait, then the
+//               scale-and-accumulate for each of its activation rows
 // With splits, each CTA stores its partial sums; the last CTA of a tile (an
 // atomic ticket) adds them in split order and writes y. Every wait is
 // bounded; a wait that gives up raises a CTA-wide abort flag so the other
