@@ -1,4 +1,4 @@
-"""Tensor-parallel sharding on the CPU (no GPU): world-size-2 and -4 gloo ranks each
+"""Tensor-parallel sharding on the CPU (no GPU): world-size-2, -4 and -8 gloo ranks each
 take their shard of the Q4_0 weights with torchnative_b200.tp, run the oracle
 (the reference's CPU arithmetic) on it, and all-gather; the gathered rows equal
 the unsharded oracle output bit for bit, because a column shard changes which
@@ -44,7 +44,10 @@ def _worker(rank, world, port, failures):
     try:
         g = tpm.TPGroup(rank, world, None)
         rng = np.random.default_rng(5)  # same weights and inputs on every rank
-        B, H, I, Hq, Hkv, D = 2, 256, 512, 8, 4, 32
+        # at least one KV head per rank
+        B, H, I, D = 2, 256, 512, 32
+        Hkv = max(4, world)
+        Hq = 2 * Hkv
         x = rng.standard_normal((B, H)).astype(np.float32)
         # column-sharded linear (o / down / lm_head)
         w = _blob(rng, H, H)
@@ -87,7 +90,7 @@ def _worker(rank, world, port, failures):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_gloo_ranks_rebuild_the_unsharded_outputs(world):
     ctx = mp.get_context("spawn")
     failures = ctx.Queue()
