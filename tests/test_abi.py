@@ -53,3 +53,37 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_native, "_lib", None)
     with pytest.raises(_native.NativeLibraryMissing):
         _native.lib()
+
+
+def _c_layout(tmp_path, ctype: str, names):
+    """sizeof and offsetof of a header struct, from a C probe compiled here."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / f"probe_{ctype}.c"
+    src.write_text("#include <stddef.h>\n#include <stdio.h>\n#include \"torchnative_b200.h\"\nint main(void) {\n"
+                   f"  printf(\"size %zu\\n\", sizeof({ctype}));\n"
+                   + "".join(f"  printf(\"{n} %zu\\n\", offsetof({ctype}, {n}));\n" for n in names)
+                   + "  return 0;\n}\n")
+    exe = tmp_path / f"probe_{ctype}"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    return {k: int(v) for k, v in (line.split() for line in out.splitlines())}
+
+
+@pytest.mark.parametrize("ctype,mirror", [("tn_counters", "Counters"), ("tn_tp_link", "TpLink")])
+def test_struct_bindings_match_the_header(tmp_path, ctype, mirror):
+    """The ctypes mirrors of the header's structs have the C size and every
+    field at the C offset (a field added on one side only would shift every
+    field read after it)."""
+    import ctypes
+
+    cls = getattr(_native, mirror)
+    names = [n for n, _ in cls._fields_]
+    got = _c_layout(tmp_path, ctype, names)
+    assert got["size"] == ctypes.sizeof(cls)
+    for n in names:
+        assert got[n] == getattr(cls, n).offset, n
