@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ops", action="store_true", help="skip the op-level BASELINE figures (configs[1], [2])")
     ap.add_argument("--case", default=None, choices=["gemv", "gemm", "sdpa_decode", "sdpa_prefill"],
                     help="kernel-level case instead of the decode step: 'gemv' times the decode GEMV alone on the "
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
@@ -386,9 +387,34 @@ def run_ours(args, rank, world, local):
 
     peak, peak_kind = measured_peaks()
     n, k = 2 * dec.i_l, HIDDEN
-    algo = q4_bytes(n, k) + B * (k + k // 32 * 8) + B * (n // 2) * 2
+    # the dominant launch as the step runs it: on one GPU at batch <= 4 the
+    # RMSNorm-prologue gate/up GEMV with the SiLU*up epilogue writing act's
+    # planar Q8_0 (bf16 h and delta in, norm weight, weights, act + its Q8 out)
+    if "gate_up_rmsnorm_gemv_silu_q8" in kernel_us:
+        dom_us = kernel_us["gate_up_rmsnorm_gemv_silu_q8"]
+        dom_name = "q4_gemv_q8_kernel<X_NORM> (gate/up as the step runs it: RMSNorm prologue, SiLU*up epilogue, planar Q8_0 out)"
+        algo = q4_bytes(n, k) + B * k * 2 * 3 + k * 2 + B * (n // 2) * (2 + 1) + B * (n // 64) * 8
+    else:
+        dom_name = f"{'q4_skinny_kernel' if 9 <= B <= 32 else 'q4_gemv_q8_kernel'} (gate/up {n}x{k} on this rank, SiLU*up epilogue)"
+        algo = q4_bytes(n, k) + B * (k + k // 32 * 8) + B * (n // 2) * 2
     achieved = algo / (dom_us * 1e-6) / 1e9
     step_bytes = dec.weight_bytes + dec.kv_bytes(int(mean_ctx))
+    per_kernel = {}
+    if kernel_us:
+        ctx = int(mean_ctx)
+        kv = 2 * B * dec.hkv * ctx * HEAD_DIM * 2
+        kbytes = {"qkv_rmsnorm_gemv": q4_bytes(dec.qkv_l, HIDDEN) + B * HIDDEN * 4 + HIDDEN * 2 + B * dec.qkv_l * 2,
+                  "sdpa_decode_step_q8": kv + B * dec.qkv_l * 2 + B * HEADS * HEAD_DIM * 3,
+                  "o_gemv": q4_bytes(HIDDEN, HEADS * HEAD_DIM) + B * HEADS * HEAD_DIM * 5 // 4 + B * HIDDEN * 2,
+                  "gate_up_rmsnorm_gemv_silu_q8": algo,
+                  "down_gemv": q4_bytes(HIDDEN, INTER) + B * INTER * 5 // 4 + B * HIDDEN * 2}
+        for name, us in kernel_us.items():
+            b = kbytes.get(name)
+            per_kernel[name] = {"us": us, "bytes": b,
+                                "frac": None if b is None else round(b / (us * 1e-6) / 1e9 / peak, 3)}
+        layer_us = sum(kernel_us.values())
+        per_kernel["per_layer_total"] = {"us": round(layer_us, 2), "bytes": sum(kbytes.values()),
+                                         "frac": round(sum(kbytes.values()) / (layer_us * 1e-6) / 1e9 / peak, 3)}
     result = {
         "metric": METRIC,
         "value": B * 1000.0 / ms,  # one model, tensor-parallel over the group: B tokens per step
@@ -413,13 +439,13 @@ def run_ours(args, rank, world, local):
                    "l2": "inputs larger than L2 (4.22 GB of weights per step)",
                    "mean_context": mean_ctx, "bytes_per_step": step_bytes,
                    "hbm_roofline_tok_s": B * peak * 1e9 / step_bytes},
-        "roofline": {"bound": "hbm", "kernel": f"{'q4_skinny_kernel' if 9 <= B <= 32 else 'q4_gemv_q8_kernel'} "
-                                               f"(gate/up {n}x{k} on this rank, SiLU*up epilogue)",
+        "roofline": {"bound": "hbm", "kernel": dom_name,
                      "achieved": achieved,
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": scaled_traffic(n), "algorithmic_bytes": algo, "avg_launch_us": dom_us},
         "step_hbm_frac": (step_bytes / (ms * 1e-3) / 1e9) / peak,
         "kernel_us_back_to_back": kernel_us,
+        "per_kernel": per_kernel,
         "e2e": {"value": B * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                 "d2h_bytes_per_step": 4 * B},
         "gpu_launches": dec.kernels_per_step * args.steps,
@@ -443,6 +469,180 @@ def run_ours(args, rank, world, local):
                                             f"{PROMPT}-token f32 cache, 32 times, + lm_head; oracle/tn_oracle.c "
                                             "restatement of the reference CPU arithmetic; min of 2"}
     return result
+
+
+def _time_graph(launches, warmup: int, reps: int) -> float:
+    """Microseconds per launch of `launches` (a list of zero-argument calls,
+    each one launch), captured once as a CUDA graph on a side stream after
+    one eager pass there (the library's workspaces are per stream and nothing
+    may allocate while capturing), timed with CUDA events on that stream."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for fn in launches:
+            fn()
+    side.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for fn in launches:
+            fn()
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(side)
+        for _ in range(reps):
+            g.replay()
+        e1.record(side)
+    side.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (reps * len(launches))
+
+
+def op_level(dev) -> dict:
+    """BASELINE configs[1] and [2] at op level, each through the C ABI with
+    device-resident inputs, CUDA events over CUDA-graph replays:
+    - Q4_0 linear tn_q4_0_linear, bf16 activations (quantiser + linear), M in
+      {1, 4, 16, 128, 2048} on the three BASELINE (N, K) shapes; M <= 16 over
+      rotating weight copies (> L2) against HBM, M >= 128 against dense bf16;
+    - SDPA decode, the flash op at L = 1 on a KV-cache view, bf16, S in {1024,
+      8192, 32768} x B in {1, 8, 32}, against HBM (K/V bytes);
+    - SDPA prefill, causal bf16, B in {1, 4} x S in {512, 4096, 16384}, against
+      dense bf16 (causal flops)."""
+    import ctypes
+    import math
+
+    import torch
+
+    from torchnative_b200 import _native as N
+    from torchnative_b200.llama_decode import random_q4_blob as rq4
+
+    hbm, _ = measured_peaks()
+    tf = _measured_tflops()
+    P = ctypes.c_void_p
+    L = N.lib()
+    cur = lambda: P(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+    gen = torch.Generator(device=dev).manual_seed(11)
+    res = {"q4_linear": [], "sdpa_decode": [], "sdpa_prefill": []}
+    for (n, k) in ((14336, 4096), (4096, 14336), (6144, 4096)):
+        wb = q4_bytes(n, k)
+        copies = max(2, -(-300_000_000 // wb))
+        ws = [rq4(n, k, gen, dev) for _ in range(copies)]
+        for M in (1, 4, 16, 128, 2048):
+            x = torch.randn((M, k), device=dev, generator=gen).to(torch.bfloat16)
+            y = torch.empty((M, n), device=dev, dtype=torch.bfloat16)
+            use = ws if M <= 16 else ws[:1]
+            fns = [lambda w=w: N.check(L.tn_q4_0_linear(P(x.data_ptr()), N.TN_BF16, k, P(w.data_ptr()), None,
+                                                         P(y.data_ptr()), N.TN_BF16, M, n, k, N.TN_ACT_Q8_0, cur()))
+                   for w in use]
+            us = _time_graph(fns, 3, 10 if M <= 128 else 5)
+            kern = ("q4_gemv_q8_kernel" if M <= 8 else "q4_skinny_kernel" if M <= 32 else "q4_gemm_kernel")
+            algo = wb + M * k * 2 + M * n * 2
+            ent = {"M": M, "N": n, "K": k, "kernel": kern + " (+ Q8_0 activation quantiser)", "us": round(us, 2)}
+            if M <= 16:
+                ent.update({"GBps": round(algo / us / 1e3, 1), "frac_hbm": round(algo / us / 1e3 / hbm, 3)})
+            else:
+                tfl = 2.0 * M * n * k / us / 1e6
+                ent.update({"TFLOPs": round(tfl, 1), "frac_bf16": round(tfl / tf, 3)})
+            res["q4_linear"].append(ent)
+            del x, y
+        del ws
+        torch.cuda.empty_cache()
+    for S in (1024, 8192, 32768):
+        for B in (1, 8, 32):
+            cap = S + 64
+            kb = torch.randn((B, KV_HEADS, cap, HEAD_DIM), device=dev, generator=gen).to(torch.bfloat16)
+            vb = torch.randn((B, KV_HEADS, cap, HEAD_DIM), device=dev, generator=gen).to(torch.bfloat16)
+            q = torch.randn((B, HEADS, 1, HEAD_DIM), device=dev, generator=gen).to(torch.bfloat16)
+            out = torch.empty_like(q)
+            lse = torch.empty((B, HEADS, 1), device=dev)
+            qs = (ctypes.c_int64 * 4)(HEADS * HEAD_DIM, HEAD_DIM, 0, 1)
+            ks = (ctypes.c_int64 * 4)(*kb.stride())
+            fns = [lambda: N.check(L.tn_sdpa_flash_attention(P(q.data_ptr()), P(kb.data_ptr()), P(vb.data_ptr()), None,
+                                                             0, None, P(out.data_ptr()), P(lse.data_ptr()), N.TN_BF16,
+                                                             B, HEADS, KV_HEADS, 1, S, HEAD_DIM, qs, ks, ks, 0,
+                                                             1.0 / math.sqrt(HEAD_DIM), cur()))]
+            us = _time_graph(fns, 3, 20)
+            algo = 2 * B * KV_HEADS * S * HEAD_DIM * 2 + 2 * B * HEADS * HEAD_DIM * 2 + 4 * B * HEADS
+            res["sdpa_decode"].append({"B": B, "S": S, "kernel": "sdpa_decode_mma_kernel (split-KV + merge)",
+                                       "us": round(us, 2), "GBps": round(algo / us / 1e3, 1),
+                                       "frac_hbm": round(algo / us / 1e3 / hbm, 3)})
+            del kb, vb, q, out, lse
+        torch.cuda.empty_cache()
+    for B in (1, 4):
+        for S in (512, 4096, 16384):
+            q = torch.randn((B, HEADS, S, HEAD_DIM), device=dev, generator=gen).to(torch.bfloat16)
+            kk = torch.randn((B, KV_HEADS, S, HEAD_DIM), device=dev, generator=gen).to(torch.bfloat16)
+            vv = torch.randn((B, KV_HEADS, S, HEAD_DIM), device=dev, generator=gen).to(torch.bfloat16)
+            out = torch.empty_like(q)
+            lse = torch.empty((B, HEADS, S), device=dev)
+            qs = (ctypes.c_int64 * 4)(*q.stride())
+            ks = (ctypes.c_int64 * 4)(*kk.stride())
+            fns = [lambda: N.check(L.tn_sdpa_flash_attention(P(q.data_ptr()), P(kk.data_ptr()), P(vv.data_ptr()), None,
+                                                             0, None, P(out.data_ptr()), P(lse.data_ptr()), N.TN_BF16,
+                                                             B, HEADS, KV_HEADS, S, S, HEAD_DIM, qs, ks, ks, 1,
+                                                             1.0 / math.sqrt(HEAD_DIM), cur()))]
+            us = _time_graph(fns, 3, 10)
+            fl = 4.0 * B * HEADS * HEAD_DIM * S * (S + 1) / 2
+            tfl = fl / us / 1e6
+            res["sdpa_prefill"].append({"B": B, "S": S, "kernel": "sdpa_prefill2_kernel" if S > 128 else
+                                        "sdpa_prefill_kernel", "us": round(us, 2), "TFLOPs": round(tfl, 1),
+                                        "frac_bf16": round(tfl / tf, 3)})
+            del q, kk, vv, out, lse
+        torch.cuda.empty_cache()
+    res["decode_batch16"] = batched_decode(dev, 16)
+    N.device_status(reset=True)
+    return res
+
+
+def batched_decode(dev, B: int, steps: int = 10, warmup: int = 3) -> dict:
+    """BASELINE configs[3] at batch B on one GPU: the decode step of B
+    sequences (the batched path: tcgen05 skinny Q4_0 kernel from 9 rows),
+    replayed as one CUDA graph, CUDA events; tok/s and the step's HBM fraction."""
+    import torch
+
+    from torchnative_b200.llama_decode import LLAMA3_8B, Q4LlamaDecoder
+
+    cap = PROMPT + warmup + steps + 8
+    dec = Q4LlamaDecoder(LLAMA3_8B, batch=B, capacity=cap, device=dev, seed=99)
+    first = torch.randint(0, LLAMA3_8B.vocab, (B,), device=dev, dtype=torch.int32)
+    dec.fill_prompt_cache(PROMPT)
+    dec.start(first)
+    g = dec.capture()
+    dec.fill_prompt_cache(PROMPT)
+    dec.start(first)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    pos0 = int(dec.pos.item())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    hbm, _ = measured_peaks()
+    step_bytes = dec.weight_bytes + dec.kv_bytes(int(pos0 + (steps + 1) / 2))
+    out = {"batch": B, "tok_s": round(B * 1000.0 / ms, 1), "ms_per_step": round(ms, 4),
+           "step_hbm_frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 3), "bytes_per_step": step_bytes,
+           "kernels_per_step": dec.kernels_per_step}
+    dec._graph = None
+    del g
+    dec.close()
+    del dec
+    torch.cuda.empty_cache()
+    return out
+
+
+def _measured_tflops() -> float:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            return float(json.load(fh)["bf16_tflops"])
+    return 1590.0
 
 
 def run_reference(args, rank, world):
@@ -508,6 +708,10 @@ def main():
         return
     rank, world, local = dist_setup(args)
     res = run_ours(args, rank, world, local)
+    if rank == 0 and world == 1 and not args.no_ops:
+        import torch
+
+        res["op_level"] = op_level(torch.device("cuda", local))
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -10,8 +10,7 @@
  * the reference's wording where the reference has one.
  *
  * Each declaration names the reference interface it replaces (paths relative
- * to the torchnative project root). The Rust binding a maintainer adds to
- * torchnative/rust/torch_c is shown in INTEGRATION.md.
+ * to the torchnative project root), or says that it has none.
  */
 #ifndef TORCHNATIVE_B200_H
 #define TORCHNATIVE_B200_H
@@ -266,8 +265,12 @@ TN_API int tn_q4_0_linear_fused_q8out(int x_mode, const void *x, int64_t x_row_s
  * Limits: M <= TN_NOALLOC_MAX_ROWS and K <= TN_NOALLOC_MAX_IN; larger calls
  * return TN_ERR_SHAPE and allocate nothing. The first call on a device looks
  * up the array's device address (cudaGetSymbolAddress, that device current);
- * make it before any stream capture. All calls share the one array, so calls
- * that can overlap on the GPU (unordered streams) race. */
+ * make it before any stream capture. The address is cached for the context
+ * current at that call: it does not survive cudaDeviceReset or a switch to
+ * another context on the device. All calls share the one array, so calls
+ * that can overlap on the GPU (unordered streams) race. Counted in
+ * tn_counters.q4_linear_calls like tn_q4_0_linear. K == 0 is refused
+ * (TN_ERR_NOT_IMPLEMENTED) as tn_q4_0_linear refuses it. */
 #define TN_NOALLOC_MAX_ROWS 16
 #define TN_NOALLOC_MAX_IN 16384
 TN_API int tn_q4_0_linear_noalloc(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob,

@@ -459,17 +459,33 @@ static double load_elem(const void *p, int dtype, int64_t i) {
     }
 }
 
-static void sdpa_head_f32(const sdpa_job *j, int64_t b, int64_t h, float *sc) {
+/* The key/value rows of one head, widened to the accumulate type once per
+ * (b, h) so the score and output loops read contiguous memory; the
+ * arithmetic and its order are unchanged (each load_elem widening is exact). */
+static void widen_head(const sdpa_job *j, int64_t b, int64_t hk, float *kf, float *vf) {
+    for (int64_t t = 0; t < j->S; ++t)
+        for (int64_t d = 0; d < j->D; ++d) {
+            kf[t * j->D + d] = (float)load_elem(j->k, j->dtype, b * j->ks[0] + hk * j->ks[1] + t * j->ks[2] + d * j->ks[3]);
+            vf[t * j->D + d] = (float)load_elem(j->v, j->dtype, b * j->vs[0] + hk * j->vs[1] + t * j->vs[2] + d * j->vs[3]);
+        }
+}
+
+/* A row whose every score is -inf (no key to attend) answers zeros and a
+ * logsumexp of 0: upstream's CPU flash kernel and the reference's blocked
+ * kernel (torch_c/src/flash.rs:758-776: row_max -inf -> 0, row_sum 0 -> 1).
+ * The default branch as written would form exp(-inf - (-inf)) = NaN there. */
+static void sdpa_head_f32(const sdpa_job *j, int64_t b, int64_t h, float *sc, float *kf, float *vf, float *qf,
+                          float *of) {
     int64_t rep = j->Hq / j->Hkv, hk = h / rep;
     float scale = (float)j->scale; /* candle's affine casts its f64 multiplier to the dtype */
+    widen_head(j, b, hk, kf, vf);
     for (int64_t i = 0; i < j->L; ++i) {
+        for (int64_t d = 0; d < j->D; ++d)
+            qf[d] = (float)load_elem(j->q, j->dtype, b * j->qs[0] + h * j->qs[1] + i * j->qs[2] + d * j->qs[3]);
         for (int64_t t = 0; t < j->S; ++t) {
+            const float *kr = kf + t * j->D;
             float s = 0.0f;
-            for (int64_t d = 0; d < j->D; ++d) {
-                float a = (float)load_elem(j->q, j->dtype, b * j->qs[0] + h * j->qs[1] + i * j->qs[2] + d * j->qs[3]);
-                float c = (float)load_elem(j->k, j->dtype, b * j->ks[0] + hk * j->ks[1] + t * j->ks[2] + d * j->ks[3]);
-                s += a * c;
-            }
+            for (int64_t d = 0; d < j->D; ++d) s += qf[d] * kr[d];
             if (j->causal && t > i)
                 s = s * scale + (-INFINITY);
             else
@@ -481,29 +497,35 @@ static void sdpa_head_f32(const sdpa_job *j, int64_t b, int64_t h, float *sc) {
         }
         float mx = -INFINITY;
         for (int64_t t = 0; t < j->S; ++t) mx = sc[t] > mx ? sc[t] : mx;
-        float sum = 0.0f;
-        for (int64_t t = 0; t < j->S; ++t) {
-            sc[t] = expf(sc[t] - mx);
-            sum += sc[t];
-        }
-        for (int64_t t = 0; t < j->S; ++t) sc[t] = sc[t] / sum;
         int64_t orow = ((b * j->Hq + h) * j->L + i) * j->D;
-        for (int64_t d = 0; d < j->D; ++d) {
-            float o = 0.0f;
-            for (int64_t t = 0; t < j->S; ++t)
-                o += sc[t] * (float)load_elem(j->v, j->dtype, b * j->vs[0] + hk * j->vs[1] + t * j->vs[2] + d * j->vs[3]);
-            if (j->dtype == 0)
-                ((float *)j->out)[orow + d] = o;
-            else if (j->dtype == 1)
-                ((uint16_t *)j->out)[orow + d] = tno_f32_to_f16(o);
-            else
-                ((uint16_t *)j->out)[orow + d] = tno_f32_to_bf16(o);
+        float sum = 0.0f;
+        if (mx == -INFINITY) {
+            for (int64_t d = 0; d < j->D; ++d) of[d] = 0.0f;
+        } else {
+            for (int64_t t = 0; t < j->S; ++t) {
+                sc[t] = expf(sc[t] - mx);
+                sum += sc[t];
+            }
+            for (int64_t t = 0; t < j->S; ++t) sc[t] = sc[t] / sum;
+            for (int64_t d = 0; d < j->D; ++d) of[d] = 0.0f;
+            for (int64_t t = 0; t < j->S; ++t) {
+                const float *vr = vf + t * j->D;
+                for (int64_t d = 0; d < j->D; ++d) of[d] += sc[t] * vr[d];
+            }
         }
-        ((float *)j->lse)[(b * j->Hq + h) * j->L + i] = logf(sum) + mx;
+        for (int64_t d = 0; d < j->D; ++d) {
+            if (j->dtype == 0)
+                ((float *)j->out)[orow + d] = of[d];
+            else if (j->dtype == 1)
+                ((uint16_t *)j->out)[orow + d] = tno_f32_to_f16(of[d]);
+            else
+                ((uint16_t *)j->out)[orow + d] = tno_f32_to_bf16(of[d]);
+        }
+        ((float *)j->lse)[(b * j->Hq + h) * j->L + i] = (mx == -INFINITY) ? 0.0f : logf(sum) + mx;
     }
 }
 
-static void sdpa_head_f64(const sdpa_job *j, int64_t b, int64_t h, double *sc) {
+static void sdpa_head_f64(const sdpa_job *j, int64_t b, int64_t h, double *sc, double *of) {
     int64_t rep = j->Hq / j->Hkv, hk = h / rep;
     double scale = j->scale;
     for (int64_t i = 0; i < j->L; ++i) {
@@ -523,33 +545,46 @@ static void sdpa_head_f64(const sdpa_job *j, int64_t b, int64_t h, double *sc) {
         double mx = -INFINITY;
         for (int64_t t = 0; t < j->S; ++t) mx = sc[t] > mx ? sc[t] : mx;
         double sum = 0.0;
-        for (int64_t t = 0; t < j->S; ++t) {
-            sc[t] = exp(sc[t] - mx);
-            sum += sc[t];
-        }
-        for (int64_t t = 0; t < j->S; ++t) sc[t] = sc[t] / sum;
         int64_t orow = ((b * j->Hq + h) * j->L + i) * j->D;
-        for (int64_t d = 0; d < j->D; ++d) {
-            double o = 0.0;
+        for (int64_t d = 0; d < j->D; ++d) of[d] = 0.0;
+        if (mx != -INFINITY) {
+            for (int64_t t = 0; t < j->S; ++t) {
+                sc[t] = exp(sc[t] - mx);
+                sum += sc[t];
+            }
+            for (int64_t t = 0; t < j->S; ++t) sc[t] = sc[t] / sum;
             for (int64_t t = 0; t < j->S; ++t)
-                o += sc[t] * load_elem(j->v, 3, b * j->vs[0] + hk * j->vs[1] + t * j->vs[2] + d * j->vs[3]);
-            ((double *)j->out)[orow + d] = o;
+                for (int64_t d = 0; d < j->D; ++d)
+                    of[d] += sc[t] * load_elem(j->v, 3, b * j->vs[0] + hk * j->vs[1] + t * j->vs[2] + d * j->vs[3]);
         }
-        ((double *)j->lse)[(b * j->Hq + h) * j->L + i] = log(sum) + mx;
+        for (int64_t d = 0; d < j->D; ++d) ((double *)j->out)[orow + d] = of[d];
+        ((double *)j->lse)[(b * j->Hq + h) * j->L + i] = (mx == -INFINITY) ? 0.0 : log(sum) + mx;
     }
 }
 
 static void *sdpa_worker(void *arg) {
     sdpa_job *j = (sdpa_job *)arg;
-    void *sc = malloc((size_t)(j->S > 0 ? j->S : 1) * 8);
+    const size_t S1 = (size_t)(j->S > 0 ? j->S : 1), D1 = (size_t)(j->D > 0 ? j->D : 1);
+    void *sc = malloc(S1 * 8);
+    double *of64 = (double *)malloc(D1 * 8);
+    float *kf = NULL, *vf = NULL, *qf = (float *)malloc(D1 * 4), *of = (float *)malloc(D1 * 4);
+    if (j->dtype != 3) {
+        kf = (float *)malloc(S1 * D1 * 4);
+        vf = (float *)malloc(S1 * D1 * 4);
+    }
     for (int64_t bh = j->bh_begin; bh < j->bh_end; ++bh) {
         int64_t b = bh / j->Hq, h = bh % j->Hq;
         if (j->dtype == 3)
-            sdpa_head_f64(j, b, h, (double *)sc);
+            sdpa_head_f64(j, b, h, (double *)sc, of64);
         else
-            sdpa_head_f32(j, b, h, (float *)sc);
+            sdpa_head_f32(j, b, h, (float *)sc, kf, vf, qf, of);
     }
     free(sc);
+    free(of64);
+    free(kf);
+    free(vf);
+    free(qf);
+    free(of);
     return NULL;
 }
 

@@ -41,3 +41,40 @@ def test_oracle_reads_a_kv_cache_view_in_place():
     ref, ref_lse = sdpa_ref.f64_reference(q.astype(np.float64), k.astype(np.float64), v.astype(np.float64),
                                           False, None)
     assert np.max(np.abs(o1 - ref)) < 1e-5 and np.max(np.abs(l1 - ref_lse)) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16", "float64"])
+def test_oracle_fully_masked_rows_answer_zeros_and_lse_zero(dtype):
+    """A query row whose every key is masked (-inf) gets zeros and a
+    logsumexp of 0: what upstream torch's CPU flash kernel returns, and what the
+    reference's blocked kernel reproduces (torch_c/src/flash.rs:758-776). The
+    other rows of the same call are untouched by the rule."""
+    import torch
+
+    tdt = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16,
+           "float64": torch.float64}[dtype]
+    g = torch.Generator().manual_seed(9)
+    q = torch.randn((1, 4, 5, 64), generator=g).to(tdt)
+    k = torch.randn((1, 2, 7, 64), generator=g).to(tdt)
+    v = torch.randn((1, 2, 7, 64), generator=g).to(tdt)
+    mask = torch.zeros((1, 4, 5, 7), dtype=tdt)
+    mask[0, 1, 2, :] = float("-inf")
+    mask[0, 3, :, :] = float("-inf")
+    mask[0, 0, 4, 3] = float("-inf")
+    kk, vv = k.repeat_interleave(2, 1), v.repeat_interleave(2, 1)
+    want, want_lse = torch.ops.aten._scaled_dot_product_flash_attention_for_cpu(q, kk, vv, 0.0, False,
+                                                                                attn_mask=mask)[:2]
+
+    def st(t):
+        return t.view(torch.int16).numpy().view(np.uint16) if dtype == "bfloat16" else t.numpy()
+
+    out, lse = oracle.sdpa(st(q), st(k), st(v), dtype=dtype, attn_mask=st(mask), mask_dtype=dtype)
+    out = sdpa_ref.from_storage(out, dtype)
+    assert not np.isnan(out).any() and not np.isnan(lse).any()
+    assert (out[0, 1, 2] == 0).all() and (out[0, 3] == 0).all()
+    assert lse[0, 1, 2] == 0 and (lse[0, 3] == 0).all()
+    assert (want.double().numpy()[0, 3] == 0).all() and (want_lse.double().numpy()[0, 3] == 0).all()
+    tol = sdpa_ref.TOL[dtype]
+    assert sdpa_ref.isclose_all(out, want.double().numpy(), tol)
+    assert sdpa_ref.isclose_all(lse, want_lse.double().numpy(), sdpa_ref.TOL["float64" if dtype == "float64"
+                                                                               else "float32"])

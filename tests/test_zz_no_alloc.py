@@ -87,3 +87,48 @@ def test_noalloc_allocates_nothing_and_refuses_oversize(lib, cuda_device):
     big = torch.randn((17, K), device=cuda_device)
     with pytest.raises(RuntimeError, match="exceed its fixed scratch"):
         _call(lib, "tn_q4_0_linear_noalloc", big, w, torch.empty((17, Nout), device=cuda_device), 17, Nout, K)
+
+
+def test_noalloc_refuses_zero_in_features_and_counts_its_calls(lib, cuda_device):
+    """K == 0 is refused by name (as tn_q4_0_linear refuses it) instead of
+    reaching the kernel planner, and every call counts as a Q4 linear call."""
+    x = torch.zeros((1, 32), device=cuda_device)
+    w = torch.zeros(8 * 18, dtype=torch.uint8, device=cuda_device)
+    y = torch.zeros((1, 8), device=cuda_device)
+    before = lib.counters()["q4_linear_calls"]
+    stream = P(torch.cuda.current_stream().cuda_stream)
+    st = lib.lib().tn_q4_0_linear_noalloc(P(x.data_ptr()), lib.TN_F32, 0, P(w.data_ptr()), None, P(y.data_ptr()),
+                                          lib.TN_F32, 1, 8, 0, stream)
+    assert st == lib.TN_ERR_NOT_IMPLEMENTED
+    assert "in_features == 0" in lib.last_error()
+    assert lib.counters()["q4_linear_calls"] == before + 1
+
+
+def test_noalloc_at_its_limits_bf16_bias_and_strided_rows(lib, cuda_device):
+    """The largest call the fixed array takes (16 rows of 16384), bf16 in and
+    out, a float32 bias and a row stride wider than K: the decode GEMV then
+    runs in row chunks at several offsets into the array. Checked twice in a
+    row against the counted bound of the exact value (the bf16 output adds
+    one rounding: half a bf16 ulp of the result)."""
+    M, Nout, K, stride = 16, 300, 16384, 16384 + 64
+    rng = np.random.default_rng(99)
+    blob = q4_exact.random_q4_0_blob(rng, Nout, K)
+    w = torch.frombuffer(bytearray(blob), dtype=torch.uint8).to(cuda_device)
+    bias_np = rng.standard_normal(Nout).astype(np.float32)
+    bias = torch.from_numpy(bias_np).to(cuda_device)
+    stream = P(torch.cuda.current_stream().cuda_stream)
+    for call in range(2):
+        xs = torch.from_numpy((rng.standard_normal((M, stride)) * (1 + call)).astype(np.float32))
+        xb = xs.to(torch.bfloat16).to(cuda_device)
+        y = torch.full((M, Nout), float("nan"), device=cuda_device, dtype=torch.bfloat16)
+        lib.check(lib.lib().tn_q4_0_linear_noalloc(P(xb.data_ptr()), lib.TN_BF16, stride, P(w.data_ptr()),
+                                                   P(bias.data_ptr()), P(y.data_ptr()), lib.TN_BF16, M, Nout, K,
+                                                   stream))
+        torch.cuda.synchronize()
+        x_np = xb[:, :K].float().cpu().numpy()
+        exact, abs_sum, ref_err = q4_exact.exact_linear_q4_0(oracle.q8_0_quantize(x_np), blob, M, Nout, K)
+        exact = exact + bias_np.astype(np.float64)
+        bound = q4_exact.linear_bound(K, abs_sum + np.abs(bias_np), ref_err) + np.abs(exact) * 2.0 ** -8
+        got = y.float().cpu().numpy().astype(np.float64)
+        assert float(np.max(np.abs(got - exact) / bound)) <= 1.0, f"call {call}"
+    lib.device_status(reset=True)

@@ -1123,6 +1123,7 @@ Plan plan_slots(int M, int nbp, int rowbytes, bool staged, size_t budget, size_t
     while (wpc > 1 && rpw * wpc * rowbytes > 24 * 1024) wpc >>= 1;
     const int groups = kConsumerWarps / wpc;
     const int slot_bytes = rpw * wpc * rowbytes;
+    if (slot_bytes <= 0) return pl;  // no weight bytes to stage (K == 0): no plan
     if (base + (size_t)groups * slot_bytes > budget) return pl;
     int nslots = (int)((budget - base) / slot_bytes);
     const int want = (int)((in_flight + slot_bytes - 1) / slot_bytes);

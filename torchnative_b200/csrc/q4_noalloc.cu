@@ -15,6 +15,10 @@
 // shadow object, not device memory. The device address is looked up once per
 // device with cudaGetSymbolAddress, with that device current, on the first call
 // made on that device; make that first call before any stream capture begins.
+// The cached address belongs to the CUDA context that was current at that first
+// call: after cudaDeviceReset, or when another context is made current on the
+// same device, the cache is stale, so those hosts must not use this entry
+// point across such a change.
 //
 // Every call shares the one array and leaves its contents behind. Nothing in it
 // has to start at zero: each call's quantiser writes every code, scale and
@@ -77,7 +81,9 @@ extern "C" int tn_q4_0_linear_noalloc(const void *x, int x_dtype, int64_t x_row_
                                                " exceed its fixed scratch (M <= " + std::to_string(kRowsMax) +
                                                ", K <= " + std::to_string(kInMax) +
                                                "); call tn_q4_0_linear, which allocates");
+    __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
     if (M == 0 || N == 0) return TN_OK;
+    if (K == 0) return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": in_features == 0 is not implemented");
     if (!x || !w_blob || !y) return tn::set_error(TN_ERR_INVALID, op + ": null device pointer");
     if (x_row_stride < K) return tn::set_error(TN_ERR_INVALID, op + ": activation row stride smaller than in_features");
     if ((reinterpret_cast<uintptr_t>(w_blob) & 1) != 0)

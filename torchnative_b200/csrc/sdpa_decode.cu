@@ -175,7 +175,8 @@ __device__ __forceinline__ void merge_if_last(const SdpaParams &p, int b, int kv
             for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
             if (lane == 0) {
                 lsm[r] = den;
-                if (p.lse) p.lse[row] = logf(den) + M;
+                // no key seen by any split: zeros and lse 0 (flash.rs:758-776)
+                if (p.lse) p.lse[row] = (den == 0.0f) ? 0.0f : logf(den) + M;
             }
         }
     }
@@ -210,7 +211,7 @@ __device__ __forceinline__ void merge_if_last(const SdpaParams &p, int b, int kv
                 acc.w = fmaf(w, o.w, acc.w);
             }
         }
-        const float inv = 1.0f / lsm[r];
+        const float inv = (lsm[r] == 0.0f) ? 0.0f : 1.0f / lsm[r];
         const float v4[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -526,7 +527,7 @@ __global__ void __launch_bounds__(128) sdpa_combine_kernel(const SdpaParams p) {
     }
     // softmax divides each weight by the sum (aten.rs:10406); here the sum is
     // applied once to the accumulated row
-    const float inv_den = 1.0f / den;
+    const float inv_den = (den == 0.0f) ? 0.0f : 1.0f / den;  // no key seen: zeros (flash.rs:758-776)
 #pragma unroll
     for (int e = 0; e < PER; ++e) {
         const float v = acc[e] * inv_den;
@@ -538,7 +539,7 @@ __global__ void __launch_bounds__(128) sdpa_combine_kernel(const SdpaParams p) {
         else
             static_cast<__half *>(p.out)[oi] = __float2half_rn(v);
     }
-    if (lane == 0 && p.lse) p.lse[row] = logf(den) + M;
+    if (lane == 0 && p.lse) p.lse[row] = (den == 0.0f) ? 0.0f : logf(den) + M;
 }
 
 // ---------------------------------------------------------------------------

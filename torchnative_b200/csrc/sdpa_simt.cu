@@ -190,14 +190,17 @@ __global__ void __launch_bounds__(SM_THREADS) sdpa_simt_kernel(const SdpaParams 
     __syncthreads();
     if ((tid & 3) == 0) {
         rowstat[sr] = l_run;
-        if (p.lse && q0 + sr < p.L) p.lse[((int64_t)b * p.Hq + hq) * p.L + q0 + sr] = logf(l_run) + m_run;
+        // a row that sees no key (every score -inf) answers zeros and lse 0,
+        // as upstream and the reference's blocked kernel do (flash.rs:758-776)
+        if (p.lse && q0 + sr < p.L)
+            p.lse[((int64_t)b * p.Hq + hq) * p.L + q0 + sr] = (l_run == 0.0f) ? 0.0f : logf(l_run) + m_run;
     }
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int row = q0 + ri + i;
         if (row >= p.L) continue;
-        const float inv = 1.0f / rowstat[ri + i];
+        const float inv = (rowstat[ri + i] == 0.0f) ? 0.0f : 1.0f / rowstat[ri + i];
         const int64_t oi = (((int64_t)b * p.Hq + hq) * p.L + row) * D + pd;
 #pragma unroll
         for (int e = 0; e < DC; ++e) {

@@ -242,6 +242,65 @@ class QuantizedLinear(torch.nn.Module):
         out_features, in_features = mod.weight.shape
         return cls(in_features, out_features, _quantize(mod.weight, fmt), mod.bias, fmt)
 
+    @classmethod
+    def pending_from_linear(cls, mod: torch.nn.Linear, fmt: str = "q4_0", shard: tuple[int, int] | None = None):
+        """The load-time swap (quant/__init__.py:154-181 of the reference): the
+        layer is replaced before its weight exists (a meta tensor during
+        `from_pretrained`), keeping the loader's `weight` entry registered until
+        `adopt` receives the tensor. `shard = (rank, world)` makes this the
+        tensor-parallel load point: the layer keeps only output rows
+        [rank * out / world, (rank + 1) * out / world) of whatever arrives, the
+        column shard of a Q4_0 linear (a row range of a GGML blob is a byte
+        range, so nothing is re-quantised)."""
+        out_features, in_features = mod.weight.shape
+        if shard is not None:
+            rank, world = shard
+            if world < 1 or not 0 <= rank < world or out_features % world != 0:
+                raise ValueError(f"cannot shard {out_features} output rows {world} ways (rank {rank})")
+            out_features //= world
+        bias = mod.bias
+        if bias is not None and shard is not None and bias.device.type != "meta":
+            bias = bias.detach()[shard[0] * out_features:(shard[0] + 1) * out_features]
+        self = cls(in_features, out_features, None, bias, fmt)
+        self.shard = shard
+        self.register_parameter("weight", mod.weight)
+        return self
+
+    def adopt(self, weight):
+        """Take the arriving weight once (quant/__init__.py:183-237 of the
+        reference): a dense tensor is quantised here (on its device, so the
+        dense copy lives only for this call); an already block-quantised
+        QTensor (a GGUF file's own blocks) is kept byte for byte. Under a
+        tensor-parallel shard only this rank's rows are kept, sliced out of the
+        dense rows before quantisation or out of the blob's rows as bytes."""
+        if self.qweight is not None:
+            raise ValueError(f"{type(self).__name__} already holds a quantised weight; adopt() is for the loading "
+                             "placeholder and runs once.")
+        if hasattr(weight, "qweight") and not isinstance(weight, QTensor):
+            weight = weight.qweight
+        shard = getattr(self, "shard", None)
+        rows = self.out_features * (shard[1] if shard else 1)
+        if isinstance(weight, QTensor):
+            if tuple(weight.shape) != (rows, self.in_features):
+                raise ValueError(f"pre-quantised weight shape {tuple(weight.shape)} does not match "
+                                 f"({rows}, {self.in_features})")
+            if shard is not None:
+                row_bytes = weight.blob.numel() // rows
+                r0 = shard[0] * self.out_features
+                blob = weight.blob.view(rows, row_bytes)[r0:r0 + self.out_features].reshape(-1).contiguous()
+                weight = QTensor(blob, (self.out_features, self.in_features), weight.format)
+            self.qweight = weight
+            self.format = weight.format
+        else:
+            if tuple(weight.shape) != (rows, self.in_features):
+                raise ValueError(f"weight shape {tuple(weight.shape)} does not match ({rows}, {self.in_features})")
+            if shard is not None:
+                r0 = shard[0] * self.out_features
+                weight = weight[r0:r0 + self.out_features]
+            self.qweight = _quantize(weight, self.format)
+        if "weight" in self._parameters:
+            del self._parameters["weight"]
+
     def _apply(self, fn, recurse=True):
         result = super()._apply(fn, recurse)
         if self.qweight is not None:
@@ -258,3 +317,58 @@ class QuantizedLinear(torch.nn.Module):
     def extra_repr(self):
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
                 f"bias={self.bias is not None}, format={self.format}")
+
+
+class QuantizeReport:
+    """What `quantize_` replaced and what it skipped (with the reason), and the
+    bytes on both sides (the reference's _Report, quant/__init__.py:255-298)."""
+
+    def __init__(self, fmt: str):
+        self.format = fmt
+        self.replaced: list[str] = []
+        self.skipped: list[tuple[str, str]] = []
+        self.dense_bytes = 0
+        self.quantized_bytes = 0
+
+    @property
+    def ratio(self) -> float:
+        return self.quantized_bytes / self.dense_bytes if self.dense_bytes else float("nan")
+
+    def __str__(self):
+        return (f"quantize_({self.format}): {len(self.replaced)} linears replaced, {len(self.skipped)} skipped, "
+                f"{self.dense_bytes} -> {self.quantized_bytes} bytes")
+
+
+def quantize_(model: torch.nn.Module, format: str = "q4_0", predicate=None) -> QuantizeReport:
+    """Swap every `nn.Linear` of `model` (on a CUDA device) for a
+    `QuantizedLinear` in place, as the reference's `quantize_`
+    (quant/__init__.py:300-365) does: `predicate(name, module)` narrows the
+    choice, `lm_head` is not special-cased, a layer the format refuses is
+    skipped with its reason, and a call that finds nothing to replace raises."""
+    report = QuantizeReport(format)
+    todo = []
+    for name, module in model.named_modules():
+        for child_name, child in module.named_children():
+            if not isinstance(child, torch.nn.Linear):
+                continue
+            full = f"{name}.{child_name}" if name else child_name
+            if predicate is not None and not predicate(full, child):
+                report.skipped.append((full, "excluded by predicate"))
+                continue
+            todo.append((module, child_name, full, child))
+    for parent, child_name, full, child in todo:
+        try:
+            q = QuantizedLinear.from_linear(child, format)
+        except NotImplementedError as exc:
+            report.skipped.append((full, str(exc).split(": ", 1)[-1]))
+            continue
+        setattr(parent, child_name, q)
+        report.replaced.append(full)
+        report.dense_bytes += child.weight.numel() * child.weight.element_size()
+        report.quantized_bytes += q.qweight.nbytes()
+    if not report.replaced and not report.skipped:
+        if isinstance(model, torch.nn.Linear):
+            raise ValueError("quantize_ replaces the children of the module it is given, not the module itself: "
+                             "assign `parent.name = QuantizedLinear.from_linear(parent.name, fmt)` instead")
+        raise ValueError(f"quantize_ found no nn.Linear to replace in {type(model).__name__}; nothing was quantised")
+    return report
