@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ops", action="store_true", help="skip the op-level BASELINE figures (configs[1], [2])")
+    ap.add_argument("--mega", action="store_true", help="run the step as the one persistent kernel per token "
+                                                        "(tn_llama_decode_token) instead of the launch-per-operator graph")
     ap.add_argument("--case", default=None, choices=["gemv", "gemm", "sdpa_decode", "sdpa_prefill"],
                     help="kernel-level case instead of the decode step: 'gemv' times the decode GEMV alone on the "
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
@@ -206,10 +208,10 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def committed_traffic():
+def committed_traffic(name: str = "q4_gemv_traffic.json"):
     """dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
-    kernel, from the committed ncu summary (profiles/q4_gemv_traffic.json)."""
-    p = os.path.join(ROOT, "profiles", "q4_gemv_traffic.json")
+    kernel, from the committed ncu summary under profiles/ (None without one)."""
+    p = os.path.join(ROOT, "profiles", name)
     if os.path.exists(p):
         with open(p) as fh:
             return json.load(fh).get("bytes_per_launch")
@@ -283,7 +285,8 @@ def run_ours(args, rank, world, local):
         from torchnative_b200.tp import TPGroup
 
         tp = TPGroup(rank, world, dist.group.WORLD)
-    dec = Q4LlamaDecoder(LLAMA3_8B, batch=B, capacity=cap, device=dev, seed=1234, tp=tp, exchange=args.exchange)
+    dec = Q4LlamaDecoder(LLAMA3_8B, batch=B, capacity=cap, device=dev, seed=1234, tp=tp, exchange=args.exchange,
+                         mega=True if (args.mega and world == 1 and B == 1) else None)
     P = ctypes.c_void_p
     cur = lambda: P(torch.cuda.current_stream().cuda_stream)  # noqa: E731
     first = torch.randint(0, LLAMA3_8B.vocab, (B,), device=dev, dtype=torch.int32)
@@ -305,15 +308,17 @@ def run_ours(args, rank, world, local):
                 P(lw["gate_up"].data_ptr()), None, P(dec.act_l.data_ptr()), _native.TN_BF16, B, 2 * dec.i_l, HIDDEN,
                 _native.TN_WEIGHTS_STATIC | _native.TN_EPILOGUE_SILU_MUL_PAIRS, cur()))
 
-    gs = torch.cuda.Stream(dev)
-    gs.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(gs):
-        gate_up_layers()
-    gs.synchronize()
-    gd = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gd, stream=gs):
-        gate_up_layers()
-    torch.cuda.current_stream(dev).wait_stream(gs)
+    gd = None
+    if not dec.mega:
+        gs = torch.cuda.Stream(dev)
+        gs.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(gs):
+            gate_up_layers()
+        gs.synchronize()
+        gd = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gd, stream=gs):
+            gate_up_layers()
+        torch.cuda.current_stream(dev).wait_stream(gs)
 
     for _ in range(args.warmup):
         g.replay()
@@ -360,17 +365,19 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
 
-    for _ in range(3):
-        gd.replay()
-    torch.cuda.synchronize()
-    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 10
-    d0.record()
-    for _ in range(reps):
-        gd.replay()
-    d1.record()
-    torch.cuda.synchronize()
-    dom_us = d0.elapsed_time(d1) * 1e3 / (reps * LAYERS)
+    dom_us = ms * 1e3
+    if gd is not None:
+        for _ in range(3):
+            gd.replay()
+        torch.cuda.synchronize()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        d0.record()
+        for _ in range(reps):
+            gd.replay()
+        d1.record()
+        torch.cuda.synchronize()
+        dom_us = d0.elapsed_time(d1) * 1e3 / (reps * LAYERS)
     # the step's parts, each as 32 back-to-back launches (one per layer)
     kernel_us = {}
     for name, kg in dec.kernel_graphs().items():
@@ -390,7 +397,14 @@ def run_ours(args, rank, world, local):
     # the dominant launch as the step runs it: on one GPU at batch <= 4 the
     # RMSNorm-prologue gate/up GEMV with the SiLU*up epilogue writing act's
     # planar Q8_0 (bf16 h and delta in, norm weight, weights, act + its Q8 out)
-    if "gate_up_rmsnorm_gemv_silu_q8" in kernel_us:
+    step_bytes = dec.weight_bytes + dec.kv_bytes(int(mean_ctx))
+    if dec.mega:
+        # the whole token is one launch: its algorithmic bytes are the step's
+        # (every weight byte once, the K/V of the mean context, the small
+        # activations and logits), its time the step's
+        dom_name = "decode_mega_kernel (the whole token: 32 layers + lm_head + argmax, one persistent launch)"
+        algo = step_bytes
+    elif "gate_up_rmsnorm_gemv_silu_q8" in kernel_us:
         dom_us = kernel_us["gate_up_rmsnorm_gemv_silu_q8"]
         dom_name = "q4_gemv_q8_kernel<X_NORM> (gate/up as the step runs it: RMSNorm prologue, SiLU*up epilogue, planar Q8_0 out)"
         algo = q4_bytes(n, k) + B * k * 2 * 3 + k * 2 + B * (n // 2) * (2 + 1) + B * (n // 64) * 8
@@ -398,7 +412,6 @@ def run_ours(args, rank, world, local):
         dom_name = f"{'q4_skinny_kernel' if 9 <= B <= 32 else 'q4_gemv_q8_kernel'} (gate/up {n}x{k} on this rank, SiLU*up epilogue)"
         algo = q4_bytes(n, k) + B * (k + k // 32 * 8) + B * (n // 2) * 2
     achieved = algo / (dom_us * 1e-6) / 1e9
-    step_bytes = dec.weight_bytes + dec.kv_bytes(int(mean_ctx))
     per_kernel = {}
     if kernel_us:
         ctx = int(mean_ctx)
@@ -430,7 +443,7 @@ def run_ours(args, rank, world, local):
         "data": "synthetic: random Q4_0 weights (codes U[-8,7], scales f16(|N(0,1)|*0.01)), bf16 norms/embeddings, "
                 "N(0,1) prompt KV cache",
         "config": {"workload": f"Llama-3-8B-shaped Q4_0 greedy decode step, batch {B}, {PROMPT}-token prompt cache "
-                               "growing one slot per step; one CUDA graph per token",
+                               "growing one slot per step",
                    "model": "Llama-3-8B-shaped (32 layers, 4096 hidden, 32/8 heads, D 128, MLP 14336, vocab 128256)",
                    "global_batch": B, "seq_len": PROMPT,
                    "parallelism": f"tp{world} (column-sharded Q4_0 linears, KV-head-group attention, "
@@ -442,7 +455,8 @@ def run_ours(args, rank, world, local):
         "roofline": {"bound": "hbm", "kernel": dom_name,
                      "achieved": achieved,
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": scaled_traffic(n), "algorithmic_bytes": algo, "avg_launch_us": dom_us},
+                     "traffic": (committed_traffic("decode_mega_traffic.json") if dec.mega else scaled_traffic(n)),
+                     "algorithmic_bytes": algo, "avg_launch_us": dom_us},
         "step_hbm_frac": (step_bytes / (ms * 1e-3) / 1e9) / peak,
         "kernel_us_back_to_back": kernel_us,
         "per_kernel": per_kernel,
@@ -451,6 +465,8 @@ def run_ours(args, rank, world, local):
         "gpu_launches": dec.kernels_per_step * args.steps,
         "clocks": clocks.summary(),
     }
+    result["config"]["step_kernel"] = ("one persistent kernel per token (tn_llama_decode_token)" if dec.mega else
+                                       f"{dec.kernels_per_step} launches per token in one CUDA graph")
     # graphs holding NCCL calls go before the process group does; no rank frees
     # its exchange region while a peer may still write it
     dec._graph = None

@@ -73,6 +73,21 @@ TN_API int tn_device_info(int device, int *sm_count, int *cc_major, int *cc_mino
  * when reset != 0). No reference counterpart (candle's kernels never wait). */
 TN_API int tn_device_status(int reset);
 
+/* The budget (GPU clock cycles, default 2^31, ~1 s) that every bounded wait of
+ * these kernels on the current device allows before it gives up and records
+ * TN_ERR_TIMEOUT; cycles <= 0 restores the default. *previous (if not NULL)
+ * receives the budget in force. For tests and failure drills: a short budget
+ * makes a wait on a peer that never signals end quickly. No reference
+ * counterpart. */
+TN_API int tn_set_wait_budget(int64_t cycles, int64_t *previous);
+
+/* The stream calls on `device` run on when they pass stream == NULL (the
+ * reference's one CudaStream per device, vendor/candle-core/src/cuda_backend/
+ * device.rs:388-389); default NULL, the legacy default stream. Every entry
+ * point given a non-NULL stream uses that one. */
+TN_API int tn_stream_set(int device, void *stream);
+TN_API int tn_stream_get(int device, void **stream);
+
 /* Caching device allocator (replaces candle's per-tensor cudarc alloc,
  * vendor/candle-core/src/cuda_backend/device.rs:78-90). Blocks are reused
  * for requests of the same rounded size on the same stream; tn_empty_cache
@@ -96,7 +111,10 @@ typedef struct {
     uint64_t sdpa_prefill_launches;
     uint64_t bytes_allocated;
     uint64_t q4_skinny_launches;   /* batched-decode (9..32 rows) tensor-core launches */
-    uint64_t reserved[5];
+    uint64_t decode_token_launches; /* persistent whole-token decode kernels (tn_llama_decode_token) */
+    uint64_t refusals;             /* calls refused by name (TN_ERR_NOT_IMPLEMENTED) */
+    uint64_t resolves;             /* devices resolved (first use of a device's facts) */
+    uint64_t reserved[2];
 } tn_counters;
 TN_API int tn_get_counters(tn_counters *out);
 TN_API int tn_reset_counters(void);
@@ -371,6 +389,82 @@ TN_API int tn_llama_argmax_embed(const void *logits, int64_t rows, int64_t V, in
 /* h[r] = embed[tokens[r]]. */
 TN_API int tn_llama_embed(const int *tokens, int64_t rows, const void *embed, int64_t H, void *h,
                           void *stream);
+
+/* ---- one greedy decode token in one persistent kernel (batch 1) ---------------
+ * The whole token of a Llama-shaped Q4_0 model -- per layer RMSNorm + q/k/v,
+ * RoPE + KV append + attention, o_proj + residual, RMSNorm + gate/up +
+ * SiLU*up, down_proj + residual; then the final norm, lm_head and argmax --
+ * as ONE launch of one CTA per SM. Each CTA streams its rows of every weight
+ * matrix and its split of every layer's past K/V through a bulk-copy ring
+ * while its math waits on grid-wide phase barriers for activations only.
+ * Same arithmetic per operator as the separate kernels (Q8_0 activations and
+ * exact integer block dots for every Q4_0 linear, k_quants.rs:312-330; the
+ * default SDPA arithmetic, aten.rs:10327-10420). No reference counterpart as
+ * one call: the reference runs these as transformers' modules around
+ * _quantized_linear (quant.rs:286-369) and the flash op (aten.rs:10092), one
+ * op at a time.
+ *
+ * The model: every pointer device memory except the per-layer arrays, which
+ * are host arrays of `layers` device pointers. Q4_0 blobs as tn_q4_0_linear
+ * reads them (16-byte aligned); qkv rows are q heads, then k heads, then v
+ * heads; gate_up rows interleave gate_proj and up_proj row by row; caches are
+ * bf16 [1][kv_heads][capacity][head_dim]; norms and the embedding bf16;
+ * inv_freq f32 [head_dim / 2]. Supported: head_dim 128, heads = 4 kv_heads,
+ * hidden and inter multiples of 256 (hidden <= 7680, inter <= 16384). */
+typedef struct {
+    int32_t layers, hidden, inter, heads, kv_heads, head_dim, vocab;
+    float eps;
+    const void *embed, *final_norm, *lm_head;
+    const void *const *attn_norm, *const *qkv, *const *o, *const *mlp_norm, *const *gate_up, *const *down;
+    void *const *k_cache, *const *v_cache;
+    int64_t capacity;
+    const float *inv_freq;
+} tn_llama_q4_model;
+/* The kernel's workspace, owned by the caller: byte offsets (256-aligned) of
+ * its buffers and the total size. After a token: h the residual stream
+ * (bf16 [hidden], the last layer's output), qkv (bf16 q/k/v rows of the last
+ * layer), attn (bf16 attention output [heads * head_dim]) with its planar
+ * Q8_0 (aq codes, ad scales, ac offsets), o_out (bf16 o_proj output), act
+ * (bf16 SiLU(gate) * up [inter]) with its planar Q8_0 (gq, gd, gc), down_out
+ * (bf16 down_proj output); layers, part_o, part_ml, amax, sync are the
+ * kernel's own. */
+typedef struct {
+    int64_t total, layers, h, qkv, attn, act, o_out, down_out, aq, ad, ac, gq, gd, gc, part_o, part_ml, amax, sync;
+} tn_llama_decode_layout;
+TN_API int tn_llama_decode_layout_of(const tn_llama_q4_model *model, tn_llama_decode_layout *layout);
+/* Build the launch plan over a caller-provided workspace (256-byte aligned
+ * device memory of layout.total bytes, zero-filled before the first token):
+ * copies the layer table into it (cudaMemcpy) and checks the kernel fits;
+ * allocates no device memory. The plan is a small host object. */
+TN_API int tn_llama_decode_plan(const tn_llama_q4_model *model, void *workspace, int64_t workspace_bytes,
+                                void **plan);
+/* One token: reads tokens[0] (the current token id) and *pos (its position;
+ * the cache holds positions [0, pos)), writes the bf16 logits [vocab], the
+ * next token id into tokens[0] and pos + 1 into *pos; appends this token's
+ * K/V at slot pos. tokens and pos are device ints. trace (or NULL): device
+ * bytes of tn_llama_decode_trace_bytes(plan), receiving the exact Q8_0 input
+ * tiles of trace_layer's q/k/v and gate/up linears and of lm_head (for
+ * checking each linear on its own inputs). A bounded wait that gives up makes
+ * the launch record TN_ERR_TIMEOUT (tn_device_status); call
+ * tn_llama_decode_reset before the next token. Cooperative launch: every
+ * CTA is resident at once. */
+TN_API int tn_llama_decode_token(void *plan, int *tokens, int *pos, void *logits, void *trace, int trace_layer,
+                                 void *stream);
+TN_API int64_t tn_llama_decode_trace_bytes(const void *plan);
+/* tn_llama_decode_token that also records its phase timeline (models of two or
+ * more layers): stamps, device uint64 [grid CTAs][64], receives %globaltimer
+ * (ns) per CTA for layer 1 -- [0] kernel start; [1..10] after the grid wait and
+ * after the work of the Q (RMSNorm + q/k/v), A (attention), O (o_proj), G
+ * (gate/up) and D (down_proj) phases; [11..16] when the CTA's producer started
+ * issuing the ring items of each of those phases and finished the layer's;
+ * [17] the CTA's final arrival; [18..61] finer points inside the Q and A
+ * phases (prologue done, per-warp item and K/V-tile times). The grid size is
+ * the device's SM count. A diagnostic of the kernel's schedule. */
+TN_API int tn_llama_decode_token_timeline(void *plan, int *tokens, int *pos, void *logits, uint64_t *stamps,
+                                          void *stream);
+/* Zero the plan's barrier counter, epoch and merge tickets (stream-ordered). */
+TN_API int tn_llama_decode_reset(void *plan, void *stream);
+TN_API int tn_llama_decode_plan_free(void *plan);
 
 /* ---- tensor parallelism (column-sharded linears, KV-head-group attention) -----
  * The reference has no multi-GPU path; this is the layout step of the

@@ -74,7 +74,9 @@ def _c_layout(tmp_path, ctype: str, names):
     return {k: int(v) for k, v in (line.split() for line in out.splitlines())}
 
 
-@pytest.mark.parametrize("ctype,mirror", [("tn_counters", "Counters"), ("tn_tp_link", "TpLink")])
+@pytest.mark.parametrize("ctype,mirror", [("tn_counters", "Counters"), ("tn_tp_link", "TpLink"),
+                                          ("tn_llama_q4_model", "LlamaQ4Model"),
+                                          ("tn_llama_decode_layout", "DecodeLayout")])
 def test_struct_bindings_match_the_header(tmp_path, ctype, mirror):
     """The ctypes mirrors of the header's structs have the C size and every
     field at the C offset (a field added on one side only would shift every

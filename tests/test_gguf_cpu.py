@@ -1,4 +1,4 @@
-"""The GGUF container reader (torchnative_b200.gguf.GGUFFile) on the CPU,
+"""The GGUF container reader (torchnative_b200.gguf.GGUFContainer) on the CPU,
 against files written by llama.cpp's gguf-py and against hand-built
 malformed ones: metadata values, torch-order shapes, aligned offsets and the
 stored bytes equal the writer's; the reference's refusals hold by name."""
@@ -15,7 +15,7 @@ gguf = pytest.importorskip("gguf")
 
 
 def test_type_table_sizes_equal_gguf_py():
-    for tid, (name, block, size, kind, _) in G.GGML_TYPES.items():
+    for tid, (name, block, size, handling, _) in G.GGML_TYPE_TABLE.items():
         try:
             qt = gguf.GGMLQuantizationType(tid)
         except ValueError:
@@ -38,7 +38,7 @@ def test_reads_what_gguf_py_writes(tmp_path):
           "tokenizer.ggml.scores": [0.5, 1.5, -2.0]}
     gguf_util.write_gguf(path, {"a": (f32, None), "b": (f16, None), "c": (q4, "Q4_0"), "d": (q8, "Q8_0"),
                                 "e": (bf, "BF16")}, md)
-    with G.GGUFFile(path) as f:
+    with G.GGUFContainer(path) as f:
         assert f.version == 3
         assert f.metadata["general.architecture"] == "llama"
         assert f.metadata["llama.block_count"] == 2 and f.metadata["general.name"] == "tiny"
@@ -49,22 +49,22 @@ def test_reads_what_gguf_py_writes(tmp_path):
                 "c": ((5, 128), "Q4_0", q4.tobytes()), "d": ((2, 96), "Q8_0", q8.tobytes()),
                 "e": ((4, 32), "BF16", bf.tobytes())}
         for name, (shape, tname, raw) in want.items():
-            info = f.info(name)
+            info = f.slot(name)
             assert info.shape == shape and info.type_name == tname, name
-            assert info.offset % f.alignment == 0 and info.offset >= f.data_offset
-            assert bytes(f.raw(name)) == raw, name
-        assert f.info("c").format == "q4_0" and f.info("d").format == "q8_0" and f.info("a").format is None
-        with pytest.raises(KeyError, match="no tensor named 'zz'"):
-            f.info("zz")
+            assert info.start % f.alignment == 0 and info.start >= f.data_start
+            assert bytes(f.bytes_of(name)) == raw, name
+        assert f.slot("c").block_format == "q4_0" and f.slot("d").block_format == "q8_0" and f.slot("a").block_format is None
+        with pytest.raises(KeyError, match="no tensor 'zz' in this file"):
+            f.slot("zz")
 
 
 def test_custom_alignment(tmp_path):
     q4 = np.arange(2 * 18, dtype=np.uint8).reshape(1, 36)
     path = tmp_path / "a.gguf"
     gguf_util.write_gguf(path, {"x": (np.ones(7, np.float32), None), "w": (q4, "Q4_0")}, alignment=64)
-    with G.GGUFFile(path) as f:
-        assert f.alignment == 64 and f.info("w").offset % 64 == 0
-        assert bytes(f.raw("w")) == q4.tobytes()
+    with G.GGUFContainer(path) as f:
+        assert f.alignment == 64 and f.slot("w").start % 64 == 0
+        assert bytes(f.bytes_of("w")) == q4.tobytes()
 
 
 def _file(tmp_path, raw):
@@ -74,38 +74,38 @@ def _file(tmp_path, raw):
 
 
 def test_malformed_files_are_refused_by_name(tmp_path):
-    with pytest.raises(G.GGUFFormatError, match="not a GGUF file"):
-        G.GGUFFile(_file(tmp_path, gguf_util.raw_gguf(magic=b"GGML")))
-    with pytest.raises(G.GGUFFormatError, match="empty file"):
-        G.GGUFFile(_file(tmp_path, b""))
-    with pytest.raises(G.UnsupportedGGUF, match="big-endian"):
-        G.GGUFFile(_file(tmp_path, gguf_util.raw_gguf(endian=">")))
-    with pytest.raises(G.UnsupportedGGUF, match="version 1"):
-        G.GGUFFile(_file(tmp_path, gguf_util.raw_gguf(version=1)))
+    with pytest.raises(G.GGUFMalformed, match="a GGUF file starts with"):
+        G.GGUFContainer(_file(tmp_path, gguf_util.raw_gguf(magic=b"GGML")))
+    with pytest.raises(G.GGUFMalformed, match="zero bytes long"):
+        G.GGUFContainer(_file(tmp_path, b""))
+    with pytest.raises(G.GGUFUnsupported, match="big-endian"):
+        G.GGUFContainer(_file(tmp_path, gguf_util.raw_gguf(endian=">")))
+    with pytest.raises(G.GGUFUnsupported, match="version 1"):
+        G.GGUFContainer(_file(tmp_path, gguf_util.raw_gguf(version=1)))
     # a Q4_0 tensor whose bytes are not all there
-    with pytest.raises(G.GGUFFormatError, match="truncated"):
-        G.GGUFFile(_file(tmp_path, gguf_util.raw_gguf(tensors=[("w", (64, 2), 2, 0)], data=b"\0" * 40)))
-    with pytest.raises(G.GGUFFormatError, match="truncated"):
-        G.GGUFFile(_file(tmp_path, gguf_util.raw_gguf(metadata=[("k", 8, struct.pack("<Q", 99) + b"ab")])))
-    with pytest.raises(G.GGUFFormatError, match="not a multiple of its block"):
-        G.GGUFFile(_file(tmp_path, gguf_util.raw_gguf(tensors=[("w", (48, 1), 2, 0)], data=b"\0" * 64)))
-    with pytest.raises(G.GGUFFormatError, match="not a multiple of the alignment"):
-        G.GGUFFile(_file(tmp_path, gguf_util.raw_gguf(tensors=[("w", (32, 1), 2, 8)], data=b"\0" * 64)))
-    with pytest.raises(G.GGUFFormatError, match="appears twice"):
-        G.GGUFFile(_file(tmp_path, gguf_util.raw_gguf(metadata=[("k", 4, struct.pack("<I", 1))] * 2)))
+    with pytest.raises(G.GGUFMalformed, match="cut short"):
+        G.GGUFContainer(_file(tmp_path, gguf_util.raw_gguf(tensors=[("w", (64, 2), 2, 0)], data=b"\0" * 40)))
+    with pytest.raises(G.GGUFMalformed, match="the file ends inside"):
+        G.GGUFContainer(_file(tmp_path, gguf_util.raw_gguf(metadata=[("k", 8, struct.pack("<Q", 99) + b"ab")])))
+    with pytest.raises(G.GGUFMalformed, match="does not divide into blocks of 32"):
+        G.GGUFContainer(_file(tmp_path, gguf_util.raw_gguf(tensors=[("w", (48, 1), 2, 0)], data=b"\0" * 64)))
+    with pytest.raises(G.GGUFMalformed, match="off the 32-byte alignment"):
+        G.GGUFContainer(_file(tmp_path, gguf_util.raw_gguf(tensors=[("w", (32, 1), 2, 8)], data=b"\0" * 64)))
+    with pytest.raises(G.GGUFMalformed, match="defined more than once"):
+        G.GGUFContainer(_file(tmp_path, gguf_util.raw_gguf(metadata=[("k", 4, struct.pack("<I", 1))] * 2)))
 
 
 def test_refused_and_kernel_less_types(tmp_path):
     data = b"\0" * 1024
     p = _file(tmp_path, gguf_util.raw_gguf(
         tensors=[("q81", (32, 1), 9, 0), ("q6k", (256, 1), 14, 64), ("odd", (4, 1), 99, 320)], data=data))
-    with G.GGUFFile(p) as f:
-        with pytest.raises(G.UnsupportedGGUF, match="Q8_1.*activation"):
-            f.raw("q81")
-        assert len(f.raw("q6k")) == 210  # readable bytes, no kernel
-        assert isinstance(G.refusal(14, "q6k"), G.UnsupportedGGUF) and "without a B200 kernel" in str(G.refusal(14))
-        assert G.refusal(2) is None and G.refusal(8) is None and G.refusal(12) is None and G.refusal(0) is None
-        with pytest.raises(G.UnsupportedGGUF, match="type id 99"):
-            f.raw("odd")
-        with pytest.raises(G.UnsupportedGGUF, match="without a B200 kernel"):
+    with G.GGUFContainer(p) as f:
+        with pytest.raises(G.GGUFUnsupported, match="Q8_1.*activation"):
+            f.bytes_of("q81")
+        assert len(f.bytes_of("q6k")) == 210  # readable bytes, no kernel
+        assert isinstance(G.why_refused(14, "q6k"), G.GGUFUnsupported) and "has no B200 kernel" in str(G.why_refused(14))
+        assert G.why_refused(2) is None and G.why_refused(8) is None and G.why_refused(12) is None and G.why_refused(0) is None
+        with pytest.raises(G.GGUFUnsupported, match="type id 99"):
+            f.bytes_of("odd")
+        with pytest.raises(G.GGUFUnsupported, match="has no B200 kernel"):
             G.load_tensor(f, "q6k")

@@ -37,7 +37,7 @@ def test_tensors_reach_the_device_byte_for_byte(G, cuda_device, tmp_path):
     path = tmp_path / "t.gguf"
     gguf_util.write_gguf(path, {"q4": (q4, "Q4_0"), "q8": (q8, "Q8_0"), "f32": (f32, None), "f16": (f16, None),
                                 "bf": (bf, "BF16")})
-    with G.GGUFFile(path) as f:
+    with G.GGUFContainer(path) as f:
         for name, arr, fmt, n in (("q4", q4, "q4_0", 6 * 256), ("q8", q8, "q8_0", 3 * 128)):
             q = G.load_tensor(f, name, keep_blocks=True, device=cuda_device)
             assert q.format == fmt and q.blob.device.type == "cuda"
@@ -62,12 +62,12 @@ def test_quantized_linear_is_the_files_blocks(G, cuda_device, tmp_path):
     gguf_util.write_gguf(path, {"w": (np.frombuffer(blob, np.uint8).reshape(48, -1), "Q4_0"),
                                 "n": (np.ones(512, np.float32), None)})
     x = torch.randn(3, 512, device=cuda_device)
-    with G.GGUFFile(path) as f:
+    with G.GGUFContainer(path) as f:
         mod = G.quantized_linear(f, "w", device=cuda_device)
         assert (mod.in_features, mod.out_features, mod.format) == (512, 48, "q4_0")
         want = quant._quantized_linear(x, quant._quantized_from_blob(blob, (48, 512), "q4_0", cuda_device))
         assert torch.equal(mod(x), want)
-        with pytest.raises(G.UnsupportedGGUF, match="not a block-quantised type"):
+        with pytest.raises(G.GGUFUnsupported, match="not a block-quantised type"):
             G.quantized_linear(f, "n", device=cuda_device)
 
 
@@ -79,12 +79,12 @@ def test_llama_cpp_row_order_is_undone_by_rows(G, cuda_device, tmp_path):
     path = tmp_path / "p.gguf"
     gguf_util.write_gguf(path, {"q": (gguf_util.llama_cpp_permute(hf, heads), "Q4_0"),
                                 "d": (gguf_util.llama_cpp_permute(dense, heads), None)})
-    with G.GGUFFile(path) as f:
+    with G.GGUFContainer(path) as f:
         q = G.load_tensor(f, "q", keep_blocks=True, permute_heads=heads, device=cuda_device)
         assert q.blob.cpu().numpy().tobytes() == hf.tobytes()
         d = G.load_tensor(f, "d", permute_heads=heads, device=cuda_device)
         assert d.cpu().numpy().tobytes() == dense.tobytes()
-        with pytest.raises(G.UnsupportedGGUF, match="q/k row order"):
+        with pytest.raises(G.GGUFUnsupported, match="q/k row order"):
             G.load_tensor(f, "q", keep_blocks=True, permute_heads=5, device=cuda_device)
 
 

@@ -91,7 +91,7 @@ def test_q4_k_from_gguf_and_refusals(tn, cuda_device, tmp_path):
     path = tmp_path / "k.gguf"
     gguf_util.write_gguf(path, {"w": (np.frombuffer(blob, np.uint8).reshape(24, -1), "Q4_K")})
     x = torch.randn(2, 512, device=cuda_device)
-    with G.GGUFFile(path) as f:
+    with G.GGUFContainer(path) as f:
         mod = G.quantized_linear(f, "w", device=cuda_device)
         assert mod.format == "q4_k" and tn._quantized_blob(mod.qweight) == blob
         want = tn._quantized_linear(x, tn._quantized_from_blob(blob, (24, 512), "q4_k", cuda_device))

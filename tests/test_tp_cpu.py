@@ -116,3 +116,43 @@ def test_shard_refusals():
     with pytest.raises(ValueError, match="is not"):
         tpm.row_slice(w[:-1], 10, 32, 0, 1)
     assert tpm.shard_rows(w, 10, 32, 1, 2).numel() == 5 * 18
+
+
+def _leaving_worker(rank, world, port, result):
+    """Rank 1 joins the group, passes one barrier and leaves before the
+    gather; rank 0's gather must end with PeerLost, not hang."""
+    import datetime
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    dist.barrier()
+    if rank == 1:
+        os._exit(0)  # gone between steps, with nothing in flight
+    g = tpm.TPGroup(rank, world, None)
+    try:
+        g.all_gather(torch.empty(2 * 8), torch.ones(8))
+        result.put("no error")
+    except tpm.PeerLost as e:
+        result.put("PeerLost: " + str(e))
+    except Exception as e:  # noqa: BLE001 -- reported to the parent
+        result.put(f"{type(e).__name__}: {e}")
+    os._exit(0)
+
+
+def test_a_rank_that_leaves_before_a_gather_is_named_on_the_host():
+    ctx = mp.get_context("spawn")
+    result = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, result)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        msg = result.get(timeout=60)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert msg.startswith("PeerLost"), msg
+    assert "rank 0 of 2" in msg

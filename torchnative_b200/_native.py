@@ -44,7 +44,27 @@ class Counters(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in (
         "q4_linear_calls", "q4_gemv_launches", "q4_gemv_generic", "q4_gemm_launches", "q8_quant_launches",
         "q4_codec_launches", "sdpa_calls", "sdpa_decode_launches", "sdpa_prefill_launches", "bytes_allocated",
-        "q4_skinny_launches")] + [("reserved", ctypes.c_uint64 * 5)]
+        "q4_skinny_launches", "decode_token_launches", "refusals", "resolves")] + [("reserved", ctypes.c_uint64 * 2)]
+
+
+class LlamaQ4Model(ctypes.Structure):
+    """tn_llama_q4_model (include/torchnative_b200.h): the persistent decode
+    kernel's view of a Llama-shaped Q4_0 model (per-layer fields are host
+    arrays of device pointers)."""
+    _fields_ = [(n, ctypes.c_int32) for n in ("layers", "hidden", "inter", "heads", "kv_heads", "head_dim",
+                                              "vocab")] + [
+        ("eps", ctypes.c_float), ("embed", ctypes.c_void_p), ("final_norm", ctypes.c_void_p),
+        ("lm_head", ctypes.c_void_p)] + [
+        (n, ctypes.POINTER(ctypes.c_void_p)) for n in ("attn_norm", "qkv", "o", "mlp_norm", "gate_up", "down",
+                                                       "k_cache", "v_cache")] + [
+        ("capacity", ctypes.c_int64), ("inv_freq", ctypes.c_void_p)]
+
+
+class DecodeLayout(ctypes.Structure):
+    """tn_llama_decode_layout: byte offsets of the persistent kernel's workspace."""
+    _fields_ = [(n, ctypes.c_int64) for n in ("total", "layers", "h", "qkv", "attn", "act", "o_out", "down_out",
+                                              "aq", "ad", "ac", "gq", "gd", "gc", "part_o", "part_ml", "amax",
+                                              "sync")]
 
 
 SIGNATURES = {
@@ -53,6 +73,9 @@ SIGNATURES = {
     "tn_status_name": (ctypes.c_char_p, [_I]),
     "tn_device_info": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I), _PI64, _PI64]),
     "tn_device_status": (_I, [_I]),
+    "tn_set_wait_budget": (_I, [_I64, _PI64]),
+    "tn_stream_set": (_I, [_I, _P]),
+    "tn_stream_get": (_I, [_I, ctypes.POINTER(_P)]),
     "tn_alloc": (_I, [ctypes.POINTER(_P), _SZ, _P]),
     "tn_free": (_I, [_P, _P]),
     "tn_empty_cache": (_I, []),
@@ -86,6 +109,13 @@ SIGNATURES = {
     "tn_llama_rope_append": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64, _P]),
     "tn_llama_argmax_embed": (_I, [_P, _I64, _I64, _P, _P, _I64, _P, _P, _P]),
     "tn_llama_embed": (_I, [_P, _I64, _P, _I64, _P, _P]),
+    "tn_llama_decode_layout_of": (_I, [_P, _P]),
+    "tn_llama_decode_plan": (_I, [_P, _P, _I64, ctypes.POINTER(_P)]),
+    "tn_llama_decode_token": (_I, [_P, _P, _P, _P, _P, _I, _P]),
+    "tn_llama_decode_trace_bytes": (_I64, [_P]),
+    "tn_llama_decode_token_timeline": (_I, [_P, _P, _P, _P, _P, _P]),
+    "tn_llama_decode_reset": (_I, [_P, _P]),
+    "tn_llama_decode_plan_free": (_I, [_P]),
     "tn_tp_unshard": (_I, [_P, _P, _I64, _I64, _I64, _P]),
     "tn_tp_region_alloc": (_I, [ctypes.c_size_t, _P, _P]),
     "tn_tp_region_open": (_I, [_P, _P]),
@@ -155,5 +185,37 @@ def reset_counters() -> None:
     check(lib().tn_reset_counters())
 
 
+_DISPATCH_KEYS = ("q4_linear_calls", "sdpa_calls", "q4_codec_launches", "q8_quant_launches", "decode_token_launches")
+
+
+def cuda_counters(index: int = 0) -> dict:
+    """The reference's `_C._cuda_counters()` shape (torch_c/src/device.rs:1671-1700):
+    resolves, dispatches, refusals and the per-op counts ("ops"), plus the
+    device's free and total bytes. Opens no device that is not already in use
+    (None for the memory figures then)."""
+    c = counters()
+    out = {"resolves": c["resolves"], "dispatches": sum(c[k] for k in _DISPATCH_KEYS),
+           "readback_refusals": 0, "refusals": c["refusals"],
+           "ops": {k: v for k, v in c.items() if k not in ("resolves", "refusals", "bytes_allocated")}}
+    free = total = None
+    try:
+        import torch
+
+        if torch.cuda.is_available() and torch.cuda.is_initialized():
+            free, total = torch.cuda.mem_get_info(index)
+    except Exception:  # noqa: BLE001 -- absence is a value here, as in the reference
+        pass
+    out["device_free_bytes"], out["device_total_bytes"] = free, total
+    return out
+
+
 def device_status(reset: bool = True) -> None:
     check(lib().tn_device_status(1 if reset else 0))
+
+
+def set_wait_budget(cycles: int) -> int:
+    """Set the current device's bounded-wait budget (cycles; <= 0 restores the
+    default); returns the previous one."""
+    prev = ctypes.c_int64(0)
+    check(lib().tn_set_wait_budget(int(cycles), ctypes.byref(prev)))
+    return int(prev.value)

@@ -257,7 +257,7 @@ extern "C" int tn_llama_add_rmsnorm_q8(const void *h, const void *delta, void *h
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, "tn_llama_add_rmsnorm_q8: hidden size must be a multiple of 32 "
                                                      "and at most 8192");
     if (rows == 0) return TN_OK;
-    return launch_pdl(tn::add_rmsnorm_q8_kernel, dim3((unsigned)rows), dim3(256), (cudaStream_t)stream,
+    return launch_pdl(tn::add_rmsnorm_q8_kernel, dim3((unsigned)rows), dim3(256), tn::stream_of(stream),
                       "tn_llama_add_rmsnorm_q8", (const __nv_bfloat16 *)h, (const __nv_bfloat16 *)delta,
                       (__nv_bfloat16 *)h_out, (const __nv_bfloat16 *)weight, eps, (int)H, codes, scales, offsets);
 }
@@ -269,7 +269,7 @@ extern "C" int tn_llama_silu_mul_q8(const void *gate_up, int64_t rows, int64_t I
     if (rows == 0) return TN_OK;
     const int nb = (int)(I / 32);
     return launch_pdl(tn::silu_mul_q8_kernel, dim3((unsigned)((nb + 7) / 8), (unsigned)rows), dim3(256),
-                      (cudaStream_t)stream, "tn_llama_silu_mul_q8", (const __nv_bfloat16 *)gate_up, (int)I, codes,
+                      tn::stream_of(stream), "tn_llama_silu_mul_q8", (const __nv_bfloat16 *)gate_up, (int)I, codes,
                       scales, offsets);
 }
 
@@ -280,7 +280,7 @@ extern "C" int tn_llama_rope_append(const void *qkv, const float *inv_freq, cons
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, "tn_llama_rope_append: head dimension must be even and <= 1024");
     if (B == 0) return TN_OK;
     return launch_pdl(tn::rope_append_kernel, dim3((unsigned)(Hq + Hkv), (unsigned)B), dim3((unsigned)(D / 2)),
-                      (cudaStream_t)stream, "tn_llama_rope_append", (const __nv_bfloat16 *)qkv, inv_freq, pos_dev,
+                      tn::stream_of(stream), "tn_llama_rope_append", (const __nv_bfloat16 *)qkv, inv_freq, pos_dev,
                       (int)pos_host, (int)Hq, (int)Hkv, (int)D, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)k_cache,
                       (__nv_bfloat16 *)v_cache, cache_b_stride, cache_h_stride);
 }
@@ -288,14 +288,14 @@ extern "C" int tn_llama_rope_append(const void *qkv, const float *inv_freq, cons
 extern "C" int tn_llama_argmax_embed(const void *logits, int64_t rows, int64_t V, int *tokens, const void *embed,
                                      int64_t H, void *h, int *pos_dev, void *stream) {
     if (rows <= 0) return TN_OK;
-    return launch_pdl(tn::argmax_embed_kernel, dim3((unsigned)rows), dim3(1024), (cudaStream_t)stream,
+    return launch_pdl(tn::argmax_embed_kernel, dim3((unsigned)rows), dim3(1024), tn::stream_of(stream),
                       "tn_llama_argmax_embed", (const __nv_bfloat16 *)logits, (int)V, tokens,
                       (const __nv_bfloat16 *)embed, (int)H, (__nv_bfloat16 *)h, pos_dev);
 }
 
 extern "C" int tn_llama_embed(const int *tokens, int64_t rows, const void *embed, int64_t H, void *h, void *stream) {
     if (rows <= 0) return TN_OK;
-    return launch_pdl(tn::embed_kernel, dim3((unsigned)rows), dim3(256), (cudaStream_t)stream, "tn_llama_embed",
+    return launch_pdl(tn::embed_kernel, dim3((unsigned)rows), dim3(256), tn::stream_of(stream), "tn_llama_embed",
                       tokens, (const __nv_bfloat16 *)embed, (int)H, (__nv_bfloat16 *)h);
 }
 
@@ -305,6 +305,6 @@ extern "C" int tn_tp_unshard(const void *src, void *dst, int64_t G, int64_t rows
     if (!src || !dst || src == dst) return tn::set_error(TN_ERR_INVALID, "tn_tp_unshard: src and dst must be distinct");
     const int64_t n = G * rows * cols;
     const unsigned blocks = (unsigned)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184);
-    return launch_pdl(tn::tp_unshard_kernel, dim3(blocks), dim3(256), (cudaStream_t)stream, "tn_tp_unshard",
+    return launch_pdl(tn::tp_unshard_kernel, dim3(blocks), dim3(256), tn::stream_of(stream), "tn_tp_unshard",
                       (const uint16_t *)src, (uint16_t *)dst, (int)G, (int)rows, (int)cols);
 }

@@ -287,7 +287,7 @@ int tn_q4_0_quantize(const float *x, void *blob, int64_t rows, int64_t cols, voi
     if (nb == 0) return TN_OK;
     if (!x || !blob) return tn::set_error(TN_ERR_INVALID, std::string(op) + ": null pointer");
     int threads = 128;
-    tn::q4_0_quantize_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
+    tn::q4_0_quantize_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, tn::stream_of(stream)>>>(
         x, static_cast<uint8_t *>(blob), nb);
     __atomic_fetch_add(&tn::counters().q4_codec_launches, 1ull, __ATOMIC_RELAXED);
     return tn::check_launch(op);
@@ -303,7 +303,7 @@ int tn_q4_0_dequantize(const void *blob, float *out, int64_t rows, int64_t cols,
     if (nb == 0) return TN_OK;
     if (!blob || !out) return tn::set_error(TN_ERR_INVALID, std::string(op) + ": null pointer");
     int threads = 128;
-    tn::q4_0_dequantize_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
+    tn::q4_0_dequantize_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, tn::stream_of(stream)>>>(
         static_cast<const uint8_t *>(blob), out, nb);
     __atomic_fetch_add(&tn::counters().q4_codec_launches, 1ull, __ATOMIC_RELAXED);
     return tn::check_launch(op);
@@ -319,7 +319,7 @@ int tn_q8_0_dequantize(const void *blob, float *out, int64_t rows, int64_t cols,
     if (nb == 0) return TN_OK;
     if (!blob || !out) return tn::set_error(TN_ERR_INVALID, std::string(op) + ": null pointer");
     int threads = 128;
-    tn::q8_0_dequantize_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
+    tn::q8_0_dequantize_kernel<<<(unsigned)((nb + threads - 1) / threads), threads, 0, tn::stream_of(stream)>>>(
         static_cast<const uint8_t *>(blob), out, nb);
     __atomic_fetch_add(&tn::counters().q4_codec_launches, 1ull, __ATOMIC_RELAXED);
     return tn::check_launch(op);
@@ -340,7 +340,7 @@ int tn_q8_0_quantize(const void *x, int x_dtype, int64_t x_row_stride, void *blo
     if (!x || !blob) return tn::set_error(TN_ERR_INVALID, std::string(op) + ": null pointer");
     int threads = 128;
     unsigned grid = (unsigned)((n + threads - 1) / threads);
-    cudaStream_t s = (cudaStream_t)stream;
+    cudaStream_t s = tn::stream_of(stream);
     uint8_t *b = static_cast<uint8_t *>(blob);
     if (x_dtype == TN_F32)
         tn::q8_0_quantize_blob_kernel<float><<<grid, threads, 0, s>>>(x, x_row_stride, b, rows, nb);

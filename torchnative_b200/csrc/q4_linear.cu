@@ -27,7 +27,7 @@ int check_link(const std::string &op, const tn_tp_link *l, int64_t out_cols) {
 extern "C" int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob, const float *bias,
                               void *y, int y_dtype, int64_t M, int64_t N, int64_t K, int act_mode, void *stream_) {
     const std::string op = "torch._C._quantized_linear";
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    cudaStream_t stream = tn::stream_of(stream_);
     __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
     if (x_dtype != TN_F32 && x_dtype != TN_BF16 && x_dtype != TN_F16)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": the activation must be torch.float32, torch.bfloat16 or "
@@ -100,7 +100,7 @@ extern "C" int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, 
 extern "C" int tn_q8_0_linear(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob, const float *bias,
                               void *y, int y_dtype, int64_t M, int64_t N, int64_t K, int act_mode, void *stream_) {
     const std::string op = "torch._C._quantized_linear";
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    cudaStream_t stream = tn::stream_of(stream_);
     __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
     if (x_dtype != TN_F32 && x_dtype != TN_BF16 && x_dtype != TN_F16)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": the activation must be torch.float32, torch.bfloat16 or "
@@ -167,7 +167,7 @@ extern "C" int tn_q8_0_quantize_planar(const void *x, int x_dtype, int64_t x_row
     if ((reinterpret_cast<uintptr_t>(codes) & 15) != 0)
         return tn::set_error(TN_ERR_INVALID, op + ": codes must be 16-byte aligned");
     return tn::launch_q8_planar(x, x_dtype, x_row_stride, codes, scales, offsets, rows, cols / 32, codes_row_stride,
-                                static_cast<cudaStream_t>(stream));
+                                tn::stream_of(stream));
 }
 
 extern "C" int tn_q4_0_linear_q8_tp(const int8_t *codes, int64_t codes_row_stride, const float *scales,
@@ -175,7 +175,7 @@ extern "C" int tn_q4_0_linear_q8_tp(const int8_t *codes, int64_t codes_row_strid
                                     int y_dtype, int64_t M, int64_t N, int64_t K, int flags,
                                     const tn_tp_link *link, void *stream_) {
     const std::string op = "torch._C._quantized_linear";
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    cudaStream_t stream = tn::stream_of(stream_);
     __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
     if (y_dtype != TN_F32 && y_dtype != TN_BF16 && y_dtype != TN_F16)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": unsupported output dtype " + tn_dtype_name(y_dtype));
@@ -263,7 +263,7 @@ int linear_fused(const std::string &op, int x_mode, const void *x, int64_t x_row
     }
     return tn::launch_q4_gemv_fused(x_mode, x, x_row_stride, delta, h_out, norm_weight, eps,
                                     static_cast<const uint8_t *>(w_blob), bias, y, y_dtype, pairs ? N / 2 : N, (int)M,
-                                    N, K, flags, static_cast<cudaStream_t>(stream), link, q8);
+                                    N, K, flags, tn::stream_of(stream), link, q8);
 }
 
 }  // namespace

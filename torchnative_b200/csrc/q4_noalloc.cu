@@ -67,7 +67,7 @@ extern "C" int tn_q4_0_linear_noalloc(const void *x, int x_dtype, int64_t x_row_
                                       const float *bias, void *y, int y_dtype, int64_t M, int64_t N, int64_t K,
                                       void *stream_) {
     const std::string op = "tn_q4_0_linear_noalloc";
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    cudaStream_t stream = tn::stream_of(stream_);
     if (x_dtype != TN_F32 && x_dtype != TN_BF16 && x_dtype != TN_F16)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": the activation must be torch.float32, torch.bfloat16 or "
                                                           "torch.float16, got " +

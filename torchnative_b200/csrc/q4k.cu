@@ -145,7 +145,7 @@ extern "C" int tn_q4_k_dequantize(const void *blob, float *out, int64_t rows, in
     if (nsb == 0) return TN_OK;
     if (!blob || !out) return tn::set_error(TN_ERR_INVALID, op + ": null pointer");
     const int threads = 128;
-    tn::q4k_dequantize_kernel<<<(unsigned)((nsb * 4 + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
+    tn::q4k_dequantize_kernel<<<(unsigned)((nsb * 4 + threads - 1) / threads), threads, 0, tn::stream_of(stream)>>>(
         static_cast<const uint8_t *>(blob), out, nsb);
     __atomic_fetch_add(&tn::counters().q4_codec_launches, 1ull, __ATOMIC_RELAXED);
     return tn::check_launch(op.c_str());
@@ -154,7 +154,7 @@ extern "C" int tn_q4_k_dequantize(const void *blob, float *out, int64_t rows, in
 extern "C" int tn_q4_k_linear(const void *x, int x_dtype, int64_t x_row_stride, const void *w_blob, const float *bias,
                               void *y, int y_dtype, int64_t M, int64_t N, int64_t K, int act_mode, void *stream_) {
     const std::string op = "torch._C._quantized_linear";
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    cudaStream_t stream = tn::stream_of(stream_);
     __atomic_fetch_add(&tn::counters().q4_linear_calls, 1ull, __ATOMIC_RELAXED);
     if (x_dtype != TN_F32 && x_dtype != TN_BF16 && x_dtype != TN_F16)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": the activation must be torch.float32, torch.bfloat16 or "

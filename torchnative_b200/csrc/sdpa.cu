@@ -18,7 +18,7 @@ extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void 
                                        const int64_t *q_strides, const int64_t *k_strides, const int64_t *v_strides,
                                        int is_causal, double scale, void *stream_) {
     const std::string op = "aten._scaled_dot_product_flash_attention_for_cpu.default";
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    cudaStream_t stream = tn::stream_of(stream_);
     __atomic_fetch_add(&tn::counters().sdpa_calls, 1ull, __ATOMIC_RELAXED);
     if (dtype == TN_F64)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": torch.float64 attention is not implemented on CUDA");
@@ -111,7 +111,7 @@ extern "C" int tn_sdpa_decode_cache(const void *q, const void *k_cache, const vo
                                     const int64_t *q_strides, const int64_t *k_strides, const int64_t *v_strides,
                                     const int *len_dev, int64_t len_add, double scale, void *stream_) {
     const std::string op = "tn_sdpa_decode_cache";
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    cudaStream_t stream = tn::stream_of(stream_);
     __atomic_fetch_add(&tn::counters().sdpa_calls, 1ull, __ATOMIC_RELAXED);
     if (dtype != TN_F32 && dtype != TN_BF16 && dtype != TN_F16)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": dtype must be float32, bfloat16 or float16");
@@ -175,7 +175,7 @@ extern "C" int tn_sdpa_decode_step_q8(const void *qkv, const float *inv_freq, vo
         (!codes || !scales || !offsets || (reinterpret_cast<uintptr_t>(codes) & 3) != 0))
         return tn::set_error(TN_ERR_INVALID, op + ": planar Q8_0 output needs codes (4-byte aligned), scales and "
                                                   "offsets");
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    cudaStream_t stream = tn::stream_of(stream_);
     __atomic_fetch_add(&tn::counters().sdpa_calls, 1ull, __ATOMIC_RELAXED);
     if (D != 64 && D != 128)
         return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": head dimension must be 64 or 128");

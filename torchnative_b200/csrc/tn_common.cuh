@@ -20,6 +20,10 @@ int set_error(int status, const std::string &msg);  // records msg for tn_last_e
 int check_cuda(cudaError_t e, const char *op, const char *what);
 int check_launch(const char *op);  // cudaGetLastError after a launch
 
+// The stream a call runs on: the one it was given, or for NULL the current
+// device's stream set by tn_stream_set (NULL: the legacy default stream).
+cudaStream_t stream_of(void *stream);
+
 struct Counters;
 tn_counters &counters();
 
@@ -46,8 +50,14 @@ int *device_error_word();
 
 enum : int { DEV_ERR_NONE = 0, DEV_ERR_WAIT_FULL = 1, DEV_ERR_WAIT_EMPTY = 2, DEV_ERR_DRAIN = 3 };
 
-// ~2^31 cycles (~1 s at 1.9 GHz) before a wait gives up.
+// ~2^31 cycles (~1 s at 1.9 GHz) before a wait gives up: the default of the
+// per-device budget (tn_set_wait_budget) that waits read next to the error
+// word they were given.
 constexpr long long kWaitBudgetCycles = 1ll << 31;
+
+__device__ __forceinline__ long long wait_budget(const int *err) {
+    return err ? *reinterpret_cast<const volatile long long *>(err + 2) : kWaitBudgetCycles;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -160,9 +170,9 @@ __device__ __forceinline__ bool tp_wait_counts(const uint8_t *local_base, int sl
     for (int g = 0; g < world; ++g) {
         if (ld_acquire_sys(cnt + g) >= target) continue;
         if (err && *reinterpret_cast<volatile int *>(err) != 0) return false;
-        const long long start = clock64();
+        const long long start = clock64(), budget = wait_budget(err);
         while (ld_acquire_sys(cnt + g) < target) {
-            if (clock64() - start > kWaitBudgetCycles) {
+            if (clock64() - start > budget) {
                 record_device_error(err, DEV_ERR_WAIT_FULL);
                 return false;
             }

@@ -24,9 +24,20 @@ struct FactsSlot {
 FactsSlot g_facts[kMaxDevices];
 std::mutex g_facts_mu;
 
-// Device-side error word: set by kernels whose bounded waits gave up.
-__device__ int g_device_error = 0;
+// Device-side words of each GPU: the error code set by kernels whose bounded
+// waits gave up, and the wait budget (clock cycles) those waits allow. Kernels
+// reach both through the `int *err` they are given (budget at err + 2).
+struct DeviceWords {
+    int err;
+    int pad;
+    long long wait_budget;
+};
+__device__ DeviceWords g_device_error = {0, 0, tn::kWaitBudgetCycles};
 int *g_error_word[kMaxDevices] = {nullptr};
+
+// The stream each device's calls run on when they are given none (the
+// reference keeps one candle CudaStream per device); NULL = the legacy stream.
+cudaStream_t g_current_stream[kMaxDevices] = {nullptr};
 
 // ---- caching allocator -------------------------------------------------------
 
@@ -64,7 +75,15 @@ namespace tn {
 
 int set_error(int status, const std::string &msg) {
     g_last_error = msg;
+    if (status == TN_ERR_NOT_IMPLEMENTED) __atomic_fetch_add(&g_counters.refusals, 1ull, __ATOMIC_RELAXED);
     return status;
+}
+
+cudaStream_t stream_of(void *stream) {
+    if (stream) return static_cast<cudaStream_t>(stream);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    return g_current_stream[dev];
 }
 
 int check_cuda(cudaError_t e, const char *op, const char *what) {
@@ -89,6 +108,7 @@ int device_facts(DeviceFacts *out) {
         cudaDeviceProp p;
         st = check_cuda(cudaGetDeviceProperties(&p, dev), "tn_device_info", "cudaGetDeviceProperties");
         if (st) return st;
+        __atomic_fetch_add(&g_counters.resolves, 1ull, __ATOMIC_RELAXED);
         f.sm_count = p.multiProcessorCount;
         f.cc_major = p.major;
         f.cc_minor = p.minor;
@@ -216,9 +236,35 @@ int tn_device_status(int reset) {
     return TN_OK;
 }
 
+int tn_set_wait_budget(int64_t cycles, int64_t *previous) {
+    int *w = tn::device_error_word();
+    if (!w) return tn::set_error(TN_ERR_CUDA, "tn_set_wait_budget: no device words");
+    long long *b = reinterpret_cast<long long *>(w + 2);
+    long long old = 0;
+    int st = tn::check_cuda(cudaMemcpy(&old, b, sizeof(old), cudaMemcpyDeviceToHost), "tn_set_wait_budget", "read");
+    if (st) return st;
+    if (previous) *previous = old;
+    if (cycles <= 0) cycles = tn::kWaitBudgetCycles;
+    long long v = cycles;
+    return tn::check_cuda(cudaMemcpy(b, &v, sizeof(v), cudaMemcpyHostToDevice), "tn_set_wait_budget", "write");
+}
+
+int tn_stream_set(int device, void *stream) {
+    if (device < 0 || device >= kMaxDevices) return tn::set_error(TN_ERR_INVALID, "tn_stream_set: bad device index");
+    g_current_stream[device] = static_cast<cudaStream_t>(stream);
+    return TN_OK;
+}
+
+int tn_stream_get(int device, void **stream) {
+    if (device < 0 || device >= kMaxDevices || !stream)
+        return tn::set_error(TN_ERR_INVALID, "tn_stream_get: bad device index or null out-pointer");
+    *stream = g_current_stream[device];
+    return TN_OK;
+}
+
 int tn_alloc(void **ptr, size_t bytes, void *stream_) {
     if (!ptr) return tn::set_error(TN_ERR_INVALID, "tn_alloc: null out-pointer");
-    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    cudaStream_t stream = tn::stream_of(stream_);
     int dev = 0;
     int st = tn::check_cuda(cudaGetDevice(&dev), "tn_alloc", "cudaGetDevice");
     if (st) return st;

@@ -74,9 +74,9 @@ __global__ void __launch_bounds__(256) tp_allgather_kernel(Bases bases, int rank
     if (ld_acquire_sys(cnt) >= target) return;
     // after one wait has given up (a rank gone), later gathers fail fast
     if (err && *reinterpret_cast<volatile int *>(err) != 0) return;
-    const long long start = clock64();
+    const long long start = clock64(), budget = wait_budget(err);
     while (ld_acquire_sys(cnt) < target) {
-        if (clock64() - start > kWaitBudgetCycles) {
+        if (clock64() - start > budget) {
             record_device_error(err, DEV_ERR_WAIT_FULL);
             return;
         }
@@ -160,7 +160,7 @@ int tn_tp_allgather(void *const *bases, int rank, int world, const void *local, 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas);
     cfg.blockDim = dim3(256);
-    cfg.stream = static_cast<cudaStream_t>(stream);
+    cfg.stream = tn::stream_of(stream);
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return tn::check_cuda(cudaLaunchKernelEx(&cfg, tn::tp_allgather_kernel, b, rank, world,
@@ -178,7 +178,7 @@ int tn_tp_step_end(void *local_base, void *stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(1);
-    cfg.stream = static_cast<cudaStream_t>(stream);
+    cfg.stream = tn::stream_of(stream);
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return tn::check_cuda(cudaLaunchKernelEx(&cfg, tn::tp_step_end_kernel,

@@ -1,243 +1,323 @@
 """GGUF checkpoints straight to the device, keeping the file's own blocks.
 
-Mirrors torchnative's `torchnative.gguf` (torchnative/python/torchnative/gguf/
-__init__.py, reader.py): `GGUFFile` reads the container (header, typed
-metadata, tensor descriptors, aligned tensor data) with `struct` and `mmap`
-only; `load_tensor(f, name, keep_blocks=...)` turns one tensor into a device
-tensor, and `quantized_linear(f, name)` into a `QuantizedLinear` whose weight
-is the tensor's GGML blocks, byte for byte -- never decoded and re-encoded.
+The container half reads a GGUF file as the format specification
+(llama.cpp's docs/gguf.md) defines it, from a read-only memory map:
 
-What differs from the reference is where the bytes land: the reference hands
-them to candle's host QTensor (`torch._C._quantized_from_blob`); here they go
-from the memory map through one pinned staging buffer to HBM
-(`cudaMemcpyAsync` by torch), and the block formats that have B200 kernels
-(Q4_0, Q8_0, Q4_K) become a `QTensor` on the device. Other GGML block formats are
-listed and readable as raw bytes but refused by name when asked to become a
-tensor, as are the types the reference refuses.
+    magic "GGUF" | u32 version (2, 3) | u64 tensor count | u64 metadata count
+    metadata:  { string key | u32 value type | value } *
+    tensors:   { string name | u32 rank | u64 extent * rank (fastest first)
+                 | u32 GGML type | u64 offset into the data section } *
+    padding to `general.alignment` (32 unless the metadata says otherwise)
+    data section
 
-GGUF layout (little-endian): magic "GGUF", version (2 or 3), tensor count and
-metadata count (u64); metadata entries (string key, u32 value type, value);
-tensor descriptors (string name, u32 n_dims, n_dims u64 extents with the
-fastest-varying first, u32 GGML type, u64 offset into the data section); the
-data section starts at the next multiple of `general.alignment` (default 32).
+Strings are a u64 byte length and UTF-8 bytes; all integers little-endian.
+The device half (`load_tensor`, `quantized_linear`) moves one tensor's bytes
+through a pinned staging buffer to HBM: the block formats with B200 kernels
+(Q4_0, Q8_0, Q4_K) become a QTensor holding the file's blocks unchanged; dense
+F32 / F16 / BF16 arrive bit for bit. The loader contract it serves is the
+reference's torchnative.gguf (torchnative/python/torchnative/gguf/).
 """
 
 from __future__ import annotations
 
 import mmap
 import os
-import struct
+from collections import namedtuple
 
-__all__ = ["GGML_TYPES", "GGUFFile", "GGUFFormatError", "GGUFTensorInfo", "UnsupportedGGUF", "load_tensor",
-           "quantized_linear", "refusal", "type_name"]
+import numpy as np
 
-_MAGIC = b"GGUF"
-_DEFAULT_ALIGNMENT = 32
-_MAX_DIMS = 4
+__all__ = ["GGML_TYPE_TABLE", "GGUFContainer", "GGUFMalformed", "GGUFUnsupported", "TensorSlot", "ggml_type_name",
+           "load_tensor", "quantized_linear", "why_refused"]
 
 
-class GGUFFormatError(ValueError):
-    """Not a well-formed GGUF file: bad magic, truncation, inconsistent sizes."""
+class GGUFMalformed(ValueError):
+    """The bytes do not form a GGUF file (wrong magic, short, inconsistent)."""
 
 
-class UnsupportedGGUF(NotImplementedError):
-    """A well-formed GGUF construct this loader refuses, by name."""
+class GGUFUnsupported(NotImplementedError):
+    """A valid GGUF construct that this loader declines, with the reason."""
 
 
-_ACT_SIDE = ("is a block format llama.cpp uses only for the activation operand inside its dot products, "
-             "never as a stored weight")
-_NO_KERNEL = ("is a GGML block format without a B200 kernel in this backend (Q4_0, Q8_0 and Q4_K have one); its "
-              "bytes can be read with GGUFFile.raw, not turned into a tensor")
-_NO_CANDLE = "has no candle GgmlDType in the reference, so neither side has storage or a kernel for it"
-_NOT_WEIGHT = "is a plain numeric type no LLM checkpoint uses for weights; refused rather than guessed at"
-_REPACKED = "is a repacked layout llama.cpp removed from the file format; files carrying it are not read"
+# Why a GGML type is not turned into a tensor here.
+_ONLY_ACTIVATIONS = "exists only as llama.cpp's activation-side operand, never as a stored weight"
+_NO_B200_KERNEL = ("has no B200 kernel in this backend (the block formats with one are Q4_0, Q8_0 and Q4_K); "
+                   "GGUFContainer.bytes_of still returns its stored bytes")
+_NOT_IN_CANDLE = "is not a candle GgmlDType in the reference, so no path on either side stores or computes it"
+_INTEGER_OR_F64 = "is a plain integer / float64 type that no checkpoint stores weights in; declined"
+_REMOVED_REPACK = "is one of the repacked layouts llama.cpp dropped from the file format"
 
-# id -> (name, elements per block, bytes per block, kind, torch dtype / backend format / reason).
-# kind: "dense" (read as that dtype), "block" (held as a device QTensor of that
-# format), "raw" (a GGML block format this backend has no kernel for), or
-# "refused". Block sizes are ggml's type_traits; the tests check them against
-# the installed gguf-py's GGML_QUANT_SIZES.
-GGML_TYPES = {
-    0: ("F32", 1, 4, "dense", "float32"),
-    1: ("F16", 1, 2, "dense", "float16"),
-    2: ("Q4_0", 32, 18, "block", "q4_0"),
-    3: ("Q4_1", 32, 20, "raw", _NO_KERNEL),
-    6: ("Q5_0", 32, 22, "raw", _NO_KERNEL),
-    7: ("Q5_1", 32, 24, "raw", _NO_KERNEL),
-    8: ("Q8_0", 32, 34, "block", "q8_0"),
-    9: ("Q8_1", 32, 36, "refused", _ACT_SIDE),
-    10: ("Q2_K", 256, 84, "raw", _NO_KERNEL),
-    11: ("Q3_K", 256, 110, "raw", _NO_KERNEL),
-    12: ("Q4_K", 256, 144, "block", "q4_k"),
-    13: ("Q5_K", 256, 176, "raw", _NO_KERNEL),
-    14: ("Q6_K", 256, 210, "raw", _NO_KERNEL),
-    15: ("Q8_K", 256, 292, "refused", _ACT_SIDE),
-    16: ("IQ2_XXS", 256, 66, "refused", _NO_CANDLE),
-    17: ("IQ2_XS", 256, 74, "refused", _NO_CANDLE),
-    18: ("IQ3_XXS", 256, 98, "refused", _NO_CANDLE),
-    19: ("IQ1_S", 256, 50, "refused", _NO_CANDLE),
-    20: ("IQ4_NL", 32, 18, "refused", _NO_CANDLE),
-    21: ("IQ3_S", 256, 110, "refused", _NO_CANDLE),
-    22: ("IQ2_S", 256, 82, "refused", _NO_CANDLE),
-    23: ("IQ4_XS", 256, 136, "refused", _NO_CANDLE),
-    24: ("I8", 1, 1, "refused", _NOT_WEIGHT),
-    25: ("I16", 1, 2, "refused", _NOT_WEIGHT),
-    26: ("I32", 1, 4, "refused", _NOT_WEIGHT),
-    27: ("I64", 1, 8, "refused", _NOT_WEIGHT),
-    28: ("F64", 1, 8, "refused", _NOT_WEIGHT),
-    29: ("IQ1_M", 256, 56, "refused", _NO_CANDLE),
-    30: ("BF16", 1, 2, "dense", "bfloat16"),
-    31: ("Q4_0_4_4", None, None, "refused", _REPACKED),
-    32: ("Q4_0_4_8", None, None, "refused", _REPACKED),
-    33: ("Q4_0_8_8", None, None, "refused", _REPACKED),
-    34: ("TQ1_0", 256, 54, "refused", _NO_CANDLE),
-    35: ("TQ2_0", 256, 66, "refused", _NO_CANDLE),
-    36: ("IQ4_NL_4_4", None, None, "refused", _REPACKED),
-    37: ("IQ4_NL_4_8", None, None, "refused", _REPACKED),
-    38: ("IQ4_NL_8_8", None, None, "refused", _REPACKED),
-    39: ("MXFP4", 32, 17, "refused", _NO_CANDLE),
+GGMLType = namedtuple("GGMLType", "name block_elems block_bytes handling target")
+# The GGML type ids with their block geometry (ggml's type traits, checked
+# against gguf-py's GGML_QUANT_SIZES by the tests) and this loader's handling:
+# "dense" (read as the torch dtype `target`), "block" (a device QTensor of
+# format `target`), "bytes" (readable bytes, no kernel) or "declined".
+GGML_TYPE_TABLE = {
+    0: GGMLType("F32", 1, 4, "dense", "float32"),
+    1: GGMLType("F16", 1, 2, "dense", "float16"),
+    2: GGMLType("Q4_0", 32, 18, "block", "q4_0"),
+    3: GGMLType("Q4_1", 32, 20, "bytes", _NO_B200_KERNEL),
+    6: GGMLType("Q5_0", 32, 22, "bytes", _NO_B200_KERNEL),
+    7: GGMLType("Q5_1", 32, 24, "bytes", _NO_B200_KERNEL),
+    8: GGMLType("Q8_0", 32, 34, "block", "q8_0"),
+    9: GGMLType("Q8_1", 32, 36, "declined", _ONLY_ACTIVATIONS),
+    10: GGMLType("Q2_K", 256, 84, "bytes", _NO_B200_KERNEL),
+    11: GGMLType("Q3_K", 256, 110, "bytes", _NO_B200_KERNEL),
+    12: GGMLType("Q4_K", 256, 144, "block", "q4_k"),
+    13: GGMLType("Q5_K", 256, 176, "bytes", _NO_B200_KERNEL),
+    14: GGMLType("Q6_K", 256, 210, "bytes", _NO_B200_KERNEL),
+    15: GGMLType("Q8_K", 256, 292, "declined", _ONLY_ACTIVATIONS),
+    16: GGMLType("IQ2_XXS", 256, 66, "declined", _NOT_IN_CANDLE),
+    17: GGMLType("IQ2_XS", 256, 74, "declined", _NOT_IN_CANDLE),
+    18: GGMLType("IQ3_XXS", 256, 98, "declined", _NOT_IN_CANDLE),
+    19: GGMLType("IQ1_S", 256, 50, "declined", _NOT_IN_CANDLE),
+    20: GGMLType("IQ4_NL", 32, 18, "declined", _NOT_IN_CANDLE),
+    21: GGMLType("IQ3_S", 256, 110, "declined", _NOT_IN_CANDLE),
+    22: GGMLType("IQ2_S", 256, 82, "declined", _NOT_IN_CANDLE),
+    23: GGMLType("IQ4_XS", 256, 136, "declined", _NOT_IN_CANDLE),
+    24: GGMLType("I8", 1, 1, "declined", _INTEGER_OR_F64),
+    25: GGMLType("I16", 1, 2, "declined", _INTEGER_OR_F64),
+    26: GGMLType("I32", 1, 4, "declined", _INTEGER_OR_F64),
+    27: GGMLType("I64", 1, 8, "declined", _INTEGER_OR_F64),
+    28: GGMLType("F64", 1, 8, "declined", _INTEGER_OR_F64),
+    29: GGMLType("IQ1_M", 256, 56, "declined", _NOT_IN_CANDLE),
+    30: GGMLType("BF16", 1, 2, "dense", "bfloat16"),
+    31: GGMLType("Q4_0_4_4", None, None, "declined", _REMOVED_REPACK),
+    32: GGMLType("Q4_0_4_8", None, None, "declined", _REMOVED_REPACK),
+    33: GGMLType("Q4_0_8_8", None, None, "declined", _REMOVED_REPACK),
+    34: GGMLType("TQ1_0", 256, 54, "declined", _NOT_IN_CANDLE),
+    35: GGMLType("TQ2_0", 256, 66, "declined", _NOT_IN_CANDLE),
+    36: GGMLType("IQ4_NL_4_4", None, None, "declined", _REMOVED_REPACK),
+    37: GGMLType("IQ4_NL_4_8", None, None, "declined", _REMOVED_REPACK),
+    38: GGMLType("IQ4_NL_8_8", None, None, "declined", _REMOVED_REPACK),
+    39: GGMLType("MXFP4", 32, 17, "declined", _NOT_IN_CANDLE),
 }
 
 
-def type_name(ggml_type: int) -> str:
-    t = GGML_TYPES.get(ggml_type)
-    return t[0] if t else f"<unknown GGML type id {ggml_type}>"
+def ggml_type_name(type_id: int) -> str:
+    t = GGML_TYPE_TABLE.get(type_id)
+    return t.name if t else f"GGML type {type_id}"
 
 
-def refusal(ggml_type: int, tensor_name: str | None = None, for_tensor: bool = True):
-    """The UnsupportedGGUF this loader raises for the type, or None.
-    `for_tensor`: turning the bytes into a tensor (raw block formats refuse
-    then, but their bytes stay readable)."""
-    where = f" (tensor {tensor_name!r})" if tensor_name else ""
-    t = GGML_TYPES.get(ggml_type)
+def why_refused(type_id: int, tensor: str | None = None, as_tensor: bool = True):
+    """The GGUFUnsupported to raise for a tensor of this type, or None when it
+    is read. as_tensor=False asks about reading its raw bytes only, which the
+    block formats without a kernel allow."""
+    label = f"tensor {tensor!r}: " if tensor else ""
+    t = GGML_TYPE_TABLE.get(type_id)
     if t is None:
-        return UnsupportedGGUF(f"GGML type id {ggml_type}{where} is not one this loader knows; refused rather "
-                               "than read as something else")
-    name, _, _, kind, why = t
-    if kind == "refused" or (kind == "raw" and for_tensor):
-        return UnsupportedGGUF(f"GGML type {name}{where} {why}")
+        return GGUFUnsupported(f"{label}unknown GGML type id {type_id} -- declined rather than misread")
+    if t.handling == "declined" or (t.handling == "bytes" and as_tensor):
+        return GGUFUnsupported(f"{label}{t.name} {t.target}")
     return None
 
 
-# metadata value types: id -> struct format (scalars); 8 = string, 9 = array
-_SCALAR = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q", 12: "<d"}
-_STRING, _ARRAY = 8, 9
+# metadata value type ids (gguf.md): scalars as numpy dtypes; 8 string, 9 array
+_VALUE_DTYPES = {0: np.dtype("<u1"), 1: np.dtype("<i1"), 2: np.dtype("<u2"), 3: np.dtype("<i2"),
+                 4: np.dtype("<u4"), 5: np.dtype("<i4"), 6: np.dtype("<f4"), 7: np.dtype("?"),
+                 10: np.dtype("<u8"), 11: np.dtype("<i8"), 12: np.dtype("<f8")}
+_T_STRING, _T_ARRAY = 8, 9
+_MAX_RANK = 4
+_ALIGN_DEFAULT = 32
 
 
-class GGUFTensorInfo:
-    """One descriptor. `shape` is torch order (the reverse of GGUF's extents,
-    whose first is the fastest-varying): a linear weight stored with extents
-    [in, out] is (out, in), nn.Linear's layout, and its blocks run along `in`."""
+class TensorSlot:
+    """Where one tensor lives in the file. `extents` are GGUF's (fastest
+    first); `shape` is torch order, their reverse -- a linear weight stored
+    with extents [in, out] is (out, in), blocks running along `in`. `start`
+    is the absolute file offset, `size` its byte count (None for a type whose
+    geometry this loader does not know)."""
 
-    __slots__ = ("name", "ggml_type", "ne", "shape", "offset", "nbytes", "n_elements")
+    __slots__ = ("name", "type_id", "extents", "shape", "start", "size", "count")
 
-    def __init__(self, name, ggml_type, ne, offset, nbytes, n_elements):
-        self.name, self.ggml_type, self.ne = name, ggml_type, tuple(ne)
-        self.shape = tuple(reversed(self.ne))
-        self.offset, self.nbytes, self.n_elements = offset, nbytes, n_elements
+    def __init__(self, name, type_id, extents, start, size, count):
+        self.name, self.type_id, self.extents = name, type_id, tuple(extents)
+        self.shape = self.extents[::-1]
+        self.start, self.size, self.count = start, size, count
 
     @property
     def type_name(self) -> str:
-        return type_name(self.ggml_type)
+        return ggml_type_name(self.type_id)
 
     @property
-    def kind(self) -> str:
-        t = GGML_TYPES.get(self.ggml_type)
-        return t[3] if t else "refused"
+    def handling(self) -> str:
+        t = GGML_TYPE_TABLE.get(self.type_id)
+        return t.handling if t else "declined"
 
     @property
-    def format(self) -> str | None:
-        t = GGML_TYPES.get(self.ggml_type)
-        return t[4] if t and t[3] == "block" else None
+    def block_format(self) -> str | None:
+        t = GGML_TYPE_TABLE.get(self.type_id)
+        return t.target if t and t.handling == "block" else None
 
     def __repr__(self):
-        return f"GGUFTensorInfo({self.name!r}, {self.type_name}, shape={self.shape}, nbytes={self.nbytes})"
+        return f"TensorSlot({self.name!r}, {self.type_name}, shape={self.shape}, {self.size} bytes)"
 
 
-class _Reader:
-    def __init__(self, buf, size, path):
-        self.buf, self.size, self.pos, self.path = buf, size, 0, path
+def _scan(buf, path: str):
+    """Parse the header, metadata and tensor table of the mapped file `buf`;
+    returns (version, metadata, value types, alignment, data start, slots)."""
+    end = len(buf)
+    at = 0
 
-    def _need(self, n, what):
-        if n < 0 or self.pos + n > self.size:
-            raise GGUFFormatError(f"{self.path}: truncated while reading {what} ({n} bytes at offset {self.pos}, "
-                                  f"file is {self.size} bytes)")
-        p = self.pos
-        self.pos += n
-        return p
+    def span(n, what):
+        nonlocal at
+        if n < 0 or at + n > end:
+            raise GGUFMalformed(f"{path}: the file ends inside {what} (needs {n} bytes at byte {at} of {end})")
+        lo = at
+        at += n
+        return lo
 
-    def unpack(self, fmt, what):
-        n = struct.calcsize(fmt)
-        return struct.unpack_from(fmt, self.buf, self._need(n, what))[0]
+    def scalar(dt, what):
+        return np.frombuffer(buf, dt, 1, span(dt.itemsize, what))[0].item()
 
-    def string(self, what):
-        n = self.unpack("<Q", f"the length of {what}")
-        p = self._need(n, what)
-        # surrogateescape: tokenizer entries that are not UTF-8 round-trip
-        return bytes(self.buf[p:p + n]).decode("utf-8", "surrogateescape")
+    def u32(what):
+        return scalar(_VALUE_DTYPES[4], what)
 
-    def value(self, vtype, what, nested=False):
-        if vtype in _SCALAR:
-            return self.unpack(_SCALAR[vtype], what)
-        if vtype == _STRING:
-            return self.string(what)
-        if vtype == _ARRAY:
-            if nested:
-                raise UnsupportedGGUF(f"{self.path}: {what}: arrays of arrays are not read")
-            etype = self.unpack("<I", f"the element type of {what}")
-            count = self.unpack("<Q", f"the element count of {what}")
-            if count > self.size - self.pos:  # every element is at least one byte
-                raise GGUFFormatError(f"{self.path}: {what} claims {count} elements with "
-                                      f"{self.size - self.pos} bytes left")
-            if etype in _SCALAR:
-                fmt = _SCALAR[etype]
-                n = struct.calcsize(fmt) * count
-                p = self._need(n, what)
-                items = list(struct.unpack_from(f"<{count}{fmt[1]}", self.buf, p))
-            else:
-                items = [self.value(etype, f"{what}[{i}]", nested=True) for i in range(count)]
-            return GGUFArray(etype, items)
-        raise GGUFFormatError(f"{self.path}: {what}: unknown metadata value type {vtype}")
+    def u64(what):
+        return scalar(_VALUE_DTYPES[10], what)
+
+    def text(what):
+        n = u64(f"the length of {what}")
+        lo = span(n, what)
+        # tokenizer pieces need not be valid UTF-8: keep their bytes round-trippable
+        return bytes(buf[lo:lo + n]).decode("utf-8", "surrogateescape")
+
+    def value(vtype, what, in_array=False):
+        if vtype in _VALUE_DTYPES:
+            return scalar(_VALUE_DTYPES[vtype], what)
+        if vtype == _T_STRING:
+            return text(what)
+        if vtype != _T_ARRAY:
+            raise GGUFMalformed(f"{path}: {what} has value type {vtype}, which the format does not define")
+        if in_array:
+            raise GGUFUnsupported(f"{path}: {what} is an array of arrays; not read")
+        etype = u32(f"the element type of {what}")
+        count = u64(f"the length of {what}")
+        if count > end - at:  # every element takes at least a byte
+            raise GGUFMalformed(f"{path}: {what} says it holds {count} elements but {end - at} bytes remain")
+        if etype in _VALUE_DTYPES:
+            dt = _VALUE_DTYPES[etype]
+            items = np.frombuffer(buf, dt, count, span(dt.itemsize * count, what)).tolist()
+        else:
+            items = [value(etype, f"element {k} of {what}", True) for k in range(count)]
+        return MetadataArray(items, etype)
+
+    head = bytes(buf[span(4, "the magic number"):4])
+    if head != b"GGUF":
+        raise GGUFMalformed(f"{path}: starts with {head!r}; a GGUF file starts with b'GGUF'")
+    version = u32("the format version")
+    if version not in (2, 3):
+        swapped = int.from_bytes(version.to_bytes(4, "little"), "big")
+        if swapped in (1, 2, 3):
+            raise GGUFUnsupported(f"{path}: written big-endian (version word {version:#010x}); this reader takes "
+                                  "little-endian files")
+        raise GGUFUnsupported(f"{path}: format version {version}; versions 2 and 3 are read")
+    n_tensors = u64("the tensor count")
+    n_meta = u64("the metadata count")
+    if 8 * (n_tensors + n_meta) > end:
+        raise GGUFMalformed(f"{path}: the header lists {n_meta} metadata entries and {n_tensors} tensors, more "
+                            f"than {end} bytes can hold")
+    meta, vtypes = {}, {}
+    for k in range(n_meta):
+        key = text(f"the key of metadata entry {k}")
+        vtype = u32(f"the value type of metadata {key!r}")
+        if key in meta:
+            raise GGUFMalformed(f"{path}: metadata {key!r} is defined more than once")
+        meta[key] = value(vtype, f"metadata {key!r}")
+        vtypes[key] = vtype
+    align = meta.get("general.alignment", _ALIGN_DEFAULT)
+    if isinstance(align, bool) or not isinstance(align, int) or align <= 0 or align & (align - 1):
+        raise GGUFMalformed(f"{path}: general.alignment is {align!r}, not a positive power of two")
+    table = []
+    for k in range(n_tensors):
+        name = text(f"the name of tensor {k}")
+        rank = u32(f"the rank of {name!r}")
+        if not 1 <= rank <= _MAX_RANK:
+            raise GGUFMalformed(f"{path}: {name!r} has rank {rank}; GGUF tensors have 1 to {_MAX_RANK} extents")
+        extents = [u64(f"extent {d} of {name!r}") for d in range(rank)]
+        tid = u32(f"the GGML type of {name!r}")
+        rel = u64(f"the offset of {name!r}")
+        table.append((name, extents, tid, rel))
+    data_start = -(-at // align) * align
+    slots = {}
+    for name, extents, tid, rel in table:
+        if name in slots:
+            raise GGUFMalformed(f"{path}: two tensors are named {name!r}")
+        if rel % align:
+            raise GGUFMalformed(f"{path}: {name!r} starts at data offset {rel}, off the {align}-byte alignment")
+        count = int(np.prod(extents, dtype=np.int64))
+        t = GGML_TYPE_TABLE.get(tid)
+        size = None
+        if t is not None and t.block_elems is not None:
+            if extents[0] % t.block_elems:
+                raise GGUFMalformed(f"{path}: {name!r} is {t.name} but its first extent {extents[0]} does not "
+                                    f"divide into blocks of {t.block_elems}")
+            size = count // t.block_elems * t.block_bytes
+            if data_start + rel + size > end:
+                raise GGUFMalformed(f"{path}: {name!r} needs {size} bytes from byte {data_start + rel} and the "
+                                    f"file ends at {end} (cut short)")
+        slots[name] = TensorSlot(name, tid, extents, data_start + rel, size, count)
+    return version, meta, vtypes, align, data_start, slots
 
 
-class GGUFArray(list):
-    """A metadata array that remembers its element type."""
+class MetadataArray(list):
+    """A metadata array value; `element_type` is its GGUF value type id."""
 
-    def __init__(self, element_type, items):
+    def __init__(self, items, element_type):
         super().__init__(items)
         self.element_type = element_type
 
 
-class GGUFFile:
-    """A GGUF file, memory-mapped read-only.
+class GGUFContainer:
+    """A GGUF file opened read-only through a memory map.
 
-        with GGUFFile(path) as f:
-            f.metadata["general.architecture"]
-            f.tensors["blk.0.attn_q.weight"]   # GGUFTensorInfo
-            f.raw("blk.0.attn_q.weight")       # the stored bytes
+        with GGUFContainer(path) as g:
+            g.metadata["general.architecture"]
+            g.slot("blk.0.attn_q.weight")        # a TensorSlot
+            g.bytes_of("blk.0.attn_q.weight")    # its stored bytes (a view)
     """
 
     def __init__(self, path):
         self.path = os.fspath(path)
-        self._fh = open(self.path, "rb")
-        self._mm = None
+        self._file = open(self.path, "rb")
+        self._map = None
         try:
-            self.size = os.fstat(self._fh.fileno()).st_size
-            if self.size == 0:
-                raise GGUFFormatError(f"{self.path}: empty file, not GGUF")
-            self._mm = mmap.mmap(self._fh.fileno(), 0, access=mmap.ACCESS_READ)
-            self._parse()
+            if os.fstat(self._file.fileno()).st_size == 0:
+                raise GGUFMalformed(f"{self.path}: zero bytes long, so not a GGUF file")
+            self._map = mmap.mmap(self._file.fileno(), 0, access=mmap.ACCESS_READ)
+            (self.version, self.metadata, self.value_types, self.alignment, self.data_start,
+             self.tensors) = _scan(memoryview(self._map), self.path)
         except BaseException:
             self.close()
             raise
 
+    def slot(self, name: str) -> TensorSlot:
+        if name not in self.tensors:
+            raise KeyError(f"{self.path}: no tensor {name!r} in this file")
+        return self.tensors[name]
+
+    def bytes_of(self, name: str, strict: bool = True) -> memoryview:
+        """The stored bytes of `name`, a view into the map. Types declined as
+        tensors stay declined here unless strict=False; block formats without
+        a kernel are readable."""
+        sl = self.slot(name)
+        if strict:
+            err = why_refused(sl.type_id, name, as_tensor=False)
+            if err is not None:
+                raise err
+        if sl.size is None:
+            raise why_refused(sl.type_id, name) or GGUFUnsupported(f"tensor {name!r}: byte size unknown")
+        return memoryview(self._map)[sl.start:sl.start + sl.size]
+
     def close(self):
-        if self._mm is not None:
-            self._mm.close()
-            self._mm = None
-        if self._fh is not None:
-            self._fh.close()
-            self._fh = None
+        if self._map is not None:
+            try:
+                self._map.close()
+            except BufferError:  # a caller still holds a view; the map goes with it
+                pass
+            self._map = None
+        if self._file is not None:
+            self._file.close()
+            self._file = None
 
     def __enter__(self):
         return self
@@ -245,89 +325,8 @@ class GGUFFile:
     def __exit__(self, *exc):
         self.close()
 
-    def _parse(self):
-        r = _Reader(self._mm, self.size, self.path)
-        magic = bytes(self._mm[r._need(4, "the magic"):4])
-        if magic != _MAGIC:
-            raise GGUFFormatError(f"{self.path}: not a GGUF file (magic {magic!r}, expected {_MAGIC!r})")
-        version = r.unpack("<I", "the version")
-        if version not in (2, 3):
-            if struct.unpack(">I", struct.pack("<I", version))[0] in (1, 2, 3):
-                raise UnsupportedGGUF(f"{self.path}: a big-endian GGUF file (version field {version:#x}); only "
-                                      "little-endian files are read")
-            raise UnsupportedGGUF(f"{self.path}: GGUF version {version} is not read (2 and 3 are)")
-        self.version = version
-        n_tensors = r.unpack("<Q", "the tensor count")
-        n_kv = r.unpack("<Q", "the metadata count")
-        if 8 * (n_tensors + n_kv) > self.size:
-            raise GGUFFormatError(f"{self.path}: {n_kv} metadata entries and {n_tensors} tensors cannot fit in "
-                                  f"{self.size} bytes")
-        self.metadata, self.metadata_types = {}, {}
-        for i in range(n_kv):
-            key = r.string(f"metadata key #{i}")
-            vtype = r.unpack("<I", f"the value type of {key!r}")
-            if key in self.metadata:
-                raise GGUFFormatError(f"{self.path}: metadata key {key!r} appears twice")
-            self.metadata[key] = r.value(vtype, f"metadata {key!r}")
-            self.metadata_types[key] = vtype
-        align = self.metadata.get("general.alignment", _DEFAULT_ALIGNMENT)
-        if isinstance(align, bool) or not isinstance(align, int) or align <= 0 or align & (align - 1):
-            raise GGUFFormatError(f"{self.path}: general.alignment = {align!r} is not a power of two")
-        self.alignment = align
-        descs = []
-        for i in range(n_tensors):
-            name = r.string(f"tensor name #{i}")
-            nd = r.unpack("<I", f"the dimension count of {name!r}")
-            if not 1 <= nd <= _MAX_DIMS:
-                raise GGUFFormatError(f"{self.path}: tensor {name!r} has {nd} dimensions (1..{_MAX_DIMS} allowed)")
-            ne = [r.unpack("<Q", f"extent {d} of {name!r}") for d in range(nd)]
-            gt = r.unpack("<I", f"the type of {name!r}")
-            off = r.unpack("<Q", f"the data offset of {name!r}")
-            descs.append((name, ne, gt, off))
-        self.data_offset = (r.pos + align - 1) // align * align
-        self.tensors = {}
-        for name, ne, gt, off in descs:
-            if name in self.tensors:
-                raise GGUFFormatError(f"{self.path}: tensor {name!r} appears twice")
-            if off % align:
-                raise GGUFFormatError(f"{self.path}: tensor {name!r} at data offset {off}, not a multiple of "
-                                      f"the alignment {align}")
-            n = 1
-            for e in ne:
-                n *= e
-            t = GGML_TYPES.get(gt)
-            nbytes = None
-            if t is not None and t[1] is not None:
-                if ne[0] % t[1]:
-                    raise GGUFFormatError(f"{self.path}: tensor {name!r} is {t[0]} with a first extent of {ne[0]}, "
-                                          f"not a multiple of its block of {t[1]}")
-                nbytes = n // t[1] * t[2]
-                if self.data_offset + off + nbytes > self.size:
-                    raise GGUFFormatError(f"{self.path}: tensor {name!r} runs past the end of the file "
-                                          "(truncated)")
-            self.tensors[name] = GGUFTensorInfo(name, gt, ne, self.data_offset + off, nbytes, n)
-
-    def info(self, name) -> GGUFTensorInfo:
-        try:
-            return self.tensors[name]
-        except KeyError:
-            raise KeyError(f"{self.path} has no tensor named {name!r}") from None
-
-    def raw(self, name, refuse=True) -> memoryview:
-        """The stored bytes of `name` (GGML blocks or packed scalars), a view
-        of the map. Types refused as tensors by the reference stay refused
-        unless refuse=False; block formats without a kernel here are readable."""
-        info = self.info(name)
-        if refuse:
-            why = refusal(info.ggml_type, name, for_tensor=False)
-            if why is not None:
-                raise why
-        if info.nbytes is None:
-            raise refusal(info.ggml_type, name) or UnsupportedGGUF(f"tensor {name!r}: no known byte size")
-        return memoryview(self._mm)[info.offset:info.offset + info.nbytes]
-
     def __repr__(self):
-        return f"GGUFFile({self.path!r}, version={getattr(self, 'version', '?')}, tensors={len(self.tensors)})"
+        return f"GGUFContainer({self.path!r}, v{getattr(self, 'version', '?')}, {len(getattr(self, 'tensors', {}))} tensors)"
 
 
 # ----------------------------------------------------------------- to the device
@@ -367,7 +366,7 @@ def _unpermute_rows(rows2d, n_head: int):
 
     n = rows2d.shape[0]
     if n_head <= 0 or n % (2 * n_head):
-        raise UnsupportedGGUF(f"cannot undo the llama.cpp q/k row order of {n} rows for {n_head} heads")
+        raise GGUFUnsupported(f"cannot undo the llama.cpp q/k row order of {n} rows for {n_head} heads")
     dim = n // n_head // 2
     h = torch.arange(n_head).view(n_head, 1, 1)
     p = torch.arange(2).view(1, 2, 1)
@@ -376,7 +375,7 @@ def _unpermute_rows(rows2d, n_head: int):
     return rows2d.index_select(0, src)
 
 
-def load_tensor(f: GGUFFile, name: str, keep_blocks: bool = False, permute_heads: int | None = None,
+def load_tensor(f: GGUFContainer, name: str, keep_blocks: bool = False, permute_heads: int | None = None,
                 device="cuda"):
     """One tensor of `f` on `device` (reference: torchnative.gguf.load_tensor).
 
@@ -390,40 +389,40 @@ def load_tensor(f: GGUFFile, name: str, keep_blocks: bool = False, permute_heads
 
     from . import quant
 
-    info = f.info(name)
-    why = refusal(info.ggml_type, name)
+    info = f.slot(name)
+    why = why_refused(info.type_id, name)
     if why is not None:
         raise why
     dev = torch.device(device)
-    data = _to_device(f.raw(name), dev)
-    if info.kind == "dense":
-        t = data.view(getattr(torch, GGML_TYPES[info.ggml_type][4])).reshape(info.shape)
+    data = _to_device(f.bytes_of(name), dev)
+    if info.handling == "dense":
+        t = data.view(getattr(torch, GGML_TYPE_TABLE[info.type_id].target)).reshape(info.shape)
         if permute_heads is not None:
             t = _unpermute_rows(t.reshape(info.shape[0], -1), permute_heads).reshape(info.shape)
         return t
     rows = info.shape[0] if len(info.shape) > 1 else 1
     if permute_heads is not None:
         data = _unpermute_rows(data.view(rows, -1), permute_heads).reshape(-1).contiguous()
-    q = quant.QTensor(data, info.shape, info.format)
+    q = quant.QTensor(data, info.shape, info.block_format)
     return q if keep_blocks else quant._dequantize(q)
 
 
-def quantized_linear(f: GGUFFile, name: str, bias=None, device="cuda", permute_heads: int | None = None):
+def quantized_linear(f: GGUFContainer, name: str, bias=None, device="cuda", permute_heads: int | None = None):
     """A QuantizedLinear whose weight is tensor `name`'s own blocks on the
     device (reference: torchnative.gguf.quantized_linear). The tensor must be
     a 2-D block tensor, (out_features, in_features) in torch order; blocks run
     along in_features, the contracted dimension, so nothing is repacked."""
     from . import quant
 
-    info = f.info(name)
-    if info.kind != "block":
-        why = refusal(info.ggml_type, name)
+    info = f.slot(name)
+    if info.handling != "block":
+        why = why_refused(info.type_id, name)
         if why is not None:
             raise why
-        raise UnsupportedGGUF(f"tensor {name!r} is {info.type_name}, not a block-quantised type: build an "
+        raise GGUFUnsupported(f"tensor {name!r} is {info.type_name}, not a block-quantised type: build an "
                               "nn.Linear from load_tensor() instead")
     if len(info.shape) != 2:
-        raise UnsupportedGGUF(f"tensor {name!r} has shape {info.shape}; a linear weight is 2-D")
+        raise GGUFUnsupported(f"tensor {name!r} has shape {info.shape}; a linear weight is 2-D")
     out_features, in_features = info.shape
     qw = load_tensor(f, name, keep_blocks=True, permute_heads=permute_heads, device=device)
-    return quant.QuantizedLinear(in_features, out_features, qw, bias, info.format)
+    return quant.QuantizedLinear(in_features, out_features, qw, bias, info.block_format)

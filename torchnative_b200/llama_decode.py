@@ -75,10 +75,15 @@ class Q4LlamaDecoder:
     full from the seed and sliced, so every group size runs the same model)."""
 
     def __init__(self, shape: LlamaShape, batch: int, capacity: int, device, seed: int = 0,
-                 layers: int | None = None, tp=None, exchange: str = "p2p", weights: dict | None = None):
+                 layers: int | None = None, tp=None, exchange: str = "p2p", weights: dict | None = None,
+                 mega: bool | None = None):
         """`weights` (from `from_gguf`): the full model's tensors on `device`
         -- per layer attn_norm, qkv, o, mlp_norm, gate_up, down as below, plus
-        final_norm, lm_head, embed -- used instead of the seeded random ones."""
+        final_norm, lm_head, embed -- used instead of the seeded random ones.
+        `mega`: run each token as the one persistent kernel
+        (tn_llama_decode_token) -- True insists (one GPU, batch 1, a shape it
+        supports); None and False keep the launch-per-operator step, which
+        measures faster today."""
         from . import tp as tpm
 
         self.s = shape
@@ -188,6 +193,74 @@ class Q4LlamaDecoder:
         # waits); the attention, SiLU*up and logits gathers stay separate launches.
         self.fused_gather = self.fused and self.xchg is not None
         self._links = self._build_links()
+        self._mega = None
+        if mega and self.tp is None and batch == 1:
+            self._mega_plan()
+        elif mega:
+            raise NotImplementedError("the persistent decode kernel runs batch 1 on one GPU")
+
+    # ---- the persistent whole-token kernel (batch 1, one GPU)
+
+    def _mega_plan(self) -> None:
+        s, n = self.s, self.n_layers
+        lib = N.lib()
+        keep = []
+
+        def arr(ts):
+            a = (ctypes.c_void_p * n)(*[t.data_ptr() for t in ts])
+            keep.append(a)
+            return ctypes.cast(a, ctypes.POINTER(ctypes.c_void_p))
+
+        L = self.layers
+        m = N.LlamaQ4Model(layers=n, hidden=s.hidden, inter=s.inter, heads=s.heads, kv_heads=s.kv_heads,
+                           head_dim=s.head_dim, vocab=s.vocab, eps=s.eps, embed=self.embed.data_ptr(),
+                           final_norm=self.final_norm.data_ptr(), lm_head=self.lm_head.data_ptr(),
+                           attn_norm=arr([lw["attn_norm"] for lw in L]), qkv=arr([lw["qkv"] for lw in L]),
+                           o=arr([lw["o"] for lw in L]), mlp_norm=arr([lw["mlp_norm"] for lw in L]),
+                           gate_up=arr([lw["gate_up"] for lw in L]), down=arr([lw["down"] for lw in L]),
+                           k_cache=arr(self.k_cache), v_cache=arr(self.v_cache), capacity=self.cap,
+                           inv_freq=self.inv_freq.data_ptr())
+        lo = N.DecodeLayout()
+        N.check(lib.tn_llama_decode_layout_of(ctypes.byref(m), ctypes.byref(lo)))
+        self.mega_ws = torch.zeros(lo.total, dtype=torch.uint8, device=self.dev)
+        plan = ctypes.c_void_p()
+        N.check(lib.tn_llama_decode_plan(ctypes.byref(m), P(self.mega_ws.data_ptr()), lo.total, ctypes.byref(plan)))
+        self._mega, self._mega_layout, self._mega_keep = plan, lo, (m, keep)
+
+    @property
+    def mega(self) -> bool:
+        return self._mega is not None
+
+    def mega_views(self) -> dict:
+        """The persistent kernel's intermediates after a token (views of its
+        workspace): h, qkv, attn, o_out, act, down_out (bf16) and the planar
+        Q8_0 of attn (aq, ad, ac) and act (gq, gd, gc) -- the last layer's."""
+        lo, s, ws = self._mega_layout, self.s, self.mega_ws
+        HD, QKV = s.heads * s.head_dim, s.qkv
+
+        def v(off, n, dt):
+            return ws[off:off + n * torch.empty((), dtype=dt).element_size()].view(dt)
+
+        bf = torch.bfloat16
+        return {"h": v(lo.h, s.hidden, bf), "qkv": v(lo.qkv, QKV, bf), "attn": v(lo.attn, HD, bf),
+                "o_out": v(lo.o_out, s.hidden, bf), "act": v(lo.act, s.inter, bf),
+                "down_out": v(lo.down_out, s.hidden, bf), "aq": v(lo.aq, HD, torch.int8),
+                "ad": v(lo.ad, HD // 32, torch.float32), "ac": v(lo.ac, HD // 32, torch.float32),
+                "gq": v(lo.gq, s.inter, torch.int8), "gd": v(lo.gd, s.inter // 32, torch.float32),
+                "gc": v(lo.gc, s.inter // 32, torch.float32)}
+
+    def mega_trace_bytes(self) -> int:
+        return int(N.lib().tn_llama_decode_trace_bytes(self._mega))
+
+    def mega_reset(self) -> None:
+        """Zero the kernel's barrier counter, epoch and merge tickets (after a
+        launch that recorded a timeout)."""
+        N.check(N.lib().tn_llama_decode_reset(self._mega, self._stream()))
+
+    def _step_mega(self, stream, trace=None, trace_layer: int = -1) -> None:
+        N.check(N.lib().tn_llama_decode_token(self._mega, P(self.tokens.data_ptr()), P(self.pos.data_ptr()),
+                                              P(self.logits.data_ptr()), None if trace is None else
+                                              P(trace.data_ptr()), trace_layer, stream))
 
     def _off(self, full: torch.Tensor) -> int:
         return {self.attn.data_ptr(): self._off_attn, self.delta.data_ptr(): self._off_delta,
@@ -223,8 +296,12 @@ class Q4LlamaDecoder:
 
     def close(self) -> None:
         """Release the peer-memory exchange (call on every rank after a
-        barrier, with no step in flight and no graph left that uses it)."""
+        barrier, with no step in flight and no graph left that uses it) and
+        the persistent kernel's plan."""
         self._graph = None
+        if self._mega is not None:
+            N.lib().tn_llama_decode_plan_free(self._mega)
+            self._mega = None
         if self.xchg is not None:
             self.xchg.close()
             self.xchg = None
@@ -252,6 +329,8 @@ class Q4LlamaDecoder:
             extra = 2 if self.fused_gather else 4
         else:
             extra = 4 if (self.tp is not None and self.B > 1) else 0
+        if self._mega is not None:
+            return 0  # the whole token is one launch (kernels_per_step)
         if self.fused:
             # one GPU: gate/up also writes the planar Q8_0 of act (no quantiser launch)
             return (5 if self.tp is None else 6) + extra
@@ -259,6 +338,8 @@ class Q4LlamaDecoder:
 
     @property
     def kernels_per_step(self) -> int:
+        if self._mega is not None:
+            return 1
         if self.xchg is not None:
             extra = 2  # the logits gather and the epoch step
         else:
@@ -282,30 +363,30 @@ class Q4LlamaDecoder:
 
         dev = torch.device(device)
         bf = torch.bfloat16
-        with G.GGUFFile(path) as f:
+        with G.GGUFContainer(path) as f:
             md = f.metadata
             if md.get("general.architecture") != "llama":
-                raise G.UnsupportedGGUF(f"{f.path}: architecture {md.get('general.architecture')!r}; the decode "
+                raise G.GGUFUnsupported(f"{f.path}: architecture {md.get('general.architecture')!r}; the decode "
                                         "engine runs llama")
 
             def need(key):
                 if key not in md:
-                    raise G.GGUFFormatError(f"{f.path}: metadata {key!r} is missing")
+                    raise G.GGUFMalformed(f"{f.path}: metadata {key!r} is missing")
                 return md[key]
 
             H, I = int(need("llama.embedding_length")), int(need("llama.feed_forward_length"))
             heads = int(need("llama.attention.head_count"))
             kv = int(md.get("llama.attention.head_count_kv", heads))
             n_layers = int(need("llama.block_count"))
-            vocab = f.info("token_embd.weight").shape[0]
+            vocab = f.slot("token_embd.weight").shape[0]
             shape = LlamaShape(H, I, heads, kv, int(md.get("llama.attention.key_length", H // heads)), vocab, n_layers,
                                float(md.get("llama.rope.freq_base", 10000.0)),
                                float(md.get("llama.attention.layer_norm_rms_epsilon", 1e-5)))
 
             def q4(name, heads_perm=None):
-                info = f.info(name)
-                if info.format != "q4_0":
-                    raise G.UnsupportedGGUF(f"{f.path}: {name} is {info.type_name}; the decode engine's linears "
+                info = f.slot(name)
+                if info.block_format != "q4_0":
+                    raise G.GGUFUnsupported(f"{f.path}: {name} is {info.type_name}; the decode engine's linears "
                                             "are Q4_0")
                 return G.load_tensor(f, name, keep_blocks=True, permute_heads=heads_perm, device=dev).blob
 
@@ -374,6 +455,8 @@ class Q4LlamaDecoder:
         """One token for every sequence: reads tokens' embeddings in self.h and
         the position self.pos; leaves the next tokens in self.tokens, their
         embeddings in self.h, and self.pos advanced by one."""
+        if self._mega is not None:
+            return self._step_mega(stream or self._stream())
         if self.fused:
             return self._step_fused(stream or self._stream())
         L, s, B = N.lib(), self.s, self.B
@@ -513,7 +596,7 @@ class Q4LlamaDecoder:
         the fused step, each running that launch once per layer with the
         step's own arguments (so 32 back-to-back launches over 32 layers'
         weights). Reads and writes the step's buffers; re-seed afterwards."""
-        if not self.fused or self.tp is not None:
+        if not self.fused or self.tp is not None or self._mega is not None:
             return {}
         L, s, B = N.lib(), self.s, self.B
         D, Hq, Hkv, H, I = s.head_dim, s.heads, s.kv_heads, s.hidden, s.inter
@@ -547,12 +630,25 @@ class Q4LlamaDecoder:
         torch.cuda.current_stream(self.dev).wait_stream(side)
         return graphs
 
-    def capture(self) -> torch.cuda.CUDAGraph:
+    def capture(self):
         """One eager step first, on the stream the capture will use (the
         library's workspaces are per stream, and are sized by that step;
         nothing may allocate while capturing), then the step captured as a
         CUDA graph on that stream. The eager step advances the state, so
-        callers re-seed (fill_prompt_cache / start) afterwards."""
+        callers re-seed (fill_prompt_cache / start) afterwards. With the
+        persistent kernel a token is one launch already: the returned object's
+        replay() launches it directly (no graph to build)."""
+        if self._mega is not None:
+            self.step()
+            torch.cuda.current_stream(self.dev).synchronize()
+            dec = self
+
+            class _Direct:
+                def replay(self):
+                    dec.step()
+
+            self._graph = _Direct()
+            return self._graph
         side = torch.cuda.Stream(self.dev)
         side.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(side):

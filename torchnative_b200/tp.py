@@ -84,6 +84,14 @@ def shard_gate_up_pairs(blob: torch.Tensor, inter: int, k: int, rank: int, world
     return row_slice(blob, 2 * inter, k, 2 * rank * c, 2 * (rank + 1) * c)
 
 
+class PeerLost(TimeoutError):
+    """A rank of the tensor-parallel group did not take part in a collective:
+    it left, or did not arrive within the process group's timeout."""
+
+
+_LOST_SIGNS = ("timed out", "timeout", "connection closed", "connection reset", "broken pipe", "peer")
+
+
 @dataclass
 class TPGroup:
     """One tensor-parallel group: this process's rank, the group size and the
@@ -98,11 +106,17 @@ class TPGroup:
         inside a CUDA-graph capture); gloo (CPU tests): the list form."""
         import torch.distributed as dist
 
-        if dist.get_backend(self.group) == "gloo":
-            parts = list(out.view(self.world, -1).unbind(0))
-            dist.all_gather(parts, inp.reshape(-1), group=self.group)
-            return
-        dist.all_gather_into_tensor(out, inp, group=self.group)
+        try:
+            if dist.get_backend(self.group) == "gloo":
+                parts = list(out.view(self.world, -1).unbind(0))
+                dist.all_gather(parts, inp.reshape(-1), group=self.group)
+                return
+            dist.all_gather_into_tensor(out, inp, group=self.group)
+        except RuntimeError as e:
+            if any(sign in str(e).lower() for sign in _LOST_SIGNS):
+                raise PeerLost(f"tensor-parallel all-gather, rank {self.rank} of {self.world}: a peer rank did not "
+                               f"take part ({e})") from e
+            raise
 
 
 def gather_rows(tp: TPGroup, local: torch.Tensor, full: torch.Tensor, scratch: torch.Tensor | None,
