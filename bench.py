@@ -17,7 +17,11 @@ one CUDA graph, replayed.
 
 Prints one JSON line (rank 0). `value` is device-resident tokens/s; `e2e`
 adds, every step, the pinned host->device copy of the input token ids, their
-embedding, and the device->host copy of the next token ids.
+embedding, and the device->host copy of the next token ids. The same line
+carries, at every N (tensor-parallel over the same group when N > 1), the
+batch-16 step (`decode_batch16`) and the Llama-3-70B-shaped batch-32 step over
+an 8192-slot cache (`llama3_70b_b32`); on one GPU also
+the op-level figures (`op_level`).
 """
 
 from __future__ import annotations
@@ -54,6 +58,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ops", action="store_true", help="skip the op-level BASELINE figures (configs[1], [2])")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the batch-16 and Llama-3-70B batch-32 decode lines (BASELINE configs[3] at batch 16, "
+                         "configs[4])")
     ap.add_argument("--mega", action="store_true", help="run the step as the one persistent kernel per token "
                                                         "(tn_llama_decode_token) instead of the launch-per-operator graph")
     ap.add_argument("--case", default=None, choices=["gemv", "gemm", "sdpa_decode", "sdpa_prefill"],
@@ -608,30 +615,45 @@ def op_level(dev) -> dict:
                                         "frac_bf16": round(tfl / tf, 3)})
             del q, kk, vv, out, lse
         torch.cuda.empty_cache()
-    res["decode_batch16"] = batched_decode(dev, 16)
     N.device_status(reset=True)
     return res
 
 
-def batched_decode(dev, B: int, steps: int = 10, warmup: int = 3) -> dict:
-    """BASELINE configs[3] at batch B on one GPU: the decode step of B
-    sequences (the batched path: tcgen05 skinny Q4_0 kernel from 9 rows),
-    replayed as one CUDA graph, CUDA events; tok/s and the step's HBM fraction."""
+def decode_config(dev, shape, B: int, cache: int, steps: int, warmup: int, rank: int = 0, world: int = 1,
+                  exchange: str = "p2p", seed: int = 99) -> dict:
+    """One BASELINE decode configuration on this rank's GPU (tensor-parallel
+    over the process group when world > 1): `shape` (Llama-3-8B or -70B),
+    batch B, every sequence's KV cache `cache` slots long with the prompt
+    filling all but the slots the timed steps append. The step replayed as
+    one CUDA graph; CUDA events on the replay stream between barriers, max
+    over ranks. tok/s counts the B tokens of a step; the HBM fraction is this
+    rank's bytes (its weight shards, its KV heads of the cache) over its time,
+    against the measured copy peak."""
     import torch
 
-    from torchnative_b200.llama_decode import LLAMA3_8B, Q4LlamaDecoder
+    from torchnative_b200.llama_decode import Q4LlamaDecoder
 
-    cap = PROMPT + warmup + steps + 8
-    dec = Q4LlamaDecoder(LLAMA3_8B, batch=B, capacity=cap, device=dev, seed=99)
-    first = torch.randint(0, LLAMA3_8B.vocab, (B,), device=dev, dtype=torch.int32)
-    dec.fill_prompt_cache(PROMPT)
+    tp = None
+    if world > 1:
+        import torch.distributed as dist
+
+        from torchnative_b200.tp import TPGroup
+
+        tp = TPGroup(rank, world, dist.group.WORLD)
+    prompt = cache - (warmup + steps + 2)
+    torch.cuda.empty_cache()
+    dec = Q4LlamaDecoder(shape, batch=B, capacity=cache, device=dev, seed=seed, tp=tp, exchange=exchange)
+    gen = torch.Generator(device=dev).manual_seed(seed)  # the same first tokens on every rank
+    first = torch.randint(0, shape.vocab, (B,), device=dev, dtype=torch.int32, generator=gen)
+    dec.fill_prompt_cache(prompt)
     dec.start(first)
     g = dec.capture()
-    dec.fill_prompt_cache(PROMPT)
+    dec.fill_prompt_cache(prompt)
     dec.start(first)
     for _ in range(warmup):
         g.replay()
     torch.cuda.synchronize()
+    barrier(world)
     pos0 = int(dec.pos.item())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -639,18 +661,45 @@ def batched_decode(dev, B: int, steps: int = 10, warmup: int = 3) -> dict:
         g.replay()
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    assert int(dec.pos.item()) == pos0 + steps, "the step did not advance the cache"
     hbm, _ = measured_peaks()
     step_bytes = dec.weight_bytes + dec.kv_bytes(int(pos0 + (steps + 1) / 2))
-    out = {"batch": B, "tok_s": round(B * 1000.0 / ms, 1), "ms_per_step": round(ms, 4),
-           "step_hbm_frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 3), "bytes_per_step": step_bytes,
+    out = {"model": f"{shape.layers} layers, hidden {shape.hidden}, {shape.heads}/{shape.kv_heads} heads, "
+                    f"MLP {shape.inter}, vocab {shape.vocab}",
+           "batch": B, "kv_cache_slots": cache, "mean_context": pos0 + (steps + 1) / 2.0, "n_gpus": world,
+           "parallelism": f"tp{world}", "steps": steps, "warmup": warmup,
+           "tok_s": round(B * 1000.0 / ms, 1), "ms_per_step": round(ms, 4),
+           "step_hbm_frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 3), "bytes_per_step_per_gpu": step_bytes,
            "kernels_per_step": dec.kernels_per_step}
     dec._graph = None
     del g
+    torch.cuda.synchronize()
+    barrier(world)
     dec.close()
     del dec
     torch.cuda.empty_cache()
     return out
+
+
+def batched_decode(dev, B: int, steps: int = 10, warmup: int = 3, rank: int = 0, world: int = 1,
+                   exchange: str = "p2p") -> dict:
+    """BASELINE configs[3] at batch B: the Llama-3-8B-shaped decode step of B
+    sequences over a PROMPT-token cache (from 9 rows the batched path: the
+    tcgen05 skinny Q4_0 kernel)."""
+    from torchnative_b200.llama_decode import LLAMA3_8B
+
+    return decode_config(dev, LLAMA3_8B, B, PROMPT + warmup + steps + 2, steps, warmup, rank, world, exchange)
+
+
+def llama70b_decode(dev, steps: int = 6, warmup: int = 3, rank: int = 0, world: int = 1,
+                    exchange: str = "p2p") -> dict:
+    """the Llama-3-70B-shaped decoder (80 layers, hidden
+    8192, 64/8 heads, MLP 28672; ~39 GB of Q4_0 weights), batch 32, an
+    8192-slot KV cache per sequence (~86 GB in bf16 on one GPU)."""
+    from torchnative_b200.llama_decode import LLAMA3_70B
+
+    return decode_config(dev, LLAMA3_70B, 32, 8192, steps, warmup, rank, world, exchange, seed=70)
 
 
 def _measured_tflops() -> float:
@@ -724,10 +773,16 @@ def main():
         return
     rank, world, local = dist_setup(args)
     res = run_ours(args, rank, world, local)
-    if rank == 0 and world == 1 and not args.no_ops:
-        import torch
+    import torch
 
-        res["op_level"] = op_level(torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    if rank == 0 and world == 1 and not args.no_ops:
+        res["op_level"] = op_level(dev)
+    if not args.no_configs:
+        # BASELINE configs[3] at batch 16 and configs[4] (70B, batch 32, 8192-slot
+        # cache), tensor-parallel over the same group at N > 1: every rank runs them
+        res["decode_batch16"] = batched_decode(dev, 16, rank=rank, world=world, exchange=args.exchange)
+        res["llama3_70b_b32"] = llama70b_decode(dev, rank=rank, world=world, exchange=args.exchange)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -107,11 +107,11 @@ def test_tcgen05_prefill_at_baseline_sizes(tn, cuda_device, B, S, dtype):
     N.device_status(reset=True)
 
 
-def _decode_inputs(cuda_device, B, S, dtype, cap):
+def _decode_inputs(cuda_device, B, S, dtype, cap, hq=HQ):
     g = torch.Generator(device=cuda_device).manual_seed(S * 7 + B)
     kbuf = torch.randn((B, HKV, cap, D), device=cuda_device, generator=g).to(DT[dtype])
     vbuf = torch.randn((B, HKV, cap, D), device=cuda_device, generator=g).to(DT[dtype])
-    q = torch.randn((B, HQ, 1, D), device=cuda_device, generator=g).to(DT[dtype])
+    q = torch.randn((B, hq, 1, D), device=cuda_device, generator=g).to(DT[dtype])
     return q, kbuf, vbuf
 
 
@@ -122,7 +122,7 @@ def _decode_groups(B):
 def _check_decode_groups(q, k, v, out, lse, S, dtype, label):
     """q [B, Hq, 1, D] (rounded), k/v [B, Hkv, >= S, D]: the first S keys."""
     B = q.shape[0]
-    rep = HQ // HKV
+    rep = q.shape[1] // HKV
     for b, hk in _decode_groups(B):
         qg = q[b:b + 1, hk * rep:(hk + 1) * rep].cpu()
         kg = k[b:b + 1, hk:hk + 1, :S].cpu()
@@ -166,6 +166,28 @@ def test_split_kv_decode_at_baseline_sizes(tn, cuda_device, B, S, dtype):
                                          1.0 / math.sqrt(D), P(torch.cuda.current_stream().cuda_stream)))
     torch.cuda.synchronize()
     _check_decode_groups(q, kbuf, vbuf, out2, lse2, S, dtype, f"decode_cache B{B} S{S}")
+    N.device_status(reset=True)
+
+
+def test_split_kv_decode_at_the_70b_shape(tn, cuda_device):
+    """BASELINE configs[4]'s attention: 64 query / 8 KV heads (a GQA group of
+    8 rows per KV head), batch 32, an 8192-slot cache, bf16, through
+    tn_sdpa_decode_cache with the length on the device."""
+    N, _ = tn
+    B, S, hq, dtype = 32, 8192, 64, "bfloat16"
+    cap = S
+    q, kbuf, vbuf = _decode_inputs(cuda_device, B, S, dtype, cap, hq=hq)
+    out = torch.empty_like(q)
+    lse = torch.empty((B, hq, 1), device=cuda_device)
+    ln = torch.tensor([S - 1], dtype=torch.int32, device=cuda_device)
+    qs = (ctypes.c_int64 * 4)(q.stride(0), q.stride(1), 0, 1)
+    ks = (ctypes.c_int64 * 4)(*kbuf.stride())
+    N.check(N.lib().tn_sdpa_decode_cache(P(q.data_ptr()), P(kbuf.data_ptr()), P(vbuf.data_ptr()), P(out.data_ptr()),
+                                         P(lse.data_ptr()), N.TN_BF16, B, hq, HKV, D, cap, qs, ks, ks,
+                                         P(ln.data_ptr()), 1, 1.0 / math.sqrt(D),
+                                         P(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    _check_decode_groups(q, kbuf, vbuf, out, lse, S, dtype, "70B shape B32 S8192")
     N.device_status(reset=True)
 
 

@@ -260,7 +260,8 @@ class QuantizedLinear(torch.nn.Module):
             out_features //= world
         bias = mod.bias
         if bias is not None and shard is not None and bias.device.type != "meta":
-            bias = bias.detach()[shard[0] * out_features:(shard[0] + 1) * out_features]
+            bias = torch.nn.Parameter(bias.detach()[shard[0] * out_features:(shard[0] + 1) * out_features].clone(),
+                                      requires_grad=False)
         self = cls(in_features, out_features, None, bias, fmt)
         self.shard = shard
         self.register_parameter("weight", mod.weight)
@@ -300,6 +301,12 @@ class QuantizedLinear(torch.nn.Module):
             self.qweight = _quantize(weight, self.format)
         if "weight" in self._parameters:
             del self._parameters["weight"]
+        # a bias the loader filled in full before the weight arrived: keep this
+        # rank's slice of it too
+        b = self.bias
+        if shard is not None and b is not None and b.device.type != "meta" and b.numel() == rows:
+            r0 = shard[0] * self.out_features
+            self.bias = torch.nn.Parameter(b.detach()[r0:r0 + self.out_features].clone(), requires_grad=False)
 
     def _apply(self, fn, recurse=True):
         result = super()._apply(fn, recurse)
