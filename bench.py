@@ -75,6 +75,10 @@ def parse():
     ap.add_argument("--seqs", default="512,4096,16384", help="sequence lengths for --case sdpa_prefill")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="tensor-parallel all-gather: peer-memory kernel or NCCL")
+    ap.add_argument("--tp-plan", default="rowwise", choices=["rowwise", "colwise"],
+                    help="tensor-parallel plan at batch <= 4 with the peer-memory exchange: o_proj/down_proj "
+                         "row-parallel with the all-reduce fused into the GEMV (rowwise), or every linear "
+                         "column-sharded with an all-gather after each (colwise)")
     return ap.parse_args()
 
 
@@ -293,7 +297,7 @@ def run_ours(args, rank, world, local):
 
         tp = TPGroup(rank, world, dist.group.WORLD)
     dec = Q4LlamaDecoder(LLAMA3_8B, batch=B, capacity=cap, device=dev, seed=1234, tp=tp, exchange=args.exchange,
-                         mega=True if (args.mega and world == 1 and B == 1) else None)
+                         mega=True if (args.mega and world == 1 and B == 1) else None, tp_plan=args.tp_plan)
     P = ctypes.c_void_p
     cur = lambda: P(torch.cuda.current_stream().cuda_stream)  # noqa: E731
     first = torch.randint(0, LLAMA3_8B.vocab, (B,), device=dev, dtype=torch.int32)
@@ -453,9 +457,12 @@ def run_ours(args, rank, world, local):
                                "growing one slot per step",
                    "model": "Llama-3-8B-shaped (32 layers, 4096 hidden, 32/8 heads, D 128, MLP 14336, vocab 128256)",
                    "global_batch": B, "seq_len": PROMPT,
-                   "parallelism": f"tp{world} (column-sharded Q4_0 linears, KV-head-group attention, "
-                                  f"{'peer-memory' if args.exchange == 'p2p' else 'NCCL'} all-gather after each "
-                                  "sharded output)" if world > 1 else "tp1",
+                   "parallelism": (f"tp{world} (rowwise: q/k/v, gate/up and lm_head column-sharded, "
+                                   "KV-head-group attention, o_proj/down_proj row-parallel with the all-reduce "
+                                   "fused into the GEMV over peer memory; logits all-gathered)" if dec.rowwise else
+                                   f"tp{world} (column-sharded Q4_0 linears, KV-head-group attention, "
+                                   f"{'peer-memory' if args.exchange == 'p2p' else 'NCCL'} all-gather after each "
+                                   "sharded output)") if world > 1 else "tp1",
                    "l2": "inputs larger than L2 (4.22 GB of weights per step)",
                    "mean_context": mean_ctx, "bytes_per_step": step_bytes,
                    "hbm_roofline_tok_s": B * peak * 1e9 / step_bytes},
@@ -620,7 +627,7 @@ def op_level(dev) -> dict:
 
 
 def decode_config(dev, shape, B: int, cache: int, steps: int, warmup: int, rank: int = 0, world: int = 1,
-                  exchange: str = "p2p", seed: int = 99) -> dict:
+                  exchange: str = "p2p", seed: int = 99, tp_plan: str = "rowwise") -> dict:
     """One BASELINE decode configuration on this rank's GPU (tensor-parallel
     over the process group when world > 1): `shape` (Llama-3-8B or -70B),
     batch B, every sequence's KV cache `cache` slots long with the prompt
@@ -642,7 +649,8 @@ def decode_config(dev, shape, B: int, cache: int, steps: int, warmup: int, rank:
         tp = TPGroup(rank, world, dist.group.WORLD)
     prompt = cache - (warmup + steps + 2)
     torch.cuda.empty_cache()
-    dec = Q4LlamaDecoder(shape, batch=B, capacity=cache, device=dev, seed=seed, tp=tp, exchange=exchange)
+    dec = Q4LlamaDecoder(shape, batch=B, capacity=cache, device=dev, seed=seed, tp=tp, exchange=exchange,
+                         tp_plan=tp_plan)
     gen = torch.Generator(device=dev).manual_seed(seed)  # the same first tokens on every rank
     first = torch.randint(0, shape.vocab, (B,), device=dev, dtype=torch.int32, generator=gen)
     dec.fill_prompt_cache(prompt)
@@ -668,7 +676,8 @@ def decode_config(dev, shape, B: int, cache: int, steps: int, warmup: int, rank:
     out = {"model": f"{shape.layers} layers, hidden {shape.hidden}, {shape.heads}/{shape.kv_heads} heads, "
                     f"MLP {shape.inter}, vocab {shape.vocab}",
            "batch": B, "kv_cache_slots": cache, "mean_context": pos0 + (steps + 1) / 2.0, "n_gpus": world,
-           "parallelism": f"tp{world}", "steps": steps, "warmup": warmup,
+           "parallelism": f"tp{world}" + (" rowwise" if dec.rowwise else " colwise" if world > 1 else ""),
+           "steps": steps, "warmup": warmup,
            "tok_s": round(B * 1000.0 / ms, 1), "ms_per_step": round(ms, 4),
            "step_hbm_frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 3), "bytes_per_step_per_gpu": step_bytes,
            "kernels_per_step": dec.kernels_per_step}

@@ -507,7 +507,21 @@ TN_API int tn_tp_step_end(void *local_base, void *stream);
  * bounded, until every rank's producer of wait_slot has signalled this step
  * before reading its activations. Slots share the numbering of
  * tn_tp_allgather; a slot is fed either by tn_tp_allgather or by fused
- * producers, never both. */
+ * producers, never both.
+ *
+ * reduce = 1 makes the GEMV a row-parallel linear with its all-reduce fused
+ * in (transformers' "rowwise" plan: each rank holds a K-slice of the weight,
+ * whole Q4_0 blocks of every row): every CTA stores its f32 partial outputs
+ * into every rank's [M][dst_row_stride] buffer at row m, columns
+ * [rank*N, (rank+1)*N) (dst_row_stride >= world*N), signals its own counter
+ * in every rank's region, waits (bounded) for the same CTA of every rank,
+ * then writes y = sum over ranks g = 0..world-1, in that order, of the
+ * partials -- the same bits on every rank. `slot` numbers the reductions of
+ * a step (< TN_TP_REDUCE_SLOTS, each once per step); consecutive reductions
+ * must alternate between two buffers. No bias, no pair epilogue, wait_slot
+ * -1. The result differs from the one-GPU linear only in the association of
+ * its f32 sum (within the same counted bound). */
+#define TN_TP_REDUCE_SLOTS 256
 typedef struct {
     int world, rank;
     void *bases[8];
@@ -515,6 +529,8 @@ typedef struct {
     int64_t dst_row_stride;
     int slot;
     int wait_slot;
+    int reduce;
+    int reserved;
 } tn_tp_link;
 TN_API int tn_q4_0_linear_q8_tp(const int8_t *codes, int64_t codes_row_stride, const float *scales,
                                 const float *offsets, const void *w_blob, const float *bias, void *y,

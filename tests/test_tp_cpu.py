@@ -83,6 +83,26 @@ def _worker(rank, world, port, failures):
                              np.ascontiguousarray(vc[:, rank * hkv:(rank + 1) * hkv]), dtype="float32")
         o = _gather_np(g, o_l.reshape(B, hq * D), world)
         assert np.array_equal(o, o_full.reshape(B, Hq * D)), "KV-head-group attention"
+        # row-parallel o_proj / down_proj (the rowwise plan): rank r's input
+        # features [r K/G, (r+1) K/G) -- its own heads' attention output -- give
+        # an f32 partial; the partials summed in rank order stay within the
+        # counted bound of the unsharded linear, with G more additions
+        K = Hq * D
+        wo = _blob(rng, H, K)
+        wo_l = tpm.shard_cols(wo, H, K, rank, world)
+        xo = o_full.reshape(B, K)
+        kc_ = K // world
+        part = oracle.q4_0_linear(np.ascontiguousarray(xo[:, rank * kc_:(rank + 1) * kc_]), wo_l.numpy().tobytes(), H)
+        parts = _gather_np(g, part, world).reshape(B, world, H)
+        y = np.zeros((B, H), dtype=np.float32)
+        for r_ in range(world):
+            y = (y + parts[:, r_]).astype(np.float32)
+        exact, abs_sum, ref_err = q4_exact.exact_linear_q4_0(oracle.q8_0_quantize(xo), wo.numpy().tobytes(), B, H, K)
+        bound = q4_exact.linear_bound(K + 32 * world, abs_sum, ref_err)
+        assert float(np.max(np.abs(y.astype(np.float64) - exact) / bound)) <= 1.0, "row-parallel partial sums"
+        # every output row's blocks are split, none re-encoded
+        assert np.array_equal(wo_l.numpy().reshape(H, K // 32 // world, 18),
+                              wo.numpy().reshape(H, K // 32, 18)[:, rank * (K // 32 // world):(rank + 1) * (K // 32 // world)])
     except AssertionError as e:
         failures.put(f"rank {rank}: {e}")
         raise
@@ -116,6 +136,10 @@ def test_shard_refusals():
     with pytest.raises(ValueError, match="is not"):
         tpm.row_slice(w[:-1], 10, 32, 0, 1)
     assert tpm.shard_rows(w, 10, 32, 1, 2).numel() == 5 * 18
+    w2 = torch.zeros(2 * 3 * 18, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="does not divide"):
+        tpm.shard_cols(w2, 2, 96, 0, 2)  # 3 blocks per row over 2 ranks
+    assert tpm.shard_cols(w2, 2, 96, 2, 3).numel() == 2 * 18
 
 
 def _leaving_worker(rank, world, port, result):

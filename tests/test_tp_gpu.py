@@ -122,7 +122,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _run(rank, world, port, batch, steps, exchange, out):
+def _run(rank, world, port, batch, steps, exchange, out, tp_plan="colwise", forced=None):
     import datetime
 
     import torch.distributed as dist
@@ -139,20 +139,27 @@ def _run(rank, world, port, batch, steps, exchange, out):
         build.build()
         shape = LlamaShape(**_small(world))
         dec = Q4LlamaDecoder(shape, batch=batch, capacity=64, device=f"cuda:{rank}", seed=3,
-                             tp=TPGroup(rank, world, dist.group.WORLD), exchange=exchange)
+                             tp=TPGroup(rank, world, dist.group.WORLD), exchange=exchange, tp_plan=tp_plan)
+        assert dec.rowwise == (tp_plan == "rowwise" and exchange == "p2p")
+        # both places of the SiLU*up quantiser: gate/up's epilogue at batch 1,
+        # down_proj's prologue at batch 2 (the small model alone would pick the latter)
+        dec.rowwise_q8out = batch == 1
         first = torch.arange(batch, device=f"cuda:{rank}", dtype=torch.int32) * 7 + 1
         dec.fill_prompt_cache(16)
         dec.start(first)
         g = dec.capture()
         dec.fill_prompt_cache(16)
         dec.start(first)
-        toks = []
-        for _ in range(steps):
+        toks, logits = [], []
+        for i in range(steps):
+            if forced is not None:  # teacher forcing: this step's input tokens from the one-GPU run
+                dec.start(torch.tensor(forced[i], device=f"cuda:{rank}", dtype=torch.int32))
             g.replay()
             toks.append(dec.tokens.clone())
+            logits.append(dec.logits.float().clone())
         torch.cuda.synchronize()
         if rank == 0:
-            out.put(torch.stack(toks).cpu().tolist())
+            out.put((torch.stack(toks).cpu().tolist(), torch.stack(logits).cpu()))
         # a graph holding NCCL calls must be gone before the process group is,
         # and no rank may free its exchange region while a peer still writes it
         dec._graph = None
@@ -164,16 +171,12 @@ def _run(rank, world, port, batch, steps, exchange, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
-@pytest.mark.parametrize("batch", [1, 2])
-@pytest.mark.parametrize("world", WORLDS)
-def test_tp_decode_matches_one_gpu(cuda_device, world, batch, exchange):
-    _need(world)
+def _one_gpu(cuda_device, world, batch, steps):
+    """The same seeded model on one GPU, free-running: tokens and logits per step."""
     from torchnative_b200 import build
     from torchnative_b200.llama_decode import LlamaShape, Q4LlamaDecoder
 
     build.build()
-    steps = 6
     dec = Q4LlamaDecoder(LlamaShape(**_small(world)), batch=batch, capacity=64, device=cuda_device, seed=3)
     first = torch.arange(batch, device=cuda_device, dtype=torch.int32) * 7 + 1
     dec.fill_prompt_cache(16)
@@ -181,18 +184,23 @@ def test_tp_decode_matches_one_gpu(cuda_device, world, batch, exchange):
     g = dec.capture()
     dec.fill_prompt_cache(16)
     dec.start(first)
-    want = []
+    toks, logits = [], []
     for _ in range(steps):
         g.replay()
-        want.append(dec.tokens.clone())
-    want = torch.stack(want).cpu().tolist()
+        toks.append(dec.tokens.clone())
+        logits.append(dec.logits.float().clone())
+    toks, logits = torch.stack(toks).cpu().tolist(), torch.stack(logits).cpu()
     dec._graph = None
     del g, dec
+    return first.cpu().tolist(), toks, logits
+
+
+def _spawn_ranks(world, batch, steps, exchange, tp_plan, forced=None):
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, batch, steps, exchange, out), daemon=True)
-             for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, batch, steps, exchange, out, tp_plan, forced),
+                         daemon=True) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -205,4 +213,49 @@ def test_tp_decode_matches_one_gpu(cuda_device, world, batch, exchange):
             if p.is_alive():
                 p.kill()
                 p.join(timeout=10)
+    return got
+
+
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+@pytest.mark.parametrize("batch", [1, 2])
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_decode_matches_one_gpu(cuda_device, world, batch, exchange):
+    """The colwise plan (every linear column-sharded, an all-gather after each):
+    a column shard changes which rank computes an output, never how, so the
+    token stream is the one-GPU stream exactly."""
+    _need(world)
+    steps = 6
+    _, want, _ = _one_gpu(cuda_device, world, batch, steps)
+    got, _ = _spawn_ranks(world, batch, steps, exchange, "colwise")
     assert got == want
+
+
+# The rowwise plan sums o_proj's and down_proj's rank partials: the same
+# terms as one GPU in another association (each partial within the counted
+# bound, then G more f32 additions), which can move a bf16 rounding of the
+# residual by one unit and, through the next Q8_0 quantiser, one activation
+# code. Logits are compared per step under teacher forcing (both sides read
+# the one-GPU run's tokens), within 4 bf16 units of the step's largest |logit|;
+# the greedy token must agree wherever the one-GPU run's top two logits are
+# further apart than that.
+def _bf16_ulps(x: torch.Tensor) -> torch.Tensor:
+    return torch.exp2(torch.floor(torch.log2(x.abs().clamp_min(1e-30))) - 7)
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_rowwise_decode_matches_one_gpu_within_the_reduction_order(cuda_device, world, batch):
+    _need(world)
+    steps = 6
+    first, want, want_logits = _one_gpu(cuda_device, world, batch, steps)
+    forced = [first] + want[:-1]
+    got, got_logits = _spawn_ranks(world, batch, steps, "p2p", "rowwise", forced)
+    for i in range(steps):
+        for b in range(batch):
+            ref, tp = want_logits[i, b], got_logits[i, b]
+            tol = 4 * float(_bf16_ulps(ref.abs().max()))
+            diff = float((ref - tp).abs().max())
+            assert diff <= tol, f"step {i} row {b}: max |logit difference| {diff:.3e} > {tol:.3e}"
+            top2 = torch.topk(ref, 2).values
+            if float(top2[0] - top2[1]) > 2 * tol:
+                assert got[i][b] == want[i][b], f"step {i} row {b}: token {got[i][b]} != {want[i][b]}"

@@ -33,10 +33,11 @@ _P, _I, _I64, _SZ, _D = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_
 
 class TpLink(ctypes.Structure):
     """tn_tp_link (include/torchnative_b200.h): a GEMV's place in a
-    tensor-parallel gather, as producer (slot) and/or consumer (wait_slot)."""
+    tensor-parallel gather, as producer (slot) and/or consumer (wait_slot), or
+    (reduce = 1) a row-parallel linear with its all-reduce fused in."""
     _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("bases", ctypes.c_void_p * 8),
                 ("dst_offset", ctypes.c_int64), ("dst_row_stride", ctypes.c_int64), ("slot", ctypes.c_int),
-                ("wait_slot", ctypes.c_int)]
+                ("wait_slot", ctypes.c_int), ("reduce", ctypes.c_int), ("reserved", ctypes.c_int)]
 _PI64 = ctypes.POINTER(ctypes.c_int64)
 
 

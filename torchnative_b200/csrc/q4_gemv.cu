@@ -71,7 +71,10 @@ struct GemvParams {
     int64_t xb_row_stride;       // elements
     // Tensor parallelism (tn_tp_link): scatter the output into every rank's
     // exchange region (tp_slot >= 0) and/or wait for a gathered input.
-    int tp_world, tp_rank, tp_slot, tp_wait;
+    // tp_reduce: row-parallel linear, the all-reduce of its f32 partials
+    // fused in (every CTA stores its columns' partials into every rank's
+    // region, then sums the same columns of every rank's partials into y).
+    int tp_world, tp_rank, tp_slot, tp_wait, tp_reduce;
     int64_t tp_dst_off, tp_dst_row, tp_cols;
     uint8_t *tp_bases[kTpMaxRanks];
     // Planar Q8_0 of y (oq != null): every CTA owns whole 32-column blocks of
@@ -616,6 +619,13 @@ __device__ __forceinline__ void store_y(const GemvParams &p, int m, int64_t n, f
         store_out(p.y, p.y_dtype, m * p.y_row_stride + n, v);
         return;
     }
+    if (p.tp_reduce) {
+        // this rank's f32 partial, straight into every rank's region (peer
+        // stores over NVLink; the CTA signals after its last row)
+        const int64_t off = kTpDataOff + p.tp_dst_off + (m * p.tp_dst_row + (int64_t)p.tp_rank * p.tp_cols + n) * 4;
+        for (int g = 0; g < p.tp_world; ++g) *reinterpret_cast<float *>(p.tp_bases[g] + off) = v;
+        return;
+    }
     // this rank's own region only; the launch's last CTA pushes the finished
     // slice to the other ranks in 16-byte pieces
     const int64_t idx = m * p.tp_dst_row + (int64_t)p.tp_rank * p.tp_cols + n;
@@ -1011,7 +1021,54 @@ __global__ void __launch_bounds__(kThreads, (MT <= 8) ? 2 : 1) q4_gemv_q8_kernel
             }
         }
     }
-    if (p.tp_slot >= 0) {
+    if (p.tp_slot >= 0 && p.tp_reduce) {
+        // Row-parallel all-reduce, CTA by CTA: this CTA's partials are in
+        // every rank's region; signal the same CTA of every rank, wait for
+        // theirs, then sum rank 0's partial + rank 1's + ... for this CTA's
+        // columns. Every rank adds the same values in the same order, so y
+        // has the same bits everywhere. After a failed wait y is not written
+        // (the error word says why).
+        __shared__ int red_ok;
+        const int nthr = kConsumerWarps * 32;
+        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            const int64_t cidx = ((int64_t)p.tp_slot * kTpRedCtas + blockIdx.x) * kTpMaxRanks;
+            for (int g = 0; g < p.tp_world; ++g)
+                atomicAdd_system(reinterpret_cast<int *>(p.tp_bases[g] + kTpRedCountOff) + cidx + p.tp_rank, 1);
+            const uint8_t *lb = p.tp_bases[p.tp_rank];
+            const int target = ld_acquire_sys(reinterpret_cast<const int *>(lb + kTpEpochOff)) + 1;
+            const int *cnt = reinterpret_cast<const int *>(lb + kTpRedCountOff) + cidx;
+            bool ok = true;
+            for (int g = 0; g < p.tp_world && ok; ++g) {
+                if (ld_acquire_sys(cnt + g) >= target) continue;
+                if (p.err && *reinterpret_cast<volatile int *>(p.err) != 0) {
+                    ok = false;
+                    break;
+                }
+                const long long start = clock64(), budget = wait_budget(p.err);
+                while (ld_acquire_sys(cnt + g) < target) {
+                    if (clock64() - start > budget) {
+                        record_device_error(p.err, DEV_ERR_WAIT_FULL);
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+            red_ok = ok;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+        if (red_ok) {
+            const float *part = reinterpret_cast<const float *>(p.tp_bases[p.tp_rank] + kTpDataOff + p.tp_dst_off);
+            for (int t = threadIdx.x; t < p.M * nrows; t += nthr) {
+                const int m = t / nrows;
+                const int64_t n = r0 + t % nrows;
+                float acc = 0.0f;
+                for (int g = 0; g < p.tp_world; ++g) acc += __ldcg(part + m * p.tp_dst_row + (int64_t)g * p.tp_cols + n);
+                store_out(p.y, p.y_dtype, m * p.y_row_stride + n, acc);
+            }
+        }
+    } else if (p.tp_slot >= 0) {
         // Every consumer's rows are stored in this rank's region. The launch's
         // last CTA (ticket) copies the whole slice to every other rank, fences
         // system-wide and signals every rank -- also after a failed wait, so
@@ -1201,6 +1258,9 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
     int64_t grid = (int64_t)f.sm_count * ctas_per_sm;
     const int64_t by_rows = (N + plan.rpw * plan.wpc - 1) / (plan.rpw * plan.wpc);
     if (by_rows < grid) grid = by_rows > 0 ? by_rows : 1;
+    if (p.tp_reduce && grid > kTpRedCtas)
+        return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: more CTAs than the tensor-parallel "
+                                                                   "reduce counters cover");
     if (p.oq) {
         // whole blocks per CTA, at most kYCap columns of them
         const int64_t blocks = ((flags & TN_EPILOGUE_SILU_MUL_PAIRS) ? N / 2 : N) / 32;
@@ -1271,7 +1331,9 @@ namespace {
 void set_link(GemvParams &p, const tn_tp_link *link, int64_t out_cols) {
     p.tp_slot = p.tp_wait = -1;
     p.tp_world = 1;
+    p.tp_reduce = 0;
     if (!link) return;
+    p.tp_reduce = link->reduce;
     p.tp_world = link->world;
     p.tp_rank = link->rank;
     p.tp_slot = link->slot;

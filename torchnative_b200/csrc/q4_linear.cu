@@ -8,11 +8,24 @@
 namespace tn {
 namespace {
 
-int check_link(const std::string &op, const tn_tp_link *l, int64_t out_cols) {
+int check_link(const std::string &op, const tn_tp_link *l, int64_t out_cols, int flags = 0,
+               const float *bias = nullptr) {
     if (l->world < 1 || l->world > kTpMaxRanks || l->rank < 0 || l->rank >= l->world)
         return set_error(TN_ERR_INVALID, op + ": tensor-parallel link: rank/world out of range (at most 8 ranks)");
     for (int g = 0; g < l->world; ++g)
         if (!l->bases[g]) return set_error(TN_ERR_INVALID, op + ": tensor-parallel link: null region base");
+    if (l->reduce) {
+        if (l->reduce != 1) return set_error(TN_ERR_INVALID, op + ": tensor-parallel link: reduce is 0 or 1");
+        if (l->slot < 0 || l->slot >= kTpRedSlots || l->wait_slot >= 0)
+            return set_error(TN_ERR_INVALID, op + ": tensor-parallel reduce: slot in [0, 256) and no wait_slot");
+        if (bias || (flags & TN_EPILOGUE_SILU_MUL_PAIRS))
+            return set_error(TN_ERR_NOT_IMPLEMENTED,
+                             op + ": tensor-parallel reduce: no bias and no pair epilogue (partials are summed)");
+        if (l->dst_offset < 0 || (l->dst_offset & 3) != 0 || l->dst_row_stride < l->world * out_cols)
+            return set_error(TN_ERR_SHAPE, op + ": tensor-parallel reduce: 4-byte aligned destination with a row "
+                                                "stride of at least world * columns");
+        return TN_OK;
+    }
     const int64_t max_slot = (kTpTicketOff - kTpCountOff) / 4 / l->world;
     if (l->slot >= max_slot || l->wait_slot >= max_slot)
         return set_error(TN_ERR_INVALID, op + ": tensor-parallel link: slot out of range");
@@ -198,7 +211,7 @@ extern "C" int tn_q4_0_linear_q8_tp(const int8_t *codes, int64_t codes_row_strid
         return tn::set_error(TN_ERR_INVALID, op + ": the SiLU*up pair epilogue needs an even N and a bf16 output");
     const int64_t ycols = pairs ? N / 2 : N;
     if (link) {
-        int st = tn::check_link(op, link, ycols);
+        int st = tn::check_link(op, link, ycols, flags, bias);
         if (st) return st;
         if (M > chunk) return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": a tensor-parallel link needs one launch (M <= " +
                                                                         std::to_string(chunk) + ")");
@@ -258,8 +271,10 @@ int linear_fused(const std::string &op, int x_mode, const void *x, int64_t x_row
     if (pairs && (N % 2 != 0 || y_dtype != TN_BF16))
         return tn::set_error(TN_ERR_INVALID, op + ": the SiLU*up pair epilogue needs an even N and a bf16 output");
     if (link) {
-        int st = tn::check_link(op, link, pairs ? N / 2 : N);
+        int st = tn::check_link(op, link, pairs ? N / 2 : N, flags, bias);
         if (st) return st;
+        if (link->reduce && q8)
+            return tn::set_error(TN_ERR_NOT_IMPLEMENTED, op + ": tensor-parallel reduce with a planar Q8_0 output");
     }
     return tn::launch_q4_gemv_fused(x_mode, x, x_row_stride, delta, h_out, norm_weight, eps,
                                     static_cast<const uint8_t *>(w_blob), bias, y, y_dtype, pairs ? N / 2 : N, (int)M,

@@ -76,14 +76,18 @@ class Q4LlamaDecoder:
 
     def __init__(self, shape: LlamaShape, batch: int, capacity: int, device, seed: int = 0,
                  layers: int | None = None, tp=None, exchange: str = "p2p", weights: dict | None = None,
-                 mega: bool | None = None):
+                 mega: bool | None = None, tp_plan: str = "rowwise"):
         """`weights` (from `from_gguf`): the full model's tensors on `device`
         -- per layer attn_norm, qkv, o, mlp_norm, gate_up, down as below, plus
         final_norm, lm_head, embed -- used instead of the seeded random ones.
         `mega`: run each token as the one persistent kernel
         (tn_llama_decode_token) -- True insists (one GPU, batch 1, a shape it
         supports); None and False keep the launch-per-operator step, which
-        measures faster today."""
+        measures faster today. `tp_plan` (tensor parallel only): "rowwise"
+        makes o_proj and down_proj row-parallel with their all-reduce fused
+        into the GEMV (peer-memory exchange, batch <= 4; otherwise it falls
+        back to "colwise"), "colwise" column-shards every linear with an
+        all-gather after each (the one-GPU token stream bit for bit)."""
         from . import tp as tpm
 
         self.s = shape
@@ -93,6 +97,9 @@ class Q4LlamaDecoder:
         self.tp = tp if tp is not None and tp.world > 1 else None
         G, r = (self.tp.world, self.tp.rank) if self.tp else (1, 0)
         self.G = G
+        if tp_plan not in ("rowwise", "colwise"):
+            raise ValueError(f"unknown tp_plan {tp_plan!r} (rowwise or colwise)")
+        self.rowwise = self.tp is not None and tp_plan == "rowwise" and batch <= 4 and exchange == "p2p"
         s, dev = shape, self.dev
         for n, what in ((s.heads, "query heads"), (s.kv_heads, "key/value heads"), (s.hidden, "hidden size"),
                         (s.inter, "intermediate size"), (s.vocab, "vocabulary")):
@@ -101,6 +108,11 @@ class Q4LlamaDecoder:
         self.hq, self.hkv = s.heads // G, s.kv_heads // G   # local heads
         self.h_l, self.i_l, self.v_l = s.hidden // G, s.inter // G, s.vocab // G
         self.qkv_l = (self.hq + 2 * self.hkv) * s.head_dim
+        # rowwise: SiLU*up's planar Q8_0 from gate/up's own epilogue needs whole
+        # 32-column blocks per CTA; when this rank's columns make too few blocks
+        # to keep the SMs streaming (Llama-3-8B on 8 ranks: 56), down_proj
+        # quantises act in its prologue instead (56 blocks per CTA)
+        self.rowwise_q8out = self.i_l // 32 >= 74
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
         bf = torch.bfloat16
@@ -118,9 +130,10 @@ class Q4LlamaDecoder:
             }
             if G > 1:
                 lw["qkv"] = tpm.shard_qkv(lw["qkv"], s.heads, s.kv_heads, s.head_dim, s.hidden, r, G)
-                lw["o"] = tpm.shard_rows(lw["o"], s.hidden, s.heads * s.head_dim, r, G)
                 lw["gate_up"] = tpm.shard_gate_up_pairs(lw["gate_up"], s.inter, s.hidden, r, G)
-                lw["down"] = tpm.shard_rows(lw["down"], s.hidden, s.inter, r, G)
+                shard = tpm.shard_cols if self.rowwise else tpm.shard_rows
+                lw["o"] = shard(lw["o"], s.hidden, s.heads * s.head_dim, r, G)
+                lw["down"] = shard(lw["down"], s.hidden, s.inter, r, G)
             self.layers.append(lw)
         if weights is not None:
             self.final_norm, self.lm_head = weights["final_norm"], weights["lm_head"]
@@ -146,6 +159,8 @@ class Q4LlamaDecoder:
         self.xchg = None
         if self.tp is not None and exchange == "p2p":
             nbytes = 2 * B * (s.heads * s.head_dim + H + I + s.vocab) + 4 * 256
+            if self.rowwise:  # two f32 partial buffers [B][G * H], alternating between reductions
+                nbytes += 2 * (B * G * H * 4 + 256)
             self.xchg = tpm.PeerExchange(self.tp, nbytes, dev)
             attn2d, self._off_attn = self.xchg.buffer(B, s.heads * s.head_dim)
             self.attn = attn2d.view(B, s.heads, 1, s.head_dim)
@@ -154,6 +169,8 @@ class Q4LlamaDecoder:
             self.logits, self._off_logits = self.xchg.buffer(B, s.vocab)
             for t in (self.attn, self.delta, self.act, self.logits):
                 t.zero_()
+            if self.rowwise:
+                self._off_part = [self.xchg.reserve(B * G * H * 4) for _ in range(2)]
         elif self.tp is not None and exchange != "nccl":
             raise ValueError(f"unknown exchange {exchange!r} (p2p or nccl)")
         else:
@@ -331,6 +348,8 @@ class Q4LlamaDecoder:
             extra = 4 if (self.tp is not None and self.B > 1) else 0
         if self._mega is not None:
             return 0  # the whole token is one launch (kernels_per_step)
+        if self.rowwise:
+            return 5  # the one-GPU fused layer; both reductions inside the GEMVs
         if self.fused:
             # one GPU: gate/up also writes the planar Q8_0 of act (no quantiser launch)
             return (5 if self.tp is None else 6) + extra
@@ -516,7 +535,47 @@ class Q4LlamaDecoder:
                                                 N.TN_WEIGHTS_STATIC | flags,
                                                 None if link is None else ctypes.addressof(link), stream))
 
+    def _step_rowwise(self, stream) -> None:
+        """The tensor-parallel step under the rowwise plan, the one-GPU fused
+        step's five launches a layer on this rank's shards: q/k/v and gate/up
+        column-sharded, attention on the local heads writing their planar
+        Q8_0 (o_proj's K-slice), SiLU*up's planar Q8_0 local (down_proj's
+        K-slice), o_proj and down_proj each ending in the all-reduce fused
+        into the GEMV, so the replicated residual stream reads `delta` in
+        stream order. Only the logits are gathered."""
+        L, s, B = N.lib(), self.s, self.B
+        D, Hq, Hkv, H = s.head_dim, self.hq, self.hkv, s.hidden
+        ha, hb = self.h, self.h2
+        links = self._links
+        q8out = self.rowwise_q8out
+        for li, lw in enumerate(self.layers):
+            self._fused_linear(N.TN_X_RMSNORM, ha, H, None if li == 0 else self.delta, hb, lw["attn_norm"],
+                               lw["qkv"], self.qkv_out, self.qkv_l, H, stream)
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            N.check(L.tn_sdpa_decode_step_q8(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()),
+                                             P(kc.data_ptr()), P(vc.data_ptr()), P(self.attn_l.data_ptr()), None,
+                                             P(self.codes.data_ptr()), P(self.scales.data_ptr()),
+                                             P(self.offsets.data_ptr()), B, Hq, Hkv, D, self.cap, self._kstr,
+                                             self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D), stream))
+            self._linear(lw["o"], self.delta, H, Hq * D, stream, link=links[("o", li)])
+            self._fused_linear(N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act_l,
+                               2 * self.i_l, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS, q8=q8out)
+            if q8out:
+                self._linear(lw["down"], self.delta, H, self.i_l, stream, link=links[("down", li)])
+            else:
+                self._fused_linear(N.TN_X_BF16, self.act_l, self.i_l, None, None, None, lw["down"], self.delta, H,
+                                   self.i_l, stream, link=links[("down", li)])
+        self._fused_linear(N.TN_X_RMSNORM, ha, H, self.delta, hb, self.final_norm, self.lm_head, self.logits_l,
+                           self.v_l, H, stream)
+        self._gather(self.logits_l, self.logits, 0, stream)
+        N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
+                                        P(self.embed.data_ptr()), s.hidden, P(ha.data_ptr()),
+                                        P(self.pos.data_ptr()), stream))
+        self._step_end(stream)
+
     def _step_fused(self, stream) -> None:
+        if self.rowwise:
+            return self._step_rowwise(stream)
         L, s, B = N.lib(), self.s, self.B
         D, Hq, Hkv, H, I = s.head_dim, self.hq, self.hkv, s.hidden, s.inter  # local heads
         HD = s.heads * D
@@ -582,6 +641,11 @@ class Q4LlamaDecoder:
         if self.xchg is None or not self.fused_gather:
             return {}
         links = {}
+        if self.rowwise:  # reductions 2l (o_proj) and 2l + 1 (down_proj), alternating partial buffers
+            for li in range(self.n_layers):
+                links[("o", li)] = self.xchg.reduce_link(2 * li, self._off_part[0], self.s.hidden)
+                links[("down", li)] = self.xchg.reduce_link(2 * li + 1, self._off_part[1], self.s.hidden)
+            return links
         for li in range(self.n_layers):
             links[("o", li)] = self._link(slot=4 * li + 1, full=self.delta)
             links[("gate_up", li)] = self._link(wait_slot=4 * li + 1)

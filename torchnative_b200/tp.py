@@ -15,7 +15,14 @@ Across G GPUs of one box the path is split only where it shards by itself:
 * after each sharded linear one NCCL all-gather over NVLink/NVSwitch
   rebuilds the full activation row on every rank (4 per layer: attention
   output, o_proj, SiLU(gate)*up, down_proj; plus the lm_head logits), and the
-  replicated parts (residual, RMSNorm, argmax) run on every rank.
+  replicated parts (residual, RMSNorm, argmax) run on every rank -- the
+  "colwise" plan, whose token stream is the one-GPU stream bit for bit;
+* or ("rowwise", transformers' colwise/rowwise plan) o_proj and down_proj
+  are row-parallel: rank r keeps input features [r K/G, (r+1) K/G) of every
+  row (its own heads' attention output, its own SiLU*up columns), so the
+  attention output and SiLU*up stay local, and each of the two linears ends
+  in an all-reduce of f32 partials fused into its own kernel: 2 exchanges a
+  layer instead of 4, no exchange launches.
 
 The reference has no multi-GPU path; the hook sits where its model-load path
 adopts quantised weights (torchnative/python/torchnative/quant/hf.py:340 and
@@ -75,6 +82,17 @@ def shard_qkv(blob: torch.Tensor, heads: int, kv_heads: int, head_dim: int, k: i
     return torch.cat([row_slice(blob, n, k, q0, q0 + hq * head_dim),
                       row_slice(blob, n, k, k0, k0 + hkv * head_dim),
                       row_slice(blob, n, k, v0, v0 + hkv * head_dim)])
+
+
+def shard_cols(blob: torch.Tensor, n: int, k: int, rank: int, world: int) -> torch.Tensor:
+    """Row-parallel linear: rank r's input features [r k/G, (r+1) k/G) of every
+    output row -- whole Q4_0 blocks of each row (k/G a multiple of 32), cut out
+    of the blob as bytes and packed as an [n, k/G] blob."""
+    rb = q4_row_bytes(k)
+    c = _split(k // 32, world, "in_features / 32")
+    if blob.numel() != n * rb:
+        raise ValueError(f"q4_0 blob of {blob.numel()} bytes is not [{n}, {k}] ({n * rb} bytes)")
+    return blob.view(n, k // 32, 18)[:, rank * c:(rank + 1) * c].reshape(-1).contiguous()
 
 
 def shard_gate_up_pairs(blob: torch.Tensor, inter: int, k: int, rank: int, world: int) -> torch.Tensor:
@@ -188,6 +206,27 @@ class PeerExchange:
         rows, c = local.shape
         N.check(N.lib().tn_tp_allgather(self.bases, self.tp.rank, self.tp.world, P(local.data_ptr()),
                                         local.stride(0), rows, c, dst_off, full_cols, slot, stream))
+
+    def reserve(self, nbytes: int) -> int:
+        """nbytes of this rank's data area (256-byte aligned) with no tensor
+        view: the row-parallel reductions' f32 partials."""
+        off = self._next
+        if off + nbytes > self.nbytes:
+            raise ValueError("exchange region too small")
+        self._next = (off + nbytes + 255) // 256 * 256
+        return off
+
+    def reduce_link(self, slot: int, partial_off: int, cols: int) -> "N.TpLink":
+        """A tn_tp_link for a row-parallel GEMV with its all-reduce fused in:
+        reduction `slot` of the step, f32 partials at partial_off laid out
+        [rows][world * cols]."""
+        ln = N.TpLink()
+        ln.world, ln.rank = self.tp.world, self.tp.rank
+        for g in range(self.tp.world):
+            ln.bases[g] = self.bases[g]
+        ln.dst_offset, ln.dst_row_stride, ln.slot, ln.wait_slot, ln.reduce = (partial_off, self.tp.world * cols,
+                                                                              slot, -1, 1)
+        return ln
 
     def link(self, slot: int = -1, dst_off: int = 0, full_cols: int = 0, wait_slot: int = -1) -> "N.TpLink":
         """A tn_tp_link for a GEMV that feeds gather `slot` (its output scattered
