@@ -67,6 +67,10 @@ def parse():
                     help="kernel-level case instead of the decode step: 'gemv' times the decode GEMV alone on the "
                          "BASELINE (N, K) shapes over rotating weights (~0.3-0.6 GB on the device; the ncu case)")
     ap.add_argument("--rows", type=int, default=1, help="activation rows M for --case gemv")
+    ap.add_argument("--fused", action="store_true",
+                    help="--case gemv: the launch as the decode step runs gate/up -- RMSNorm prologue on bf16 h + "
+                         "delta, SiLU*up pair epilogue, act's planar Q8_0 written by the same launch "
+                         "(tn_q4_0_linear_fused_q8out; N is the interleaved gate/up rows, M <= 4)")
     ap.add_argument("--shape", default=None, help="one N,K for --case gemv (default: BASELINE's four shapes)")
     ap.add_argument("--format", default="q4_0", choices=["q4_0", "q8_0", "q4_k"],
                     help="weight format for --case gemv (q8_0 / q4_k time tn_q8_0_linear / tn_q4_k_linear: "
@@ -427,11 +431,12 @@ def run_ours(args, rank, world, local):
     if kernel_us:
         ctx = int(mean_ctx)
         kv = 2 * B * dec.hkv * ctx * HEAD_DIM * 2
+        hd_l = dec.hq * HEAD_DIM  # this rank's heads (all of them on one GPU)
         kbytes = {"qkv_rmsnorm_gemv": q4_bytes(dec.qkv_l, HIDDEN) + B * HIDDEN * 4 + HIDDEN * 2 + B * dec.qkv_l * 2,
-                  "sdpa_decode_step_q8": kv + B * dec.qkv_l * 2 + B * HEADS * HEAD_DIM * 3,
-                  "o_gemv": q4_bytes(HIDDEN, HEADS * HEAD_DIM) + B * HEADS * HEAD_DIM * 5 // 4 + B * HIDDEN * 2,
+                  "sdpa_decode_step_q8": kv + B * dec.qkv_l * 2 + B * hd_l * 3,
+                  "o_gemv": q4_bytes(HIDDEN, hd_l) + B * hd_l * 5 // 4 + B * HIDDEN * 2,
                   "gate_up_rmsnorm_gemv_silu_q8": algo,
-                  "down_gemv": q4_bytes(HIDDEN, INTER) + B * INTER * 5 // 4 + B * HIDDEN * 2}
+                  "down_gemv": q4_bytes(HIDDEN, dec.i_l) + B * dec.i_l * 5 // 4 + B * HIDDEN * 2}
         for name, us in kernel_us.items():
             b = kbytes.get(name)
             per_kernel[name] = {"us": us, "bytes": b,
@@ -439,6 +444,15 @@ def run_ours(args, rank, world, local):
         layer_us = sum(kernel_us.values())
         per_kernel["per_layer_total"] = {"us": round(layer_us, 2), "bytes": sum(kbytes.values()),
                                          "frac": round(sum(kbytes.values()) / (layer_us * 1e-6) / 1e9 / peak, 3)}
+        if world > 1:
+            # the same launches on this rank's shards without their reductions,
+            # against the step: what remains is the exchanges, their waits and
+            # the lm_head / logits gather / argmax tail
+            step_us = ms * 1e3
+            per_kernel["tp_breakdown"] = {
+                "step_us": round(step_us, 2), "local_kernels_us_per_layer": round(layer_us, 2),
+                "layers_x_local_us": round(LAYERS * layer_us, 2),
+                "exchange_wait_and_tail_share": round(max(0.0, 1.0 - LAYERS * layer_us / step_us), 3)}
     result = {
         "metric": METRIC,
         "value": B * 1000.0 / ms,  # one model, tensor-parallel over the group: B tokens per step
@@ -940,7 +954,24 @@ def run_case_gemv(args):
         N.check(L.tn_q8_0_quantize_planar(P(x.data_ptr()), N.TN_BF16, k, P(codes.data_ptr()), k,
                                           P(scales.data_ptr()), P(offs.data_ptr()), M, k, s()))
 
+        if args.fused:
+            h = torch.randn((M, k), device=dev, generator=gen).to(torch.bfloat16)
+            delta = (0.1 * torch.randn((M, k), device=dev, generator=gen)).to(torch.bfloat16)
+            h_out = torch.empty_like(h)
+            norm_w = (1.0 + 0.1 * torch.randn(k, device=dev, generator=gen)).to(torch.bfloat16)
+            y = torch.empty((M, n // 2), device=dev, dtype=torch.bfloat16)
+            oq = torch.empty((M, n // 2), device=dev, dtype=torch.int8)
+            od = torch.empty((M, n // 64), device=dev)
+            oc = torch.empty((M, n // 64), device=dev)
+
         def launch(w):
+            if args.fused:
+                N.check(L.tn_q4_0_linear_fused_q8out(
+                    N.TN_X_RMSNORM, P(h.data_ptr()), k, P(delta.data_ptr()), P(h_out.data_ptr()),
+                    P(norm_w.data_ptr()), 1e-5, P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, M, n, k,
+                    N.TN_WEIGHTS_STATIC | N.TN_EPILOGUE_SILU_MUL_PAIRS, P(oq.data_ptr()), n // 2, P(od.data_ptr()),
+                    P(oc.data_ptr()), s()))
+                return
             if q8w or q4k:  # the bf16 activation's quantiser launch, then the GEMV of that weight format
                 fn = L.tn_q8_0_linear if q8w else L.tn_q4_k_linear
                 N.check(fn(P(x.data_ptr()), N.TN_BF16, k, P(w.data_ptr()), None, P(y.data_ptr()), N.TN_BF16, M, n, k,
@@ -974,6 +1005,9 @@ def run_case_gemv(args):
         us = e0.elapsed_time(e1) * 1e3 / (args.steps * copies)
         algo = wbytes + M * (k + k // 32 * 8) + M * n * 2
         kernel = "q4_skinny_kernel" if args.format == "q4_0" and 9 <= M <= 32 and k % 256 == 0 else "q4_gemv_q8_kernel"
+        if args.fused:  # bf16 h, delta and h_out, the norm weight; bf16 act + its planar Q8_0 out
+            algo = wbytes + M * k * 2 * 3 + k * 2 + M * (n // 2) * (2 + 1) + M * (n // 64) * 8
+            kernel = "q4_gemv_q8_kernel<X_NORM> (RMSNorm prologue, SiLU*up epilogue, planar Q8_0 out)"
         print(json.dumps({"case": "gemv", "format": args.format, "kernel": kernel, "M": M, "N": n, "K": k,
                           "us_per_launch": us,
                           "GBps": algo / us / 1e3, "frac": algo / us / 1e3 / peak, "peak": peak,

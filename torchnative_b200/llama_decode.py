@@ -659,27 +659,34 @@ class Q4LlamaDecoder:
         """For timing the step's parts: one CUDA graph per kind of launch in
         the fused step, each running that launch once per layer with the
         step's own arguments (so 32 back-to-back launches over 32 layers'
-        weights). Reads and writes the step's buffers; re-seed afterwards."""
-        if not self.fused or self.tp is not None or self._mega is not None:
+        weights). Reads and writes the step's buffers; re-seed afterwards.
+        Under the rowwise tensor-parallel plan the same launches on this
+        rank's shards without their reductions (o_proj and down_proj write
+        their local partial as `delta`): the step's time beyond these is the
+        exchange and its waits."""
+        if not self.fused or (self.tp is not None and not self.rowwise) or self._mega is not None:
             return {}
         L, s, B = N.lib(), self.s, self.B
-        D, Hq, Hkv, H, I = s.head_dim, s.heads, s.kv_heads, s.hidden, s.inter
+        D, Hq, Hkv, H = s.head_dim, self.hq, self.hkv, s.hidden  # this rank's heads
         ha, hb = self.h, self.h2
+        q8out = self.rowwise_q8out
         side = torch.cuda.Stream(self.dev)
         side.wait_stream(torch.cuda.current_stream(self.dev))
         parts = {
             "qkv_rmsnorm_gemv": lambda lw, li, st: self._fused_linear(
-                N.TN_X_RMSNORM, ha, H, self.delta, hb, lw["attn_norm"], lw["qkv"], self.qkv_out, s.qkv, H, st),
+                N.TN_X_RMSNORM, ha, H, self.delta, hb, lw["attn_norm"], lw["qkv"], self.qkv_out, self.qkv_l, H, st),
             "sdpa_decode_step_q8": lambda lw, li, st: N.check(L.tn_sdpa_decode_step_q8(
                 P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()), P(self.k_cache[li].data_ptr()),
-                P(self.v_cache[li].data_ptr()), P(self.attn.data_ptr()), None, P(self.codes.data_ptr()),
+                P(self.v_cache[li].data_ptr()), P(self.attn_l.data_ptr()), None, P(self.codes.data_ptr()),
                 P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, Hq, Hkv, D, self.cap, self._kstr,
                 self._kstr, P(self.pos.data_ptr()), 1.0 / math.sqrt(D), st)),
             "o_gemv": lambda lw, li, st: self._linear(lw["o"], self.delta, H, Hq * D, st),
             "gate_up_rmsnorm_gemv_silu_q8": lambda lw, li, st: self._fused_linear(
-                N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act, 2 * I, H, st,
-                N.TN_EPILOGUE_SILU_MUL_PAIRS, q8=True),
-            "down_gemv": lambda lw, li, st: self._linear(lw["down"], self.delta, H, I, st),
+                N.TN_X_RMSNORM, hb, H, self.delta, ha, lw["mlp_norm"], lw["gate_up"], self.act_l, 2 * self.i_l, H,
+                st, N.TN_EPILOGUE_SILU_MUL_PAIRS, q8=q8out),
+            "down_gemv": (lambda lw, li, st: self._linear(lw["down"], self.delta, H, self.i_l, st)) if q8out else
+                         (lambda lw, li, st: self._fused_linear(N.TN_X_BF16, self.act_l, self.i_l, None, None, None,
+                                                                lw["down"], self.delta, H, self.i_l, st)),
         }
         graphs = {}
         for name, fn in parts.items():
