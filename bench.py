@@ -234,10 +234,11 @@ def committed_traffic(name: str = "q4_gemv_traffic.json"):
 
 
 def scaled_traffic(n_rows: int):
-    """The committed per-launch DRAM traffic of the 28672-row gate/up GEMV,
+    """The committed per-launch DRAM traffic of the 28672-row gate/up launch
+    as the step runs it (RMSNorm prologue, SiLU*up epilogue, planar Q8_0 out),
     scaled to a rank's shard of n_rows rows (traffic grows with the rows
     streamed); None without a committed capture."""
-    t = committed_traffic()
+    t = committed_traffic("q4_gemv_gate_up_fused_traffic.json")
     return None if t is None else int(t * n_rows / (2 * INTER))
 
 

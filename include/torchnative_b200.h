@@ -410,7 +410,7 @@ TN_API int tn_llama_embed(const int *tokens, int64_t rows, const void *embed, in
  * heads; gate_up rows interleave gate_proj and up_proj row by row; caches are
  * bf16 [1][kv_heads][capacity][head_dim]; norms and the embedding bf16;
  * inv_freq f32 [head_dim / 2]. Supported: head_dim 128, heads = 4 kv_heads,
- * hidden and inter multiples of 256 (hidden <= 7680, inter <= 16384). */
+ * hidden and inter multiples of 256 (hidden <= 5632, inter <= 16384). */
 typedef struct {
     int32_t layers, hidden, inter, heads, kv_heads, head_dim, vocab;
     float eps;

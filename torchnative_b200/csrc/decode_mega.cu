@@ -1318,7 +1318,7 @@ int check_model(const tn_llama_q4_model *m, const std::string &op) {
                                                       "heads per key/value head (Llama-3-8B's shape family)");
     if (H % 256 != 0 || I % 256 != 0 || (Hq * D) % 256 != 0 || H / 16 > kCT || I > kMaxK || Hq * D > kMaxK)
         return set_error(TN_ERR_NOT_IMPLEMENTED, op + ": hidden and intermediate sizes must be multiples of 256 "
-                                                      "(hidden <= 7680, intermediate <= 16384)");
+                                                      "(hidden <= 5632, intermediate <= 16384)");
     return TN_OK;
 }
 
