@@ -103,6 +103,14 @@ extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void 
     const int64_t rows = (int64_t)p.B * p.Hq * p.L;
     p.part_o = static_cast<float *>(ws);
     p.part_ml = p.part_o + rows * p.splits * p.D;
+    if (p.L == 1 && p.row_groups == 1) {
+        // one query row per head: the last CTA of each KV head merges the
+        // splits (a zeroed ticket per head, reset by that CTA), no combine launch
+        void *cnt = nullptr;
+        st = tn::workspace_zeroed(&cnt, (size_t)p.B * p.Hkv * sizeof(int) + 256, stream, /*slot=*/3);
+        if (st) return st;
+        p.counters = static_cast<int *>(cnt);
+    }
     return tn::launch_sdpa_decode(p, dtype, stream);
 }
 
@@ -154,6 +162,12 @@ extern "C" int tn_sdpa_decode_cache(const void *q, const void *k_cache, const vo
     if (st) return st;
     p.part_o = static_cast<float *>(ws);
     p.part_ml = p.part_o + (int64_t)p.B * p.Hq * p.splits * p.D;
+    if (p.row_groups == 1) {  // the last CTA of each KV head merges the splits (no combine launch)
+        void *cnt = nullptr;
+        st = tn::workspace_zeroed(&cnt, (size_t)p.B * p.Hkv * sizeof(int) + 256, stream, /*slot=*/3);
+        if (st) return st;
+        p.counters = static_cast<int *>(cnt);
+    }
     return tn::launch_sdpa_decode(p, dtype, stream);
 }
 
