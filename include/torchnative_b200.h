@@ -511,16 +511,18 @@ TN_API int tn_tp_step_end(void *local_base, void *stream);
  *
  * reduce = 1 makes the GEMV a row-parallel linear with its all-reduce fused
  * in (transformers' "rowwise" plan: each rank holds a K-slice of the weight,
- * whole Q4_0 blocks of every row): every CTA stores its f32 partial outputs
- * into every rank's [M][dst_row_stride] buffer at row m, columns
- * [rank*N, (rank+1)*N) (dst_row_stride >= world*N), signals its own counter
- * in every rank's region, waits (bounded) for the same CTA of every rank,
- * then writes y = sum over ranks g = 0..world-1, in that order, of the
- * partials -- the same bits on every rank. `slot` numbers the reductions of
- * a step (< TN_TP_REDUCE_SLOTS, each once per step); consecutive reductions
- * must alternate between two buffers. No bias, no pair epilogue, wait_slot
- * -1. The result differs from the one-GPU linear only in the association of
- * its f32 sum (within the same counted bound). */
+ * whole Q4_0 blocks of every row): every CTA stores its f32 partial outputs,
+ * each as one 8-byte word {value, tag = epoch * 256 + slot + 1}, into every
+ * rank's [M][dst_row_stride] buffer of 8-byte words at row m, columns
+ * [rank*N, (rank+1)*N) (dst_row_stride >= world*N), then polls (bounded)
+ * the words of its own columns until every rank's carries this launch's tag,
+ * and writes y = sum over ranks g = 0..world-1, in that order, of the
+ * partials -- the same bits on every rank; no fence and no separate signal.
+ * `slot` numbers the reductions of a step (< TN_TP_REDUCE_SLOTS, each once
+ * per step, tn_tp_step_end after the step); consecutive reductions must
+ * alternate between two buffers. No bias, no pair epilogue, wait_slot -1.
+ * The result differs from the one-GPU linear only in the association of its
+ * f32 sum (within the same counted bound). */
 #define TN_TP_REDUCE_SLOTS 256
 typedef struct {
     int world, rank;

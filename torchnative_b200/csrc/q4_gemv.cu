@@ -612,6 +612,20 @@ __device__ __forceinline__ void stage_x(const Smem &s, const GemvParams &p, int 
     }
 }
 
+// The tag of this launch's row-parallel reduction (epoch * 256 + slot + 1):
+// set by consumer thread 0 before the main loop, read by every store and
+// every poll of the reduction.
+__shared__ uint32_t g_red_tag;
+
+__device__ __forceinline__ void st_relaxed_sys_u64(uint8_t *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint8_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Output column n of row m: into y, or (tensor-parallel producer) into this
 // rank's columns of the gathered buffer in its exchange region.
 __device__ __forceinline__ void store_y(const GemvParams &p, int m, int64_t n, float v) {
@@ -620,10 +634,12 @@ __device__ __forceinline__ void store_y(const GemvParams &p, int m, int64_t n, f
         return;
     }
     if (p.tp_reduce) {
-        // this rank's f32 partial, straight into every rank's region (peer
-        // stores over NVLink; the CTA signals after its last row)
-        const int64_t off = kTpDataOff + p.tp_dst_off + (m * p.tp_dst_row + (int64_t)p.tp_rank * p.tp_cols + n) * 4;
-        for (int g = 0; g < p.tp_world; ++g) *reinterpret_cast<float *>(p.tp_bases[g] + off) = v;
+        // this rank's f32 partial with its use tag in one 8-byte word, straight
+        // into every rank's region (peer stores over NVLink): a reader that
+        // sees the tag sees the value, so no fence and no separate signal
+        const int64_t off = kTpDataOff + p.tp_dst_off + (m * p.tp_dst_row + (int64_t)p.tp_rank * p.tp_cols + n) * 8;
+        const uint64_t word = ((uint64_t)g_red_tag << 32) | __float_as_uint(v);
+        for (int g = 0; g < p.tp_world; ++g) st_relaxed_sys_u64(p.tp_bases[g] + off, word);
         return;
     }
     // this rank's own region only; the launch's last CTA pushes the finished
@@ -925,6 +941,9 @@ __global__ void __launch_bounds__(kThreads, (MT <= 8) ? 2 : 1) q4_gemv_q8_kernel
 
     // ---------------- consumers
     pdl_wait();  // the activations may come from the previous kernel in the stream
+    if (p.tp_reduce && threadIdx.x == 0)  // (visible to the other consumers after the staging barrier)
+        g_red_tag = (uint32_t)ld_acquire_sys(reinterpret_cast<const int *>(p.tp_bases[p.tp_rank] + kTpEpochOff)) *
+                        (uint32_t)kTpRedSlots + (uint32_t)p.tp_slot + 1u;
     if (p.tp_wait >= 0) {  // gathered activations: every rank's producer has signalled this step
         if (threadIdx.x == 0) {
             const uint8_t *lb = p.tp_bases[p.tp_rank];
@@ -1022,51 +1041,38 @@ __global__ void __launch_bounds__(kThreads, (MT <= 8) ? 2 : 1) q4_gemv_q8_kernel
         }
     }
     if (p.tp_slot >= 0 && p.tp_reduce) {
-        // Row-parallel all-reduce, CTA by CTA: this CTA's partials are in
-        // every rank's region; signal the same CTA of every rank, wait for
-        // theirs, then sum rank 0's partial + rank 1's + ... for this CTA's
-        // columns. Every rank adds the same values in the same order, so y
-        // has the same bits everywhere. After a failed wait y is not written
-        // (the error word says why).
-        __shared__ int red_ok;
+        // Row-parallel all-reduce of this CTA's columns: poll every rank's
+        // tagged partial word of each (row, column) until it carries this
+        // launch's tag (bounded), and sum rank 0's + rank 1's + ... in that
+        // order -- the same bits on every rank. A wait that gives up records
+        // the error; the others then stop at once and y is left unwritten.
         const int nthr = kConsumerWarps * 32;
-        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-        if (threadIdx.x == 0) {
-            __threadfence_system();
-            const int64_t cidx = ((int64_t)p.tp_slot * kTpRedCtas + blockIdx.x) * kTpMaxRanks;
-            for (int g = 0; g < p.tp_world; ++g)
-                atomicAdd_system(reinterpret_cast<int *>(p.tp_bases[g] + kTpRedCountOff) + cidx + p.tp_rank, 1);
-            const uint8_t *lb = p.tp_bases[p.tp_rank];
-            const int target = ld_acquire_sys(reinterpret_cast<const int *>(lb + kTpEpochOff)) + 1;
-            const int *cnt = reinterpret_cast<const int *>(lb + kTpRedCountOff) + cidx;
-            bool ok = true;
-            for (int g = 0; g < p.tp_world && ok; ++g) {
-                if (ld_acquire_sys(cnt + g) >= target) continue;
-                if (p.err && *reinterpret_cast<volatile int *>(p.err) != 0) {
-                    ok = false;
-                    break;
-                }
-                const long long start = clock64(), budget = wait_budget(p.err);
-                while (ld_acquire_sys(cnt + g) < target) {
-                    if (clock64() - start > budget) {
-                        record_device_error(p.err, DEV_ERR_WAIT_FULL);
-                        ok = false;
-                        break;
+        const uint32_t tag = g_red_tag;
+        const uint8_t *part = p.tp_bases[p.tp_rank] + kTpDataOff + p.tp_dst_off;
+        const long long budget = wait_budget(p.err);
+        bool ok = true;
+        for (int t = threadIdx.x; t < p.M * nrows && ok; t += nthr) {
+            const int m = t / nrows;
+            const int64_t n = r0 + t % nrows;
+            float acc = 0.0f;
+            for (int g = 0; g < p.tp_world; ++g) {
+                const uint8_t *w = part + (m * p.tp_dst_row + (int64_t)g * p.tp_cols + n) * 8;
+                uint64_t x = ld_relaxed_sys_u64(w);
+                if ((uint32_t)(x >> 32) != tag) {
+                    const long long start = clock64();
+                    while ((uint32_t)(x >> 32) != tag) {
+                        if ((p.err && *reinterpret_cast<volatile int *>(p.err) != 0) || clock64() - start > budget) {
+                            record_device_error(p.err, DEV_ERR_WAIT_FULL);
+                            ok = false;
+                            break;
+                        }
+                        x = ld_relaxed_sys_u64(w);
                     }
+                    if (!ok) break;
                 }
+                acc += __uint_as_float((uint32_t)x);
             }
-            red_ok = ok;
-        }
-        asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-        if (red_ok) {
-            const float *part = reinterpret_cast<const float *>(p.tp_bases[p.tp_rank] + kTpDataOff + p.tp_dst_off);
-            for (int t = threadIdx.x; t < p.M * nrows; t += nthr) {
-                const int m = t / nrows;
-                const int64_t n = r0 + t % nrows;
-                float acc = 0.0f;
-                for (int g = 0; g < p.tp_world; ++g) acc += __ldcg(part + m * p.tp_dst_row + (int64_t)g * p.tp_cols + n);
-                store_out(p.y, p.y_dtype, m * p.y_row_stride + n, acc);
-            }
+            if (ok) store_out(p.y, p.y_dtype, m * p.y_row_stride + n, acc);
         }
     } else if (p.tp_slot >= 0) {
         // Every consumer's rows are stored in this rank's region. The launch's
@@ -1258,9 +1264,6 @@ int launch_gemv(GemvParams p, int M, int64_t N, int64_t K, int flags, cudaStream
     int64_t grid = (int64_t)f.sm_count * ctas_per_sm;
     const int64_t by_rows = (N + plan.rpw * plan.wpc - 1) / (plan.rpw * plan.wpc);
     if (by_rows < grid) grid = by_rows > 0 ? by_rows : 1;
-    if (p.tp_reduce && grid > kTpRedCtas)
-        return set_error(TN_ERR_NOT_IMPLEMENTED, std::string(op) + ": internal: more CTAs than the tensor-parallel "
-                                                                   "reduce counters cover");
     if (p.oq) {
         // whole blocks per CTA, at most kYCap columns of them
         const int64_t blocks = ((flags & TN_EPILOGUE_SILU_MUL_PAIRS) ? N / 2 : N) / 32;

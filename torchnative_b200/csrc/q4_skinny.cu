@@ -67,6 +67,7 @@ struct Layout {
     static constexpr int TMEM_COLS = NS * NP;
     static_assert(ASLOT % 1024 == 0 && OFF_R % 128 == 0, "TMA destinations");
     static_assert(TMEM_COLS == 256, "two CTAs per SM share the 512 TMEM columns");
+    static_assert(NS % EB == 0 && 4 % EB == 0, "epilogue groups of EB blocks in consecutive accumulators");
 };
 
 struct SkinnyArgs {
@@ -250,14 +251,21 @@ __global__ void __launch_bounds__(SK_THREADS, 2) q4_skinny_kernel(const __grid_c
                     const uint32_t ab = sb + L::OFF_A + (c % NA) * L::ASLOT + q * L::APANEL;
                     for (int h = 0; h < 4; ++h) {
                         const int i = 4 * p + h, s = i % NS;
-                        if (i >= NS && !wait_or_abort(&s_empty[s], ((i / NS) - 1) & 1, abort, g.err)) {
+                        // EB consecutive blocks form one epilogue group in EB
+                        // consecutive accumulators: the group's slots are free
+                        // once its last one is released, and its MMAs are done
+                        // once the last one's commit lands (one issuing thread:
+                        // a commit tracks every earlier MMA of it)
+                        const int il = i + EB - 1;
+                        if (i % EB == 0 && i >= NS &&
+                            !wait_or_abort(&s_empty[il % NS], ((il / NS) - 1) & 1, abort, g.err)) {
                             ok = false;
                             break;
                         }
                         tc05::fence_after();
                         mma_i8(tmem + s * NP, tc05::desc_sw128(wb + 32 * h, 16, 1024),
                                tc05::desc_sw128(ab + 32 * h, 16, 1024), idesc);
-                        tc05::commit(&s_full[s]);
+                        if (i % EB == EB - 1) tc05::commit(&s_full[s]);
                     }
                     if (!ok) break;
                     tc05::commit(&b_empty[p % NB]);
@@ -342,13 +350,11 @@ __global__ void __launch_bounds__(SK_THREADS, 2) q4_skinny_kernel(const __grid_c
                 ok = __all_sync(0xffffffffu, wait_or_abort(&d_full[p % ND], (p / ND) & 1, abort, g.err));
                 if (!ok) break;
                 for (int hb = 0; hb < 4; hb += EB) {
-                    bool got = true;
-#pragma unroll
-                    for (int e = 0; e < EB; ++e) {
-                        const int i = 4 * p + hb + e;
-                        got = got && wait_or_abort(&s_full[i % NS], (i / NS) & 1, abort, g.err);
-                    }
-                    ok = __all_sync(0xffffffffu, got);
+                    // one wait for the group (its last block's commit covers the
+                    // group's earlier MMAs) and one release (the issuer waits on
+                    // the group's last slot before reusing any of its slots)
+                    const int il = 4 * p + hb + EB - 1;
+                    ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[il % NS], (il / NS) & 1, abort, g.err));
                     if (!ok) break;
                     tc05::fence_after();
                     uint32_t dv[EB][EW];
@@ -357,10 +363,7 @@ __global__ void __launch_bounds__(SK_THREADS, 2) q4_skinny_kernel(const __grid_c
                     tc05::wait_ld();
                     tc05::fence_before();
                     __syncwarp();
-                    if (lane == 0) {
-#pragma unroll
-                        for (int e = 0; e < EB; ++e) mbar_arrive(&s_empty[(4 * p + hb + e) % NS]);
-                    }
+                    if (lane == 0) mbar_arrive(&s_empty[il % NS]);
                     float dw[EB];
 #pragma unroll
                     for (int e = 0; e < EB; ++e) dw[e] = dws[((p % ND) * 4 + hb + e) * SN + r];

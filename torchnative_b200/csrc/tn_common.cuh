@@ -152,15 +152,11 @@ __device__ __forceinline__ void record_device_error(int *word, int code) {
 //   [0, 4)                  epoch: steps this rank has completed
 //   [64, 32768)             counters[slot][src]
 //   [32768, 65536)          tickets[slot]: CTAs of this rank's producer kernel done
-//   [65536, +2.5 MB)        reduce counters[slot][cta][src]: CTA cta of rank src
-//                           stored its partials of reduction `slot` here
-//   [3 MB, ...)             gathered activation rows, reduction partials
+//   [65536, ...)            gathered activation rows; row-parallel partials as
+//                           8-byte words {f32 value, tag = epoch * 256 + slot + 1}
 constexpr int kTpMaxRanks = 8;
-constexpr int kTpRedSlots = 256, kTpRedCtas = 320;
-constexpr int64_t kTpEpochOff = 0, kTpCountOff = 64, kTpTicketOff = 32768, kTpRedCountOff = 65536;
-constexpr int64_t kTpDataOff = 3 << 20;
-static_assert(kTpRedCountOff + (int64_t)kTpRedSlots * kTpRedCtas * kTpMaxRanks * 4 <= kTpDataOff,
-              "reduce counters overlap the data area");
+constexpr int kTpRedSlots = 256;  // reductions per step (the tag's slot field)
+constexpr int64_t kTpEpochOff = 0, kTpCountOff = 64, kTpTicketOff = 32768, kTpDataOff = 65536;
 
 __device__ __forceinline__ int ld_acquire_sys(const int *p) {
     int v;

@@ -10,8 +10,9 @@
 //                      gather `slot`; for gathers fused into a GEMV's epilogue
 //                      (q4_gemv.cu), launches of rank src that finished
 //   [32768, 65536)     tickets[slot]: the fused producer's finished CTAs
-//   [65536, 3 MB)      reduce counters of the row-parallel GEMV (q4_gemv.cu)
-//   [3 MB, ...)        the gathered activation rows, at caller-chosen offsets
+//   [65536, ...)       the gathered activation rows and the row-parallel
+//                      GEMV's tagged partials (q4_gemv.cu), at caller-chosen
+//                      offsets
 // One gather: every rank stores its [rows][cols] slice straight into every
 // rank's region (row r, columns [rank * cols, (rank + 1) * cols) of a
 // [rows][dst_row_stride] buffer), fences system-wide and adds 1 to its counter

@@ -159,8 +159,8 @@ class Q4LlamaDecoder:
         self.xchg = None
         if self.tp is not None and exchange == "p2p":
             nbytes = 2 * B * (s.heads * s.head_dim + H + I + s.vocab) + 4 * 256
-            if self.rowwise:  # two f32 partial buffers [B][G * H], alternating between reductions
-                nbytes += 2 * (B * G * H * 4 + 256)
+            if self.rowwise:  # two partial buffers [B][G * H] of tagged 8-byte words, alternating
+                nbytes += 2 * (B * G * H * 8 + 256)
             self.xchg = tpm.PeerExchange(self.tp, nbytes, dev)
             attn2d, self._off_attn = self.xchg.buffer(B, s.heads * s.head_dim)
             self.attn = attn2d.view(B, s.heads, 1, s.head_dim)
@@ -170,7 +170,7 @@ class Q4LlamaDecoder:
             for t in (self.attn, self.delta, self.act, self.logits):
                 t.zero_()
             if self.rowwise:
-                self._off_part = [self.xchg.reserve(B * G * H * 4) for _ in range(2)]
+                self._off_part = [self.xchg.reserve(B * G * H * 8) for _ in range(2)]
         elif self.tp is not None and exchange != "nccl":
             raise ValueError(f"unknown exchange {exchange!r} (p2p or nccl)")
         else:

@@ -218,8 +218,8 @@ class PeerExchange:
 
     def reduce_link(self, slot: int, partial_off: int, cols: int) -> "N.TpLink":
         """A tn_tp_link for a row-parallel GEMV with its all-reduce fused in:
-        reduction `slot` of the step, f32 partials at partial_off laid out
-        [rows][world * cols]."""
+        reduction `slot` of the step, its tagged f32 partials (8-byte words)
+        at partial_off laid out [rows][world * cols]."""
         ln = N.TpLink()
         ln.world, ln.rank = self.tp.world, self.tp.rank
         for g in range(self.tp.world):
