@@ -315,21 +315,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) q4_gemm_kernel(const __grid_c
                 }
                 tc05::fence_after();
                 const float *dw = dwt + ((p % NB) * 2 + h) * GN + cg * EPI_COLS;
-                // the block's 64 columns in two TMEM round trips of 32 (both
-                // loads of a pair issued before its wait)
 #pragma unroll
-                for (int k = 0; k < EPI_COLS / 16; k += 2) {
-                    float v0[16], v1[16];
-                    tc05::ld16(taddr + s * GN + 16 * k, v0);
-                    tc05::ld16(taddr + s * GN + 16 * (k + 1), v1);
+                for (int k = 0; k < EPI_COLS / 16; ++k) {
+                    float v[16];
+                    tc05::ld16(taddr + s * GN + 16 * k, v);
                     tc05::wait_ld();
-                    if (k + 2 == EPI_COLS / 16) {
+                    if (k == EPI_COLS / 16 - 1) {
                         tc05::fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&s_empty[s]);
                     }
-                    scale_add(v0, dw, 16 * k, dx8[bi]);
-                    scale_add(v1, dw, 16 * (k + 1), dx8[bi]);
+                    scale_add(v, dw, 16 * k, dx8[bi]);
                 }
                 if (h == 1) {
                     __syncwarp();

@@ -70,12 +70,13 @@ extern "C" int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, 
     const int64_t nb = K / 32;
     void *ws = nullptr;
     int st;
-    if (x_dtype == TN_BF16 && M <= 4 && K <= 4096 && K % 256 == 0 &&
+    if (x_dtype == TN_BF16 && M == 1 && K <= 4096 && K % 256 == 0 &&
         ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_blob) | (uintptr_t)(x_row_stride * 2)) &
          15) == 0)
-        // A few bf16 rows of a short K: every CTA quantises the rows to Q8_0 in
-        // its own prologue (the same codes tn_q8_0_quantize_planar writes, 128
-        // blocks per CTA), one launch instead of quantiser + GEMV
+        // One bf16 row of a short K: every CTA quantises it to Q8_0 in its own
+        // prologue (the same codes tn_q8_0_quantize_planar writes, 128 blocks
+        // per CTA), one launch instead of quantiser + GEMV. (At 4 rows the
+        // repeated prologue costs more than the launch it saves.)
         return tn::launch_q4_gemv_fused(TN_X_BF16, x, x_row_stride, nullptr, nullptr, nullptr, 0.0f,
                                         static_cast<const uint8_t *>(w_blob), bias, y, y_dtype, N, (int)M, N, K, 0,
                                         stream, nullptr, nullptr);

@@ -103,9 +103,11 @@ extern "C" int tn_sdpa_flash_attention(const void *q, const void *k, const void 
     const int64_t rows = (int64_t)p.B * p.Hq * p.L;
     p.part_o = static_cast<float *>(ws);
     p.part_ml = p.part_o + rows * p.splits * p.D;
-    if (p.L == 1 && p.row_groups == 1) {
-        // one query row per head: the last CTA of each KV head merges the
-        // splits (a zeroed ticket per head, reset by that CTA), no combine launch
+    if (p.L == 1 && p.row_groups == 1 && (int64_t)p.B * p.Hkv <= 32) {
+        // one query row per head and few heads: the last CTA of each KV head
+        // merges the splits (a zeroed ticket per head, reset by that CTA), no
+        // combine launch. (With many (batch, head) pairs the separate combine
+        // kernel spreads the merges wider and measures faster.)
         void *cnt = nullptr;
         st = tn::workspace_zeroed(&cnt, (size_t)p.B * p.Hkv * sizeof(int) + 256, stream, /*slot=*/3);
         if (st) return st;
@@ -162,7 +164,7 @@ extern "C" int tn_sdpa_decode_cache(const void *q, const void *k_cache, const vo
     if (st) return st;
     p.part_o = static_cast<float *>(ws);
     p.part_ml = p.part_o + (int64_t)p.B * p.Hq * p.splits * p.D;
-    if (p.row_groups == 1) {  // the last CTA of each KV head merges the splits (no combine launch)
+    if (p.row_groups == 1 && (int64_t)p.B * p.Hkv <= 32) {  // in-kernel merge, as the flash op does
         void *cnt = nullptr;
         st = tn::workspace_zeroed(&cnt, (size_t)p.B * p.Hkv * sizeof(int) + 256, stream, /*slot=*/3);
         if (st) return st;
