@@ -242,9 +242,12 @@ def _bf16_ulps(x: torch.Tensor) -> torch.Tensor:
     return torch.exp2(torch.floor(torch.log2(x.abs().clamp_min(1e-30))) - 7)
 
 
-@pytest.mark.parametrize("batch", [1, 2])
+@pytest.mark.parametrize("batch", [1, 2, 8])
 @pytest.mark.parametrize("world", WORLDS)
 def test_tp_rowwise_decode_matches_one_gpu_within_the_reduction_order(cuda_device, world, batch):
+    """Batch 1 and 2: the fused five-launch step (act's Q8_0 from gate/up's
+    epilogue at batch 1, in down_proj's prologue at batch 2); batch 8: the
+    separate-kernel step with the tensor-core q/k/v and gate/up."""
     _need(world)
     steps = 6
     first, want, want_logits = _one_gpu(cuda_device, world, batch, steps)

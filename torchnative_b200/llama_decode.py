@@ -99,7 +99,13 @@ class Q4LlamaDecoder:
         self.G = G
         if tp_plan not in ("rowwise", "colwise"):
             raise ValueError(f"unknown tp_plan {tp_plan!r} (rowwise or colwise)")
-        self.rowwise = self.tp is not None and tp_plan == "rowwise" and batch <= 4 and exchange == "p2p"
+        # rowwise at batch <= 4 (the fused five-launch step), and up to 16 rows
+        # while the row-parallel K-slices still fit the GEMV's one-launch tile
+        # (o_proj and down_proj carry the fused reduction; 16 rows of at most
+        # 7168 columns)
+        self.rowwise = (self.tp is not None and tp_plan == "rowwise" and exchange == "p2p" and
+                        (batch <= 4 or (batch <= 16 and shape.inter // G <= 7168 and
+                                        shape.heads // G * shape.head_dim <= 7168)))
         s, dev = shape, self.dev
         for n, what in ((s.heads, "query heads"), (s.kv_heads, "key/value heads"), (s.hidden, "hidden size"),
                         (s.inter, "intermediate size"), (s.vocab, "vocabulary")):
@@ -109,10 +115,11 @@ class Q4LlamaDecoder:
         self.h_l, self.i_l, self.v_l = s.hidden // G, s.inter // G, s.vocab // G
         self.qkv_l = (self.hq + 2 * self.hkv) * s.head_dim
         # rowwise: SiLU*up's planar Q8_0 from gate/up's own epilogue needs whole
-        # 32-column blocks per CTA; when this rank's columns make too few blocks
-        # to keep the SMs streaming (Llama-3-8B on 8 ranks: 56), down_proj
-        # quantises act in its prologue instead (56 blocks per CTA)
-        self.rowwise_q8out = self.i_l // 32 >= 74
+        # 32-column blocks per CTA, so gate/up runs on at most i_l / 32 CTAs;
+        # below ~200 blocks (Llama-3-8B on 4 ranks: 112 CTAs, 10.1 us for 16.5
+        # MB) down_proj quantises act in its own prologue instead and gate/up
+        # keeps the full grid
+        self.rowwise_q8out = self.i_l // 32 >= 200
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
         bf = torch.bfloat16
@@ -348,8 +355,8 @@ class Q4LlamaDecoder:
             extra = 4 if (self.tp is not None and self.B > 1) else 0
         if self._mega is not None:
             return 0  # the whole token is one launch (kernels_per_step)
-        if self.rowwise:
-            return 5  # the one-GPU fused layer; both reductions inside the GEMVs
+        if self.rowwise:  # both reductions inside the GEMVs
+            return 5 if self.fused else 10
         if self.fused:
             # one GPU: gate/up also writes the planar Q8_0 of act (no quantiser launch)
             return (5 if self.tp is None else 6) + extra
@@ -478,6 +485,8 @@ class Q4LlamaDecoder:
             return self._step_mega(stream or self._stream())
         if self.fused:
             return self._step_fused(stream or self._stream())
+        if self.rowwise:
+            return self._step_rowwise_rows(stream or self._stream())
         L, s, B = N.lib(), self.s, self.B
         stream = stream or self._stream()
         D, Hq, Hkv = s.head_dim, self.hq, self.hkv  # local heads
@@ -573,6 +582,46 @@ class Q4LlamaDecoder:
                                         P(self.pos.data_ptr()), stream))
         self._step_end(stream)
 
+    def _step_rowwise_rows(self, stream) -> None:
+        """The rowwise plan for 5 to 16 rows: the separate-kernel step (RMSNorm
+        + Q8_0 launches, the tensor-core skinny kernel for q/k/v and gate/up on
+        this rank's columns, RoPE + append, split-KV attention on the local
+        heads), with o_proj and down_proj row-parallel GEMVs whose reduction
+        is fused in (their K-slices are the local heads' attention output and
+        the local SiLU*up columns, each quantised once). 10 launches a layer,
+        2 exchanges, where the colwise step has 15 launches and 4 gathers."""
+        L, s, B = N.lib(), self.s, self.B
+        D, Hq, Hkv, H = s.head_dim, self.hq, self.hkv, s.hidden
+        HD = Hq * D
+        links = self._links
+        for li, lw in enumerate(self.layers):
+            self._norm(None if li == 0 else self.delta, lw["attn_norm"], stream)
+            self._linear(lw["qkv"], self.qkv_out, self.qkv_l, H, stream)
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            N.check(L.tn_llama_rope_append(P(self.qkv_out.data_ptr()), P(self.inv_freq.data_ptr()),
+                                           P(self.pos.data_ptr()), 0, B, Hq, Hkv, D, P(self.q_rot.data_ptr()),
+                                           P(kc.data_ptr()), P(vc.data_ptr()), kc.stride(0), kc.stride(1), stream))
+            N.check(L.tn_sdpa_decode_cache(P(self.q_rot.data_ptr()), P(kc.data_ptr()), P(vc.data_ptr()),
+                                           P(self.attn_l.data_ptr()), None, N.TN_BF16, B, Hq, Hkv, D, self.cap,
+                                           self._qstr, self._kstr, self._kstr, P(self.pos.data_ptr()), 1,
+                                           1.0 / math.sqrt(D), stream))
+            N.check(L.tn_q8_0_quantize_planar(P(self.attn_l.data_ptr()), N.TN_BF16, HD, P(self.codes.data_ptr()), HD,
+                                              P(self.scales.data_ptr()), P(self.offsets.data_ptr()), B, HD, stream))
+            self._linear(lw["o"], self.delta, H, HD, stream, link=links[("o", li)])
+            self._norm(self.delta, lw["mlp_norm"], stream)
+            self._linear(lw["gate_up"], self.act_l, 2 * self.i_l, H, stream, N.TN_EPILOGUE_SILU_MUL_PAIRS)
+            N.check(L.tn_q8_0_quantize_planar(P(self.act_l.data_ptr()), N.TN_BF16, self.i_l,
+                                              P(self.codes.data_ptr()), self.i_l, P(self.scales.data_ptr()),
+                                              P(self.offsets.data_ptr()), B, self.i_l, stream))
+            self._linear(lw["down"], self.delta, H, self.i_l, stream, link=links[("down", li)])
+        self._norm(self.delta, self.final_norm, stream)
+        self._linear(self.lm_head, self.logits_l, self.v_l, H, stream)
+        self._gather(self.logits_l, self.logits, 0, stream)
+        N.check(L.tn_llama_argmax_embed(P(self.logits.data_ptr()), B, s.vocab, P(self.tokens.data_ptr()),
+                                        P(self.embed.data_ptr()), s.hidden, P(self.h.data_ptr()),
+                                        P(self.pos.data_ptr()), stream))
+        self._step_end(stream)
+
     def _step_fused(self, stream) -> None:
         if self.rowwise:
             return self._step_rowwise(stream)
@@ -635,17 +684,19 @@ class Q4LlamaDecoder:
         self._step_end(stream)
 
     def _build_links(self) -> dict:
-        """The fused gathers' links: o_proj and down_proj scatter their rows
-        into every rank's `delta` (slots 4l + 1, 4l + 3); the next RMSNorm GEMV
-        (gate/up, the next layer's q/k/v, lm_head) waits for them."""
-        if self.xchg is None or not self.fused_gather:
-            return {}
-        links = {}
+        """Under the rowwise plan, the reduce links of o_proj and down_proj.
+        Otherwise the fused gathers' links: o_proj and down_proj scatter their
+        rows into every rank's `delta` (slots 4l + 1, 4l + 3); the next RMSNorm
+        GEMV (gate/up, the next layer's q/k/v, lm_head) waits for them."""
         if self.rowwise:  # reductions 2l (o_proj) and 2l + 1 (down_proj), alternating partial buffers
+            links = {}
             for li in range(self.n_layers):
                 links[("o", li)] = self.xchg.reduce_link(2 * li, self._off_part[0], self.s.hidden)
                 links[("down", li)] = self.xchg.reduce_link(2 * li + 1, self._off_part[1], self.s.hidden)
             return links
+        if self.xchg is None or not self.fused_gather:
+            return {}
+        links = {}
         for li in range(self.n_layers):
             links[("o", li)] = self._link(slot=4 * li + 1, full=self.delta)
             links[("gate_up", li)] = self._link(wait_slot=4 * li + 1)
