@@ -115,11 +115,12 @@ class Q4LlamaDecoder:
         self.h_l, self.i_l, self.v_l = s.hidden // G, s.inter // G, s.vocab // G
         self.qkv_l = (self.hq + 2 * self.hkv) * s.head_dim
         # rowwise: SiLU*up's planar Q8_0 from gate/up's own epilogue needs whole
-        # 32-column blocks per CTA, so gate/up runs on at most i_l / 32 CTAs;
-        # below ~200 blocks (Llama-3-8B on 4 ranks: 112 CTAs, 10.1 us for 16.5
-        # MB) down_proj quantises act in its own prologue instead and gate/up
-        # keeps the full grid
-        self.rowwise_q8out = self.i_l // 32 >= 200
+        # 32-column blocks per CTA, so gate/up runs on at most i_l / 32 CTAs.
+        # Below half an SM's worth of blocks (Llama-3-8B on 8 ranks: 56)
+        # down_proj quantises act in its own prologue instead. On 4 ranks (112
+        # blocks) both ways measured alike: gate/up 10.1 -> 8.0 us, down 4.2 ->
+        # 7.6 us, 679 -> 672 tok/s, so the epilogue keeps it there.
+        self.rowwise_q8out = self.i_l // 32 >= 74
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
         bf = torch.bfloat16
