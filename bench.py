@@ -80,9 +80,9 @@ def parse():
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="tensor-parallel all-gather: peer-memory kernel or NCCL")
     ap.add_argument("--tp-plan", default="rowwise", choices=["rowwise", "colwise"],
-                    help="tensor-parallel plan at batch <= 4 with the peer-memory exchange: o_proj/down_proj "
+                    help="tensor-parallel plan with the peer-memory exchange up to 16 rows: o_proj/down_proj "
                          "row-parallel with the all-reduce fused into the GEMV (rowwise), or every linear "
-                         "column-sharded with an all-gather after each (colwise)")
+                         "column-sharded with an all-gather after each (colwise; always beyond 16 rows)")
     return ap.parse_args()
 
 
@@ -295,7 +295,7 @@ def run_ours(args, rank, world, local):
     B = args.batch
     cap = PROMPT + args.warmup + args.steps + 8
     tp = None
-    if world > 1:  # column-sharded tensor parallelism, one all-gather after each sharded output
+    if world > 1:  # tensor parallelism over the group (--tp-plan: rowwise by default)
         import torch.distributed as dist
 
         from torchnative_b200.tp import TPGroup

@@ -69,10 +69,12 @@ def rope_inv_freq(head_dim: int, theta: float) -> torch.Tensor:
 
 class Q4LlamaDecoder:
     """The decode step on one GPU, or on rank `tp.rank` of a tensor-parallel
-    group (`tp` a torchnative_b200.tp.TPGroup): then every Q4_0 linear holds
-    its column shard, attention its KV-head group, and one all-gather after
-    each sharded output rebuilds the full row (the weights are generated in
-    full from the seed and sliced, so every group size runs the same model)."""
+    group (`tp` a torchnative_b200.tp.TPGroup): then q/k/v, gate/up and
+    lm_head hold their column shards, attention its KV-head group, and o_proj
+    and down_proj either their K-slices with the all-reduce fused into the
+    GEMV (tp_plan "rowwise") or their column shards with an all-gather after
+    each sharded output ("colwise"). The weights are generated in full from
+    the seed and sliced, so every group size runs the same model."""
 
     def __init__(self, shape: LlamaShape, batch: int, capacity: int, device, seed: int = 0,
                  layers: int | None = None, tp=None, exchange: str = "p2p", weights: dict | None = None,
