@@ -207,6 +207,56 @@ def cpu_step_seconds(layer_blobs: dict, lm_head_blob, threads: int, reps: int = 
     return best
 
 
+def upstream_cpu_step_seconds(layer_blobs: dict, lm_head_blob, threads: int, reps: int = 1,
+                              context: int = PROMPT) -> float:
+    """The labelled "upstream CPU" comparator: the same token's two hot
+    operators in upstream torch on the host -- each Q4_0 weight dequantised to
+    f32 once, outside the timing (the dequantised values are exact), then per
+    layer four f32 `x @ W.T` and torch's own CPU scaled_dot_product_attention
+    over a `context`-token f32 cache with GQA, and lm_head. Not the
+    reference's arithmetic (no Q8_0 activations): a yardstick beside it.
+    Seconds per token (min over reps)."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle
+
+    torch.set_num_threads(threads)
+    ws = {name: torch.from_numpy(oracle.q4_0_dequantize(layer_blobs[name], n * k).reshape(n, k))
+          for name, n, k in LAYER_LINEARS}
+    lm = torch.from_numpy(oracle.q4_0_dequantize(lm_head_blob, VOCAB * HIDDEN).reshape(VOCAB, HIDDEN))
+    g = torch.Generator().manual_seed(2)
+    xs = {k: torch.randn((1, k), generator=g) for k in (HIDDEN, INTER)}
+    q = torch.randn((1, HEADS, 1, HEAD_DIM), generator=g)
+    kc = torch.randn((1, KV_HEADS, context, HEAD_DIM), generator=g)
+    vc = torch.randn((1, KV_HEADS, context, HEAD_DIM), generator=g)
+    best = float("inf")
+    with torch.no_grad():
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            for _layer in range(LAYERS):
+                for name, _n, k in LAYER_LINEARS:
+                    xs[k] @ ws[name].T
+                torch.nn.functional.scaled_dot_product_attention(q, kc, vc, enable_gqa=True)
+            xs[HIDDEN] @ lm.T
+            best = min(best, time.perf_counter() - t0)
+    return best
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), for the baseline's label."""
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 def host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -510,9 +560,17 @@ def run_ours(args, rank, world, local):
         th = host_threads()
         sec = cpu_step_seconds(blobs, lm, th, reps=2)
         result["cpu_baseline"] = {"value": 1.0 / sec, "unit": "tok/s", "cores": th, "kind": "port",
+                                  "host": cpu_model(), "nproc": os.cpu_count(),
                                   "sample": f"one token at batch 1: layer 0's four Q4_0 linears and SDPA over a "
                                             f"{PROMPT}-token f32 cache, 32 times, + lm_head; oracle/tn_oracle.c "
                                             "restatement of the reference CPU arithmetic; min of 2"}
+        usec = upstream_cpu_step_seconds(blobs, lm, th, reps=2)
+        result["upstream_cpu"] = {"value": 1.0 / usec, "unit": "tok/s", "cores": th, "host": cpu_model(),
+                                  "sample": "the same token in upstream torch " + __import__("torch").__version__ +
+                                            " on the host: f32 weights dequantised once (untimed), four f32 "
+                                            "x @ W.T and torch's CPU scaled_dot_product_attention (GQA) per layer, "
+                                            "32 times, + lm_head; min of 2. A yardstick, not the reference's "
+                                            "arithmetic"}
     return result
 
 
