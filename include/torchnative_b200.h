@@ -51,7 +51,9 @@ typedef enum { TN_F32 = 0, TN_F16 = 1, TN_BF16 = 2, TN_F64 = 3 } tn_dtype;
  *   to GGML Q8_0 (k_quants.rs:676-706), block dots are exact integers and the
  *   per-block scales are applied in float32 (k_quants.rs:312-330).
  * TN_ACT_FLOAT: no activation quantisation; weights are dequantised exactly
- *   to float32 and multiplied with the float activations (fp32 accumulate). */
+ *   to float32 and multiplied with the float activations (fp32 accumulate).
+ *   tn_q4_0_linear runs it for up to 16 activation rows (refused by name
+ *   above); the Q8_0 and Q4_K linears refuse it. */
 typedef enum { TN_ACT_Q8_0 = 0, TN_ACT_FLOAT = 1 } tn_act_mode;
 
 /* ---------------------------------------------------------------- runtime -- */

@@ -56,6 +56,12 @@ int launch_q4k_gemv(const uint8_t *w, const int8_t *xq, const float *xd, const f
                     const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
                     cudaStream_t stream);
 
+// The float-activation mode (TN_ACT_FLOAT) for M <= 16: weights dequantised
+// exactly to f32, x widened from f32 / bf16 / f16, f32 accumulate (q4_float.cu).
+int launch_q4_float_gemv(const uint8_t *w, const void *x, int x_dtype, int64_t x_row_stride, const float *bias,
+                         void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,
+                         cudaStream_t stream);
+
 // Decode GEMV over planar Q8_0 activations: y[m, n] for m < M (M <= 16).
 int launch_q4_gemv_q8(const uint8_t *w, const int8_t *xq, const float *xd, const float *xc, int64_t xq_row_stride,
                       const float *bias, void *y, int y_dtype, int64_t y_row_stride, int M, int64_t N, int64_t K,

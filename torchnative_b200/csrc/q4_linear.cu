@@ -62,10 +62,16 @@ extern "C" int tn_q4_0_linear(const void *x, int x_dtype, int64_t x_row_stride, 
     if (x_row_stride < K) return tn::set_error(TN_ERR_INVALID, op + ": activation row stride smaller than in_features");
     if ((reinterpret_cast<uintptr_t>(w_blob) & 1) != 0)
         return tn::set_error(TN_ERR_INVALID, op + ": the q4_0 blob must be at least 2-byte aligned");
-    if (act_mode == TN_ACT_FLOAT)
-        return tn::set_error(TN_ERR_NOT_IMPLEMENTED,
-                             op + ": the float-activation mode is not implemented on CUDA yet; use the Q8_0 mode "
-                                  "(the reference's arithmetic)");
+    if (act_mode == TN_ACT_FLOAT) {
+        // no activation quantisation: exact f32 weights times the widened
+        // activations, f32 accumulate (decode-sized inputs)
+        if (M > 16)
+            return tn::set_error(TN_ERR_NOT_IMPLEMENTED,
+                                 op + ": the float-activation mode runs at most 16 activation rows on CUDA; use the "
+                                      "Q8_0 mode (the reference's arithmetic) for more");
+        return tn::launch_q4_float_gemv(static_cast<const uint8_t *>(w_blob), x, x_dtype, x_row_stride, bias, y,
+                                        y_dtype, N, (int)M, N, K, stream);
+    }
 
     const int64_t nb = K / 32;
     void *ws = nullptr;
