@@ -5,7 +5,7 @@ their dtype, f32 accumulate, f32 bias. Checked against the exact value in
 float64 of the same dequantised weights and widened activations, within the
 kernel's counted f32 bound: every term passes through at most 32 (a block's
 sum) + ceil(K / 1024) (a lane's blocks) + 5 (the warp's butterfly) + 1 (the
-bias) roundings, plus half an ulp of the output dtype."""
+bias) roundings, plus the rounding to the output dtype."""
 
 import ctypes
 
@@ -57,8 +57,10 @@ def test_float_mode_within_its_f32_bound(N, cuda_device, x_dtype, M, Nout, K):
         exact = xs @ w.T + bias.cpu().numpy().astype(np.float64)
         absum = np.abs(xs) @ np.abs(w).T + np.abs(bias.cpu().numpy().astype(np.float64))
         depth = 32 + -(-K // 1024) + 6
-        out_ulp = 2.0 ** -24 if y_dtype == "float32" else 2.0 ** -9
-        bound = _gamma(depth) * absum + np.abs(exact) * out_ulp * 1.01 + 1e-30
+        # the output's rounding: unit roundoff 2^-24 (f32) or 2^-8 (bf16, 8
+        # significant bits) of the value
+        out_u = 2.0 ** -24 if y_dtype == "float32" else 2.0 ** -8
+        bound = _gamma(depth) * absum + np.abs(exact) * out_u * (1 + _gamma(depth)) + 1e-30
         got = y.float().cpu().numpy().astype(np.float64)
         worst = float(np.max(np.abs(got - exact) / bound))
         assert worst <= 1.0, f"{x_dtype} -> {y_dtype}: {worst:.3g}x the bound"
