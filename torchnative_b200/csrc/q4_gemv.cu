@@ -1054,29 +1054,23 @@ __global__ void __launch_bounds__(kThreads, (MT <= 8) ? 2 : 1) q4_gemv_q8_kernel
         for (int t = threadIdx.x; t < p.M * nrows && ok; t += nthr) {
             const int m = t / nrows;
             const int64_t n = r0 + t % nrows;
-            const uint8_t *w0 = part + (m * p.tp_dst_row + n) * 8;
-            const int64_t gstep = p.tp_cols * 8;
-            // every rank's word requested at once (one round trip, not world)
-            uint64_t x[kTpMaxRanks];
-#pragma unroll
-            for (int g = 0; g < kTpMaxRanks; ++g)
-                if (g < p.tp_world) x[g] = ld_relaxed_sys_u64(w0 + g * gstep);
             float acc = 0.0f;
-#pragma unroll
-            for (int g = 0; g < kTpMaxRanks; ++g) {
-                if (g >= p.tp_world || !ok) break;
-                if ((uint32_t)(x[g] >> 32) != tag) {
+            for (int g = 0; g < p.tp_world; ++g) {
+                const uint8_t *w = part + (m * p.tp_dst_row + (int64_t)g * p.tp_cols + n) * 8;
+                uint64_t x = ld_relaxed_sys_u64(w);
+                if ((uint32_t)(x >> 32) != tag) {
                     const long long start = clock64();
-                    while ((uint32_t)(x[g] >> 32) != tag) {
+                    while ((uint32_t)(x >> 32) != tag) {
                         if ((p.err && *reinterpret_cast<volatile int *>(p.err) != 0) || clock64() - start > budget) {
                             record_device_error(p.err, DEV_ERR_WAIT_FULL);
                             ok = false;
                             break;
                         }
-                        x[g] = ld_relaxed_sys_u64(w0 + g * gstep);
+                        x = ld_relaxed_sys_u64(w);
                     }
+                    if (!ok) break;
                 }
-                acc += __uint_as_float((uint32_t)x[g]);
+                acc += __uint_as_float((uint32_t)x);
             }
             if (ok) store_out(p.y, p.y_dtype, m * p.y_row_stride + n, acc);
         }
